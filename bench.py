@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Benchmark: stream-steps/s of the cache-aware streaming 24-layer FastConformer encoder step on B200.
+
+Workload ("C3"): per GPU, 256 synchronous streams at attention context [70,13]
+(T = 14 encoder frames per step from 121-row mel chunks, 105 rows for a stream's first chunk), bf16, the full
+step of the reference's NemotronStreamer.step: subsampling, 24 conformer layers over the paged K/V / conv caches,
+the joint encoder projection, and greedy RNN-T decoding of the kept frames with carried decoder state.
+Synthetic data: each stream's 30 s of N(0,1) 128-bin mel (seed = stream id); weights N(0, 0.02), seed 0.
+One bench "step" = one batched step of all streams on a GPU; `value` = streams x steps x GPUs / max-over-ranks
+device time. Scaling is weak (256 streams per GPU); GPUs share nothing (no collectives on the data path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--streams S] [--lookahead R]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Rank 0 prints one JSON line. `--impl reference` times the CPU restatement of the reference's own step
+(oracle/, the reference being Swift/Metal plus a torch CPU restatement that cannot run on the GPU host) on
+all host cores, one stream-step per bench step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "universal-dictator_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "stream-steps/s (24-layer enc step)"
+UNIT = "stream-steps/s"
+L_CTX, MEL, TOTAL_ROWS = 70, 128, 3000          # 30 s of mel at 100 fps
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def chunk_schedule(R: int, total_rows: int):
+    """The live chunk walk (NemotronStreamer.swift:109-154) over a whole utterance: (start, rows) per step,
+    first chunk 1+8R rows, then 9 pre-encode rows + 8+8R new rows; only full chunks."""
+    first, chunk = 1 + 8 * R, 8 + 8 * R
+    out = [(0, first)]
+    idx = first
+    while idx + chunk <= total_rows:
+        out.append((idx - 9, 9 + chunk))
+        idx += chunk
+    return out
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons with NVML every 10 ms during the timed region."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz, self.ok = [], set(), None, False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            pass
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def gemm_flops_per_step(n: int, T: int, R: int, cfg) -> float:
+    """Algorithmic FLOPs of the step's tensor-core GEMMs: per layer the FF (2 x 2 x 4096 x 1024), QKV (3 x 1024^2),
+    output (1024^2), pointwise conv (2048 x 1024 + 1024^2) projections over M = n*T rows, the subsampling
+    pointwise and output GEMMs over their rows, and the joint encoder projection."""
+    D, F, C, J, NL = cfg.d_model, cfg.ff_dim, cfg.sub_channels, cfg.joint_dim, cfg.n_layers
+    M = n * T
+    layers = NL * M * 2 * (2 * F * D + 3 * D * D + D * D + 2 * D * D + D * D + 2 * F * D)
+    nxt = lambda t: t // 2 + 1  # noqa: E731
+    rows = 9 + 8 + 8 * R
+    T1, T2, T3 = nxt(rows), nxt(nxt(rows)), nxt(nxt(nxt(rows)))
+    F1, F2, F3 = nxt(MEL), nxt(nxt(MEL)), nxt(nxt(nxt(MEL)))
+    sub = n * T2 * F2 * 2 * C * C + n * T3 * F3 * 2 * C * C + n * T3 * 2 * (C * F3) * D
+    joint = M * 2 * D * J
+    return float(layers + sub + joint)
+
+
+def cpu_baseline(sd, R: int, budget_s: float = 12.0, max_steps: int = 40):
+    """The CPU restatement of the reference's step (fp32, batch 1, all host threads) on a bounded sample of
+    the same workload: one stream's consecutive chunks. Returns (stream-steps/s, threads, sample text)."""
+    from oracle.rnnt import RNNT, DecoderState
+    from oracle.stream_step import Encoder, StreamState
+    from oracle.weights import NEMOTRON
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    enc = Encoder(sd, NEMOTRON)
+    dec = RNNT(sd, NEMOTRON)
+    st, ds = StreamState(NEMOTRON), DecoderState(NEMOTRON)
+    mel = torch.randn(TOTAL_ROWS, MEL, generator=torch.Generator().manual_seed(0))
+    sched = chunk_schedule(R, TOTAL_ROWS)
+    n = 0
+    with torch.inference_mode():
+        proj, *_ = enc.stream_step(st, mel[0:sched[0][1]], sched[0][1], sched[0][1], False, R)  # warm-up
+        t0 = time.perf_counter()
+        while n < max_steps and (time.perf_counter() - t0) < budget_s:
+            start, rows = sched[1 + n % (len(sched) - 1)]
+            proj, *_ = enc.stream_step(st, mel[start:start + rows], rows, rows, False, R)
+            dec.greedy(proj, ds)
+            n += 1
+        dt = time.perf_counter() - t0
+    return n / dt, torch.get_num_threads(), f"{n} consecutive stream-steps of one stream ({dt:.1f} s), [70,{R}], fp32, 24 layers + joint + greedy"
+
+
+def run_reference(args, world, rank):
+    """Reference arm: rank 0 times the CPU restatement; other ranks exit without work."""
+    if rank != 0:
+        return None
+    from oracle.rnnt import RNNT, DecoderState
+    from oracle.stream_step import Encoder, StreamState
+    from oracle.weights import NEMOTRON, make_weights
+
+    R = args.lookahead
+    sd = make_weights(NEMOTRON, seed=0)
+    torch.set_num_threads(os.cpu_count() or 1)
+    enc, dec = Encoder(sd, NEMOTRON), RNNT(sd, NEMOTRON)
+    st, ds = StreamState(NEMOTRON), DecoderState(NEMOTRON)
+    mel = torch.randn(TOTAL_ROWS, MEL, generator=torch.Generator().manual_seed(0))
+    sched = chunk_schedule(R, TOTAL_ROWS)
+
+    def one(i):
+        start, rows = sched[i % len(sched)]
+        if i % len(sched) == 0:
+            st.__init__(NEMOTRON)
+            ds.__init__(NEMOTRON)
+        proj, *_ = enc.stream_step(st, mel[start:start + rows], rows, rows, False, R)
+        dec.greedy(proj, ds)
+
+    with torch.inference_mode():
+        for i in range(args.warmup):
+            one(i)
+        t0 = time.perf_counter()
+        for i in range(args.warmup, args.warmup + args.steps):
+            one(i)
+        dt = time.perf_counter() - t0
+    v = args.steps / dt
+    cores = torch.get_num_threads()
+    return {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"one stream-step per bench step ({args.steps} timed), batch 1, fp32, torch "
+                                       f"{torch.__version__}, CPU restatement of tools/nemotron_ane.py Step + RNN-T greedy"},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def workload_config(args):
+    return {"workload": f"C3: {args.streams} synchronous streams/GPU, [70,{args.lookahead}] (T={args.lookahead + 1}, "
+                        f"{9 + 8 + 8 * args.lookahead}-row mel chunks), 24-layer FastConformer + joint.enc + RNN-T greedy",
+            "streams_per_gpu": args.streams, "lookahead": args.lookahead, "n_layers": 24, "d_model": 1024,
+            "cache": "paged rings, 16-frame pages", "decode": not args.no_decode,
+            "l2": "inputs larger than L2 (1.16 GB of weights and the per-stream caches stream through each step)",
+            "parallelism": f"stream-sharded x{args.gpus}, no collectives"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--streams", type=int, default=256)
+    ap.add_argument("--lookahead", type=int, default=13)
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, world, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import ud
+    from oracle.weights import NEMOTRON, make_weights
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    R, n = args.lookahead, args.streams
+    T = R + 1
+    cfg = ud.default_config(max_streams=n, max_batch=n, max_chunk_frames=max(16, T))
+    eng = ud.Engine(cfg, device=local)
+    sd = make_weights(NEMOTRON, seed=0)
+    eng.load_weights(sd)
+    ids = [eng.open(R) for _ in range(n)]
+
+    dev = torch.device("cuda", local)
+    mel = torch.empty(n, TOTAL_ROWS, MEL, device=dev)
+    for s in range(n):
+        mel[s].normal_(generator=torch.Generator(device=dev).manual_seed(s))
+    tm, J, ms = cfg.max_chunk_frames, cfg.joint_dim, cfg.max_symbols
+    proj = torch.empty(n, tm, J, device=dev)
+    toks = torch.empty(n, tm * ms, device=dev, dtype=torch.int32)
+    ntok = torch.empty(n, device=dev, dtype=torch.int32)
+    torch.cuda.synchronize()
+    sched = chunk_schedule(R, TOTAL_ROWS)
+    decode = not args.no_decode
+    state = {"i": 0}
+
+    def step():
+        c = state["i"] % len(sched)
+        if c == 0 and state["i"] > 0:
+            eng.cache_evict(ids)           # the utterance ended: fresh caches and decoder state, same slots
+        start, rows = sched[c]
+        eng.step_batch_device(ids, mel.data_ptr() + start * MEL * 4, TOTAL_ROWS, [rows] * n, [rows] * n, [False] * n,
+                              proj.data_ptr(), toks.data_ptr() if decode else None, ntok.data_ptr() if decode else None)
+        state["i"] += 1
+
+    stream = torch.cuda.ExternalStream(eng.cuda_stream(), device=dev)
+    for _ in range(args.warmup):
+        step()
+    eng.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = eng.launch_count()
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        ev1.synchronize()
+    eng.synchronize()
+    launches = eng.launch_count() - l0
+    ms_dev = ev0.elapsed_time(ev1)
+    t_max = ms_dev
+    if dist:
+        t = torch.tensor([ms_dev], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max = float(t.item())
+        dist.barrier()
+    value = n * args.steps * world / (t_max / 1e3)
+
+    # Kernel attribution (outside the timed region): per-class device time over two more steps.
+    eng.profile(True)
+    for _ in range(2):
+        step()
+    prof = eng.profile_read()
+    eng.profile(False)
+    hbm, bf16_burst, bf16_sus, src = peaks()
+    tc_ms = prof["gemm_tc"][0] / 2
+    tc_launches = prof["gemm_tc"][1] / 2
+    flops = gemm_flops_per_step(n, T, R, cfg)
+    achieved = flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else None
+    traffic = None
+    tfile = ROOT / "profiles" / "gemm_tc_c3_traffic.txt"
+    if tfile.exists():
+        for line in tfile.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = float(line.split(":")[1])
+
+    # End to end through the host-buffer API (pinned host mel in, projections + tokens out), wall clock.
+    e2e = None
+    if not args.no_e2e:
+        hmel = torch.empty(n, TOTAL_ROWS, MEL, pin_memory=True)
+        hmel.copy_(mel.cpu())
+        hnp = hmel.numpy()
+        eng.cache_evict(ids)
+        state_h = {"i": 0}
+
+        def step_host():
+            c = state_h["i"] % len(sched)
+            if c == 0 and state_h["i"] > 0:
+                eng.cache_evict(ids)
+            start, rows = sched[c]
+            eng.step_batch(ids, [hnp[s, start:start + rows] for s in range(n)], [rows] * n, [rows] * n, [False] * n,
+                           decode=decode)
+            state_h["i"] += 1
+            return rows
+
+        for _ in range(args.warmup):
+            step_host()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        rows_sum = 0
+        for _ in range(args.steps):
+            rows_sum += step_host()
+        dt = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([dt], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        h2d = rows_sum / args.steps * MEL * 4 * n
+        d2h = n * tm * J * 4 + ((n * tm * ms * 4 + n * 4) if decode else 0)
+        e2e = {"value": n * args.steps * world / dt, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "timing": "host wall clock, synchronous ud_step_batch calls"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_baseline(sd, R)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        res = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args),
+               "e2e": e2e, "gpu_launches": launches,
+               "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
+                            "frac": (achieved / bf16_sus) if achieved else None, "traffic": traffic,
+                            "kernel": "gemm_tc (tcgen05)",
+                            "note": f"algorithmic GEMM FLOPs per step / summed tcgen05 GEMM time per step "
+                                    f"({tc_launches:.0f} launches), CUDA events on the engine stream; peak = "
+                                    f"{src} sustained bf16"},
+               "kernel_ms_per_step": {k: round(v[0] / 2, 4) for k, v in prof.items() if v[1]},
+               "cpu_baseline": cpu, "clocks": clk.summary()}
+        print(json.dumps(res), flush=True)
+
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

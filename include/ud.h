@@ -1,0 +1,204 @@
+/*
+ * ud.h — C ABI of the B200 streaming FastConformer engine (libud.so).
+ *
+ * This is the drop-in boundary for the reference's encoder protocol
+ *   public protocol NemotronEncoder: AnyObject {
+ *       var schedule: NemotronSchedule { get }
+ *       func step(mel: UnsafeBufferPointer<Float>, nRows: Int, validRows: Int, keepAll: Bool) throws
+ *           -> (proj: [Float], frames: Int)
+ *   }                                   (Sources/DictatorCore/Nemotron/NemotronStreamer.swift:6-12)
+ * whose GPU implementation is MetalNemotronEncoder (Sources/DictatorEngine/Models/Nemotron.swift:51-91)
+ * over FastConformerEncoder.encodeStreamStep (Sources/DictatorEngine/Models/FastConformer.swift:441-480).
+ *
+ * Plain C types only; no PyTorch. Every call returns ud_status (UD_OK = 0) and never aborts; the text
+ * of the last error on the calling thread is available from ud_last_error(). An engine is bound to one
+ * CUDA device and one CUDA stream. Calls on one engine must be serialised by the caller, as the
+ * reference drives one stream from one serial queue (Sources/DictatorCore/API/Dictation.swift:301).
+ * Different engines (for example one per GPU) may be used from different threads.
+ */
+#ifndef UD_H
+#define UD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UD_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define UD_API __attribute__((visibility("default")))
+#else
+#define UD_API
+#endif
+
+typedef enum ud_status {
+    UD_OK = 0,
+    UD_ERR_INVALID_ARGUMENT = 1, /* a size, pointer or id out of range                              */
+    UD_ERR_CUDA = 2,             /* a CUDA runtime/driver call failed                               */
+    UD_ERR_OUT_OF_MEMORY = 3,    /* device or pinned host allocation failed                         */
+    UD_ERR_NO_STREAM = 4,        /* unknown or closed stream id                                     */
+    UD_ERR_POOL_EXHAUSTED = 5,   /* no free stream slot or cache page                               */
+    UD_ERR_WEIGHTS = 6,          /* missing, duplicate or mis-shaped weight tensor                  */
+    UD_ERR_NOT_READY = 7,        /* weights not loaded yet                                          */
+    UD_ERR_DEVICE_TIMEOUT = 8,   /* a bounded device-side wait expired (the kernel returned early)  */
+    UD_ERR_IO = 9,               /* file could not be read or parsed                                */
+    UD_ERR_UNSUPPORTED = 10      /* configuration not supported by this build                       */
+} ud_status;
+
+typedef enum ud_dtype {
+    UD_DTYPE_F32 = 0,  /* weights, activations and caches in fp32 (FFMA GEMMs)                       */
+    UD_DTYPE_BF16 = 1  /* bf16 weights/activations/caches, fp32 accumulation, LN and softmax (tcgen05) */
+} ud_dtype;
+
+/* Static model + engine configuration (FastConformerConfig, FastConformer.swift:5-38, plus the
+ * RNN-T head of RNNTDecoder, Sources/DictatorCore/Decoding/RNNT.swift:7-18). */
+typedef struct ud_config {
+    int n_layers;         /* 24                                                                      */
+    int d_model;          /* 1024 (this build: 1024)                                                 */
+    int n_heads;          /* 8    (head dim must be 128)                                             */
+    int ff_dim;           /* 4096                                                                    */
+    int conv_kernel;      /* 9    (causal depthwise; cache of conv_kernel-1 frames)                  */
+    int left_context;     /* 70   (attention left context L of [L, R])                               */
+    int sub_channels;     /* 256; 0 = no subsampling: steps take encoder frames instead of mel rows  */
+    int mel_bins;         /* 128                                                                     */
+    int joint_dim;        /* 640; 0 = no joint projection / RNN-T head                               */
+    int vocab;            /* 1025 (1024 ids + blank; blank = vocab-1)                                */
+    int pred_layers;      /* LSTM layers of the prediction net                                       */
+    int pred_hidden;      /* 640                                                                     */
+    int max_symbols;      /* greedy symbols per frame, 10                                            */
+    int dtype;            /* ud_dtype                                                                */
+    int max_streams;      /* concurrent stream slots                                                 */
+    int max_batch;        /* streams per batched step                                                */
+    int max_chunk_frames; /* largest T (encoder frames per step) any step may produce, <= 32         */
+    int page_frames;      /* frames per cache page (16)                                              */
+    int n_pages;          /* page pool size; 0 = enough for every slot                               */
+} ud_config;
+
+typedef struct ud_engine ud_engine;
+typedef int32_t ud_stream_id;
+
+/* One weight tensor in checkpoint naming and layout (docs/specs/nemotron.md section 8), fp32 host data. */
+typedef struct ud_weight {
+    const char* name;
+    const float* data;
+    int ndim;
+    int64_t shape[4];
+} ud_weight;
+
+/* Nemotron defaults: 24 layers, d 1024, 8x128 heads, ff 4096, k 9, L 70, subsampling 256, joint 640,
+ * vocab 1025, 1 LSTM layer of 640, bf16, 64 slots, batch 64, 16 frames per chunk, 16-frame pages. */
+UD_API void ud_config_default(ud_config* cfg);
+
+UD_API ud_status ud_init(const ud_config* cfg, int device, ud_engine** out);
+UD_API ud_status ud_shutdown(ud_engine* e);
+
+/* Copies (and converts) every tensor the configuration needs; all must be present with checkpoint
+ * shapes. Replaces NemotronModel.init's weight loading (Sources/DictatorEngine/Models/Nemotron.swift:35-46). */
+UD_API ud_status ud_load_weights(ud_engine* e, const ud_weight* table, int n);
+/* Same from a safetensors file with F32/F16/BF16 tensors (Sources/DictatorEngine/Core/SafeTensors.swift). */
+UD_API ud_status ud_load_safetensors(ud_engine* e, const char* path);
+
+/* A stream = the caches and decoder state one NemotronEncoder object owns (zeroed on open). */
+UD_API ud_status ud_stream_open(ud_engine* e, int lookahead, ud_stream_id* out);
+UD_API ud_status ud_stream_close(ud_engine* e, ud_stream_id id);   /* evicts: frees its pages and slot */
+
+/* The protocol call, one stream: mel [n_rows, mel_bins] fp32 host rows (pre-encode cache rows
+ * included), the first valid_rows real. Writes proj_out [frames, joint_dim] fp32 host (room for
+ * max_chunk_frames rows) and *frames_out = keep_all ? validT : min(validT, lookahead+1)
+ * (Nemotron.swift:74-91). Synchronous. With sub_channels == 0 the input is encoder frames
+ * [n_rows, d_model] and the output is the last layer's output [n_rows, d_model]. */
+UD_API ud_status ud_stream_step(ud_engine* e, ud_stream_id id, const float* mel, int n_rows, int valid_rows,
+                         int keep_all, float* proj_out, int* frames_out);
+
+/* Batched protocol calls over n distinct streams (one encoder pass for all of them), host buffers.
+ * mel[i] points at stream i's rows. proj_out: n * max_chunk_frames * joint_dim floats, stream i at
+ * proj_out + i*max_chunk_frames*joint_dim. If tokens_out is not NULL the RNN-T greedy decoder
+ * (RNNT.swift:127-151) also runs on the kept frames with each stream's carried state:
+ * tokens_out holds n * max_chunk_frames * max_symbols ids, stream i at offset
+ * i*max_chunk_frames*max_symbols, and n_tokens_out[i] their count. Synchronous. */
+UD_API ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* const* mel,
+                        const int* n_rows, const int* valid_rows, const int* keep_all,
+                        float* proj_out, int* frames_out, int32_t* tokens_out, int* n_tokens_out);
+
+/* Same with device-resident input and outputs, asynchronous on the engine's CUDA stream:
+ * mel_dev [n, rows_stride, mel_bins] fp32 (stream i's rows at i*rows_stride), proj_dev
+ * [n, max_chunk_frames, joint_dim], tokens_dev / n_tokens_dev as above or NULL. frames_out (host)
+ * is known before the kernels run and is filled on return. */
+UD_API ud_status ud_step_batch_device(ud_engine* e, int n, const ud_stream_id* ids, const float* mel_dev,
+                               int rows_stride, const int* n_rows, const int* valid_rows,
+                               const int* keep_all, float* proj_dev, int* frames_out,
+                               int32_t* tokens_dev, int* n_tokens_dev);
+
+/* RNN-T greedy decode of projected frames f [frames, joint_dim] (fp32 host) with the stream's carried
+ * decoder state (RNNT.swift:127-151). tokens_out has room for frames*max_symbols ids. */
+UD_API ud_status ud_rnnt_decode(ud_engine* e, ud_stream_id id, const float* f, int frames, int32_t* tokens_out,
+                         int* n_tokens_out);
+
+/* Cache operations on the paged per-stream rings (the reference's cache roll, FastConformer.swift:464-477).
+ * kind: 0 = K (projected keys), 1 = V (projected values), 2 = conv (depthwise-conv inputs).
+ * Rows are in the engine dtype (bf16 or fp32), d_model wide, device pointers.
+ *   append: kv_rows [n, n_layers, 2, k, d]; conv_rows [n, n_layers, k, d] (either may be NULL);
+ *           writes the k frames after each stream's head (allocating pages as needed).
+ *   roll:   head += k, cacheLen = min(cacheLen + k, L); frees pages that left the window (metadata).
+ *   gather: kv_out [n, n_layers, 2, L, d] = each stream's window (unfilled rows zero);
+ *           conv_out [n, n_layers, conv_kernel-1, d] (either may be NULL).
+ *   evict:  close and reopen the stream (fresh zero caches, same id).
+ * append/gather are asynchronous on the engine stream; use ud_synchronize before reading results. */
+UD_API ud_status ud_cache_append(ud_engine* e, int n, const ud_stream_id* ids, int k, const void* kv_rows,
+                          const void* conv_rows);
+UD_API ud_status ud_cache_roll(ud_engine* e, int n, const ud_stream_id* ids, int k);
+UD_API ud_status ud_cache_gather(ud_engine* e, int n, const ud_stream_id* ids, void* kv_out, void* conv_out);
+UD_API ud_status ud_cache_evict(ud_engine* e, int n, const ud_stream_id* ids);
+/* One stream's window of one layer and kind, copied to host: K/V [L, d], conv [conv_kernel-1, d]. */
+UD_API ud_status ud_cache_read(ud_engine* e, ud_stream_id id, int layer, int kind, void* host_out);
+/* cacheLen and absolute head frame of a stream. */
+UD_API ud_status ud_stream_info(ud_engine* e, ud_stream_id id, int* cache_len, int* head, int* step);
+
+/* Engine facts: the CUDA stream (cudaStream_t) work is issued on, free pages, element size. */
+UD_API ud_status ud_get_cuda_stream(ud_engine* e, void** stream_out);
+UD_API ud_status ud_pool_info(ud_engine* e, int* free_pages, int* total_pages, int* elem_bytes);
+UD_API ud_status ud_synchronize(ud_engine* e);
+/* Number of this library's kernels launched on the engine since init (counts graph replays' kernels). */
+UD_API ud_status ud_launch_count(ud_engine* e, int64_t* out);
+
+/* Per-kernel-class timing (CUDA events around each launch on the engine stream). Off by default; enabling
+ * it clears the totals. ud_profile_read synchronises and returns the summed device time and launch count
+ * of one class. Used outside timed regions to attribute a step's time to its kernels. */
+typedef enum ud_kernel_kind {
+    UD_KIND_GEMM_TC = 0,    /* tcgen05 GEMM                                    */
+    UD_KIND_GEMM_SIMT = 1,  /* few-row / fp32 FFMA GEMM                         */
+    UD_KIND_ATTENTION = 2,  /* rel-pos attention + K/V append                   */
+    UD_KIND_CONV = 3,       /* conv module (GLU, depthwise, LN, SiLU, ring)     */
+    UD_KIND_NORM = 4,       /* LayerNorm                                        */
+    UD_KIND_SUBSAMPLE = 5,  /* subsampling convs, row select / pack             */
+    UD_KIND_RNNT = 6,       /* RNN-T greedy                                     */
+    UD_KIND_CACHE = 7,      /* cache append / gather / reset                    */
+    UD_KIND_OTHER = 8,
+    UD_KIND_COUNT = 9
+} ud_kernel_kind;
+UD_API ud_status ud_profile_enable(ud_engine* e, int enable);
+UD_API ud_status ud_profile_read(ud_engine* e, int kind, double* ms_total, int64_t* launches);
+
+/* Kernel-level test hook (the reference's GemmTests.swift contract, Step.gemm in Core/Kernels.swift:79-113):
+ * C = out_scale * act(A . W^T + bias) + res_scale * R, device pointers, A [M,K] and W [N,K] in the
+ * engine dtype, C fp32 [M,N] (or bf16 if out_bf16), act 0 none / 1 relu / 2 silu, R fp32 or NULL. */
+UD_API ud_status ud_debug_gemm(ud_engine* e, const void* A, const void* W, int M, int N, int K, const float* bias,
+                        int act, float out_scale, const float* residual, float res_scale, void* C, int out_bf16);
+
+/* Failure-detection probe: launches a kernel that waits on a device flag nothing sets, with the same bounded
+ * wait the pipelined kernels use; it gives up after limit_ns, and the call returns UD_ERR_DEVICE_TIMEOUT
+ * with the engine still usable. */
+UD_API ud_status ud_debug_wait_probe(ud_engine* e, uint64_t limit_ns);
+
+/* Text of the last error on this thread ("" if none). Returns the full length. */
+UD_API size_t ud_last_error(char* buf, size_t len);
+UD_API const char* ud_status_string(ud_status s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UD_H */

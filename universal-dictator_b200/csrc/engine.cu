@@ -1,0 +1,1520 @@
+// libud engine: the C ABI of include/ud.h over the sm_100a kernels.
+//
+// One engine = one CUDA device + one CUDA stream + shared weights + a pool of stream slots. It replaces
+// MetalNemotronEncoder (Sources/DictatorEngine/Models/Nemotron.swift:51-91) and the per-stream
+// FastConformerEncoder.StreamState (FastConformer.swift:406-435) with:
+//   * paged per-stream K/V rings (pages of page_frames frames, kPageSlots page slots per stream, frame f at
+//     row f % PF of page pages[(f / PF) % kPageSlots]); the roll is metadata only;
+//   * a conv ring of conv_kernel-1 rows per (layer, stream);
+//   * batched steps: the frames of all streams in a call are packed into one [M, d_model] activation block,
+//     so every projection is one GEMM over M = sum of T (tcgen05 for bf16, FFMA for fp32).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "ud.h"
+
+using namespace ud;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+ud_status fail(ud_status s, const std::string& msg) {
+    g_last_error = msg;
+    return s;
+}
+
+#define UD_CK(call)                                                                                  \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) return fail(UD_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+int nxt(int t) { return t / 2 + 1; }
+int sub_len(int t) { return nxt(nxt(nxt(t))); }
+
+struct WeightMat {
+    void* p = nullptr;
+    int N = 0, K = 0;
+    TmaMatrix tma128, tma256;
+    bool has_tma = false, has256 = false;
+};
+
+struct LayerW {
+    WeightMat ff1_w1, ff1_w2, ff2_w1, ff2_w2, wqkv, wo, pw1, pw2;
+    float *ln_ff1_g, *ln_ff1_b, *ln_att_g, *ln_att_b, *ln_conv_g, *ln_conv_b, *ln_cbn_g, *ln_cbn_b;
+    float *ln_ff2_g, *ln_ff2_b, *ln_out_g, *ln_out_b;
+    float *pos_u, *pos_v, *dw;
+    void* ptab;
+};
+
+struct Slot {
+    bool open = false;
+    int lookahead = 0, step = 0, head = 0, cache_len = 0;
+    int lp[kPageSlots];
+    int pages[kPageSlots];
+    void reset() {
+        step = head = cache_len = 0;
+        for (int i = 0; i < kPageSlots; ++i) lp[i] = pages[i] = -1;
+    }
+};
+
+}  // namespace
+
+struct ud_engine {
+    ud_config cfg{};
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    bool loaded = false;
+    bool bf = true;
+    int esz = 2;
+    int tmax = 16, L = 70, D = 1024, H = 8, F = 4096, KC = 9, C = 256, F1 = 65, F2 = 33, F3 = 17, J = 640;
+    int max_rows_in = 0;  // input rows per stream per step
+    int in_width = 0;     // mel_bins or d_model
+    int out_width = 0;    // joint_dim or d_model
+    int Mcap = 0;
+    std::vector<void*> allocs;
+    std::vector<void*> host_allocs;
+
+    std::vector<LayerW> layers;
+    float *c0_w = nullptr, *c0_b = nullptr, *c2_w = nullptr, *c2_b = nullptr, *c5_w = nullptr, *c5_b = nullptr;
+    float *c3_b = nullptr, *c6_b = nullptr, *out_b = nullptr;
+    WeightMat c3, c6, sub_out, jenc;
+    float* jenc_b = nullptr;
+    RnntWeights rw{};
+    RnntState rs{};
+
+    CacheGeom cg{};
+    std::vector<int> free_pages;
+    std::vector<Slot> slots;
+    std::vector<int> free_slots;
+
+    float* x = nullptr;
+    void *h = nullptr, *hid = nullptr, *qkv = nullptr, *att = nullptr, *pw = nullptr, *y = nullptr;
+    float* proj = nullptr;
+    void *a1 = nullptr, *a2 = nullptr, *a3 = nullptr, *a4 = nullptr, *a5 = nullptr;
+    float* subout = nullptr;
+    float* in_stage = nullptr;
+    float* out_stage = nullptr;
+    int32_t* tok_dev = nullptr;
+    int* ntok_dev = nullptr;
+    void* gather_scratch = nullptr;
+
+    float* h_in = nullptr;
+    float* h_out = nullptr;
+    int32_t* h_tok = nullptr;
+    int* h_ntok = nullptr;
+
+    static constexpr int kRing = 4;
+    BatchEntry* meta_h[kRing] = {};
+    BatchEntry* meta_d[kRing] = {};
+    cudaEvent_t meta_ev[kRing] = {};
+    int meta_i = 0;
+    int* slots_h = nullptr;
+    int* slots_d = nullptr;
+    int* err_d = nullptr;
+    int* err_h = nullptr;
+    int64_t launches = 0;
+    std::map<std::tuple<const void*, int, int, int>, TmaMatrix> amaps;
+    // per-kernel-class timing
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_events;
+    std::vector<std::pair<int, size_t>> prof_marks;  // (kind, index of the begin event; end = index + 1)
+    size_t prof_used = 0;
+    double prof_ms[UD_KIND_COUNT] = {};
+    int64_t prof_n[UD_KIND_COUNT] = {};
+};
+
+namespace {
+
+// Counts one launch of this library's kernels and, when profiling, brackets it with events.
+struct Launch {
+    ud_engine* e;
+    int kind;
+    size_t idx = 0;
+    bool on;
+    Launch(ud_engine* e_, int k) : e(e_), kind(k), on(e_->prof) {
+        if (!on) return;
+        if (e->prof_used + 2 > e->prof_events.size()) {
+            for (int i = 0; i < 256; ++i) {
+                cudaEvent_t ev;
+                cudaEventCreate(&ev);
+                e->prof_events.push_back(ev);
+            }
+        }
+        idx = e->prof_used;
+        e->prof_used += 2;
+        cudaEventRecord(e->prof_events[idx], e->stream);
+    }
+    ~Launch() {
+        e->launches++;
+        if (!on) return;
+        cudaEventRecord(e->prof_events[idx + 1], e->stream);
+        e->prof_marks.emplace_back(kind, idx);
+    }
+};
+
+void prof_flush(ud_engine* e) {
+    if (e->prof_marks.empty()) return;
+    cudaStreamSynchronize(e->stream);
+    for (auto& m : e->prof_marks) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, e->prof_events[m.second], e->prof_events[m.second + 1]) == cudaSuccess) {
+            e->prof_ms[m.first] += ms;
+            e->prof_n[m.first] += 1;
+        }
+    }
+    cudaGetLastError();
+    e->prof_marks.clear();
+    e->prof_used = 0;
+}
+
+template <typename T>
+ud_status dalloc(ud_engine* e, T** p, size_t count) {
+    void* q = nullptr;
+    if (count == 0) count = 1;
+    if (cudaMalloc(&q, count * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(UD_ERR_OUT_OF_MEMORY, "cudaMalloc of " + std::to_string(count * sizeof(T)) + " bytes failed");
+    }
+    e->allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return UD_OK;
+}
+
+ud_status dalloc_bytes(ud_engine* e, void** p, size_t bytes) {
+    return dalloc<uint8_t>(e, reinterpret_cast<uint8_t**>(p), bytes);
+}
+
+template <typename T>
+ud_status halloc(ud_engine* e, T** p, size_t count) {
+    void* q = nullptr;
+    if (count == 0) count = 1;
+    if (cudaMallocHost(&q, count * sizeof(T)) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(UD_ERR_OUT_OF_MEMORY, "cudaMallocHost failed");
+    }
+    e->host_allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return UD_OK;
+}
+
+#define UD_TRY(x)                      \
+    do {                               \
+        ud_status s_ = (x);            \
+        if (s_ != UD_OK) return s_;    \
+    } while (0)
+
+bool tc_ok(int N, int K) { return N % 128 == 0 && K % 64 == 0; }
+
+// One GEMM through the engine's dispatch: tcgen05 for bf16 with more than 16 rows, SIMT otherwise.
+ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, const GemmEpilogue& epi) {
+    if (M <= 0) return UD_OK;
+    const bool tc = e->bf && M > 16 && W.has_tma;
+    Launch L_(e, tc ? UD_KIND_GEMM_TC : UD_KIND_GEMM_SIMT);
+    if (e->bf) {
+        if (!tc) {
+            gemm_simt<bf16, bf16>(static_cast<const bf16*>(A), lda, static_cast<const bf16*>(W.p), M, W.N, W.K, epi,
+                                  e->stream);
+        } else {
+            auto key = std::make_tuple(A, M, W.K, lda);
+            auto it = e->amaps.find(key);
+            if (it == e->amaps.end()) {
+                TmaMatrix t;
+                if (!make_tma_bf16(t, A, M, W.K, lda, 128))
+                    return fail(UD_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
+                it = e->amaps.emplace(key, t).first;
+            }
+            const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;
+            gemm_tc(it->second, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms, e->stream);
+        }
+    } else {
+        gemm_simt<float, float>(static_cast<const float*>(A), lda, static_cast<const float*>(W.p), M, W.N, W.K, epi,
+                                e->stream);
+    }
+    return UD_OK;
+}
+
+GemmEpilogue epi_out(void* out, int ldo, bool out_act_dtype, const ud_engine* e) {
+    GemmEpilogue g;
+    g.out = out;
+    g.ldo = ldo;
+    g.out_bf16 = (out_act_dtype && e->bf) ? 1 : 0;
+    return g;
+}
+
+ud_status check_device_error(ud_engine* e) {
+    UD_CK(cudaMemcpyAsync(e->err_h, e->err_d, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    UD_CK(cudaStreamSynchronize(e->stream));
+    const int code = *e->err_h;
+    if (code != 0) {
+        UD_CK(cudaMemsetAsync(e->err_d, 0, sizeof(int), e->stream));
+        UD_CK(cudaStreamSynchronize(e->stream));
+        static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
+                                      "GEMM TMEM drain wait", "unmapped cache page", "test wait"};
+        const char* nm = (code >= 0 && code <= 6) ? names[code] : "unknown";
+        if (code == DEV_BAD_PAGE) return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
+        return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
+    }
+    return UD_OK;
+}
+
+// ---------------------------------------------------------------- pages
+void free_out_of_window(ud_engine* e, Slot& s) {
+    const int PF = e->cfg.page_frames;
+    const int win_lo = s.head - e->L;  // first frame still in the left context
+    for (int i = 0; i < kPageSlots; ++i) {
+        if (s.lp[i] >= 0 && (s.lp[i] + 1) * PF <= win_lo) {
+            e->free_pages.push_back(s.pages[i]);
+            s.lp[i] = s.pages[i] = -1;
+        }
+    }
+}
+
+void free_all_pages(ud_engine* e, Slot& s) {
+    for (int i = 0; i < kPageSlots; ++i) {
+        if (s.lp[i] >= 0) e->free_pages.push_back(s.pages[i]);
+        s.lp[i] = s.pages[i] = -1;
+    }
+}
+
+// Maps pages for frames [s.head, s.head + k). Records what it mapped so a failed batch can undo it.
+ud_status map_pages(ud_engine* e, Slot& s, int k, std::vector<std::pair<Slot*, int>>& undo) {
+    const int PF = e->cfg.page_frames;
+    for (int f = s.head; f < s.head + k; ++f) {
+        const int lp = f / PF, ps = lp % kPageSlots;
+        if (s.lp[ps] == lp) continue;
+        if (s.lp[ps] >= 0)
+            return fail(UD_ERR_INVALID_ARGUMENT, "page ring overflow: a chunk plus the left context exceeds the ring");
+        if (e->free_pages.empty()) return fail(UD_ERR_POOL_EXHAUSTED, "cache page pool exhausted");
+        s.pages[ps] = e->free_pages.back();
+        e->free_pages.pop_back();
+        s.lp[ps] = lp;
+        undo.emplace_back(&s, ps);
+    }
+    return UD_OK;
+}
+
+void undo_pages(ud_engine* e, std::vector<std::pair<Slot*, int>>& undo) {
+    for (auto it = undo.rbegin(); it != undo.rend(); ++it) {
+        e->free_pages.push_back(it->first->pages[it->second]);
+        it->first->lp[it->second] = it->first->pages[it->second] = -1;
+    }
+    undo.clear();
+}
+
+BatchEntry* next_meta_host(ud_engine* e, int* ring_index) {
+    const int mi = e->meta_i;
+    cudaEventSynchronize(e->meta_ev[mi]);
+    *ring_index = mi;
+    return e->meta_h[mi];
+}
+
+ud_status upload_meta(ud_engine* e, int mi, int n) {
+    UD_CK(cudaMemcpyAsync(e->meta_d[mi], e->meta_h[mi], sizeof(BatchEntry) * n, cudaMemcpyHostToDevice, e->stream));
+    UD_CK(cudaEventRecord(e->meta_ev[mi], e->stream));
+    e->meta_i = (mi + 1) % ud_engine::kRing;
+    return UD_OK;
+}
+
+ud_status check_ids(ud_engine* e, int n, const ud_stream_id* ids) {
+    if (n < 1 || n > e->cfg.max_batch) return fail(UD_ERR_INVALID_ARGUMENT, "batch size out of range");
+    if (!ids) return fail(UD_ERR_INVALID_ARGUMENT, "ids is NULL");
+    std::vector<int> seen;
+    seen.reserve(n);
+    for (int i = 0; i < n; ++i) {
+        const int id = ids[i];
+        if (id < 0 || id >= e->cfg.max_streams || !e->slots[id].open)
+            return fail(UD_ERR_NO_STREAM, "unknown or closed stream id " + std::to_string(id));
+        seen.push_back(id);
+    }
+    std::sort(seen.begin(), seen.end());
+    if (std::adjacent_find(seen.begin(), seen.end()) != seen.end())
+        return fail(UD_ERR_INVALID_ARGUMENT, "a stream id appears twice in one batch");
+    return UD_OK;
+}
+
+// ---------------------------------------------------------------- the batched step
+ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* in_dev, int rows_stride,
+                    const int* n_rows, const int* valid_rows, const int* keep_all, float* out_dev, int* frames_out,
+                    int32_t* tokens_dev, int* ntok_dev) {
+    if (!e->loaded) return fail(UD_ERR_NOT_READY, "weights not loaded");
+    UD_TRY(check_ids(e, n, ids));
+    if (!n_rows || !valid_rows || !in_dev || !out_dev) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (tokens_dev && !e->cfg.joint_dim) return fail(UD_ERR_INVALID_ARGUMENT, "no RNN-T head in this configuration");
+    const bool sub = e->cfg.sub_channels > 0;
+    const int L = e->L, D = e->D;
+    int mi = 0;
+    BatchEntry* mh = next_meta_host(e, &mi);
+    int M = 0, tmax_b = 0, rows_max = 0;
+    for (int i = 0; i < n; ++i) {
+        Slot& s = e->slots[ids[i]];
+        const int nr = n_rows[i], vr = valid_rows[i];
+        if (nr < 1 || nr > rows_stride || nr > e->max_rows_in || vr < 0 || vr > nr)
+            return fail(UD_ERR_INVALID_ARGUMENT, "n_rows/valid_rows out of range for stream " + std::to_string(ids[i]));
+        int drop = 0, T, vt, keep;
+        if (sub) {
+            drop = s.step == 0 ? 0 : 2;
+            T = sub_len(nr) - drop;
+            vt = std::max(0, std::min(sub_len(vr) - drop, T));
+            keep = (keep_all && keep_all[i]) ? vt : std::min(vt, s.lookahead + 1);
+        } else {
+            T = nr;
+            vt = vr;
+            keep = T;
+        }
+        if (T < 1 || T > e->tmax)
+            return fail(UD_ERR_INVALID_ARGUMENT, "chunk of " + std::to_string(T) + " frames outside [1, max_chunk_frames]");
+        BatchEntry& b = mh[i];
+        b.slot = ids[i];
+        b.row_off = M;
+        b.T = T;
+        b.valid_t = vt;
+        b.cache_len = s.cache_len;
+        b.head = s.head;
+        b.drop = drop;
+        b.valid_mel = vr;
+        b.n_rows = nr;
+        b.keep = keep;
+        b.tok_off = i * e->tmax * e->cfg.max_symbols;
+        b.pad = 0;
+        M += T;
+        tmax_b = std::max(tmax_b, T);
+        rows_max = std::max(rows_max, nr);
+    }
+    std::vector<std::pair<Slot*, int>> undo;
+    for (int i = 0; i < n; ++i) {
+        ud_status st = map_pages(e, e->slots[ids[i]], mh[i].T, undo);
+        if (st != UD_OK) {
+            undo_pages(e, undo);
+            return st;
+        }
+        std::memcpy(mh[i].pages, e->slots[ids[i]].pages, sizeof(mh[i].pages));
+    }
+    UD_TRY(upload_meta(e, mi, n));
+    const BatchEntry* md = e->meta_d[mi];
+    cudaStream_t st = e->stream;
+
+    // ---- encoder input: subsampling, or frames as given
+    if (sub) {
+        const int Tin = rows_max, T1 = nxt(Tin), T2 = nxt(T1), T3 = nxt(T2), C = e->C;
+        {
+            Launch L_(e, UD_KIND_SUBSAMPLE);
+            if (e->bf)
+                sub_conv0<bf16>(in_dev, rows_stride, e->cfg.mel_bins, md, n, Tin, e->c0_w, e->c0_b, (bf16*)e->a1, T1, e->F1, C, st);
+            else
+                sub_conv0<float>(in_dev, rows_stride, e->cfg.mel_bins, md, n, Tin, e->c0_w, e->c0_b, (float*)e->a1, T1, e->F1, C, st);
+        }
+        {
+            Launch L_(e, UD_KIND_SUBSAMPLE);
+            if (e->bf)
+                sub_dwconv<bf16>((bf16*)e->a1, T1, e->F1, nullptr, 1, md, n, e->c2_w, e->c2_b, (bf16*)e->a2, T2, e->F2, C, st);
+            else
+                sub_dwconv<float>((float*)e->a1, T1, e->F1, nullptr, 1, md, n, e->c2_w, e->c2_b, (float*)e->a2, T2, e->F2, C, st);
+        }
+        GemmEpilogue g3 = epi_out(e->a3, C, true, e);
+        g3.bias = e->c3_b;
+        g3.act = ACT_RELU;
+        UD_TRY(gemm(e, e->a2, C, n * T2 * e->F2, e->c3, g3));
+        {
+        Launch L_(e, UD_KIND_SUBSAMPLE);
+        if (e->bf)
+            sub_dwconv<bf16>((bf16*)e->a3, T2, e->F2, nullptr, 2, md, n, e->c5_w, e->c5_b, (bf16*)e->a4, T3, e->F3, C, st);
+        else
+            sub_dwconv<float>((float*)e->a3, T2, e->F2, nullptr, 2, md, n, e->c5_w, e->c5_b, (float*)e->a4, T3, e->F3, C, st);
+        }
+        GemmEpilogue g6 = epi_out(e->a5, C, true, e);
+        g6.bias = e->c6_b;
+        g6.act = ACT_RELU;
+        UD_TRY(gemm(e, e->a4, C, n * T3 * e->F3, e->c6, g6));
+        GemmEpilogue go = epi_out(e->subout, D, false, e);
+        go.bias = e->out_b;
+        UD_TRY(gemm(e, e->a5, e->F3 * C, n * T3, e->sub_out, go));
+        {
+            Launch L_(e, UD_KIND_SUBSAMPLE);
+            sub_select<float>(e->subout, T3, e->out_b, md, n, e->x, D, st);
+        }
+    } else {
+        Launch L_(e, UD_KIND_SUBSAMPLE);
+        pack_frames(in_dev, rows_stride, md, n, tmax_b, e->x, D, st);
+    }
+
+    // ---- conformer layers
+    const int NL = e->cfg.n_layers;
+    auto ln = [&](const float* g, const float* b) {
+        Launch L_(e, UD_KIND_NORM);
+        if (e->bf) layer_norm<bf16>(e->x, g, b, (bf16*)e->h, M, D, st);
+        else layer_norm<float>(e->x, g, b, (float*)e->h, M, D, st);
+    };
+    auto resid = [&](float scale) {
+        GemmEpilogue g = epi_out(e->x, D, false, e);
+        g.residual = e->x;
+        g.ldr = D;
+        g.out_scale = scale;
+        return g;
+    };
+    if (NL > 0) ln(e->layers[0].ln_ff1_g, e->layers[0].ln_ff1_b);
+    for (int l = 0; l < NL; ++l) {
+        LayerW& w = e->layers[l];
+        GemmEpilogue gs = epi_out(e->hid, e->F, true, e);
+        gs.act = ACT_SILU;
+        UD_TRY(gemm(e, e->h, D, M, w.ff1_w1, gs));
+        UD_TRY(gemm(e, e->hid, e->F, M, w.ff1_w2, resid(0.5f)));
+        ln(w.ln_att_g, w.ln_att_b);
+        UD_TRY(gemm(e, e->h, D, M, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
+        {
+        Launch L_(e, UD_KIND_ATTENTION);
+        if (e->bf)
+            relpos_attention<bf16>((bf16*)e->qkv, 3 * D, (bf16*)w.ptab, e->tmax, w.pos_u, w.pos_v, md, n, tmax_b, e->cg, l,
+                                   (bf16*)e->att, D, e->H, e->err_d, st);
+        else
+            relpos_attention<float>((float*)e->qkv, 3 * D, (float*)w.ptab, e->tmax, w.pos_u, w.pos_v, md, n, tmax_b, e->cg,
+                                    l, (float*)e->att, D, e->H, e->err_d, st);
+        }
+        UD_TRY(gemm(e, e->att, D, M, w.wo, resid(1.0f)));
+        ln(w.ln_conv_g, w.ln_conv_b);
+        UD_TRY(gemm(e, e->h, D, M, w.pw1, epi_out(e->pw, 2 * D, true, e)));
+        {
+        Launch L_(e, UD_KIND_CONV);
+        if (e->bf)
+            conv_module<bf16>((bf16*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, md, n, tmax_b, e->cg, l, e->KC, (bf16*)e->y,
+                              D, st);
+        else
+            conv_module<float>((float*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, md, n, tmax_b, e->cg, l, e->KC,
+                               (float*)e->y, D, st);
+        }
+        UD_TRY(gemm(e, e->y, D, M, w.pw2, resid(1.0f)));
+        ln(w.ln_ff2_g, w.ln_ff2_b);
+        UD_TRY(gemm(e, e->h, D, M, w.ff2_w1, gs));
+        UD_TRY(gemm(e, e->hid, e->F, M, w.ff2_w2, resid(0.5f)));
+        if (l + 1 < NL) {
+            LayerW& nx = e->layers[l + 1];
+            Launch L_(e, UD_KIND_NORM);
+            if (e->bf) layer_norm2<bf16>(e->x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (bf16*)e->h, M, D, st);
+            else layer_norm2<float>(e->x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (float*)e->h, M, D, st);
+        } else if (e->cfg.joint_dim) {
+            ln(w.ln_out_g, w.ln_out_b);  // h = LN_out(x): the joint's operand
+        } else {
+            Launch L_(e, UD_KIND_NORM);
+            layer_norm<float>(e->x, w.ln_out_g, w.ln_out_b, e->x, M, D, st);
+        }
+    }
+
+    // ---- joint encoder projection, outputs, RNN-T
+    if (e->cfg.joint_dim) {
+        GemmEpilogue gj = epi_out(e->proj, e->J, false, e);
+        gj.bias = e->jenc_b;
+        UD_TRY(gemm(e, e->h, D, M, e->jenc, gj));
+        {
+            Launch L_(e, UD_KIND_OTHER);
+            scatter_rows(e->proj, md, n, out_dev, e->tmax, e->J, st);
+        }
+        if (tokens_dev) {
+            Launch L_(e, UD_KIND_RNNT);
+            rnnt_greedy(e->rw, e->rs, e->proj, e->J, md, n, tokens_dev, e->tmax * e->cfg.max_symbols, ntok_dev, st);
+        }
+    } else {
+        Launch L_(e, UD_KIND_OTHER);
+        scatter_rows(e->x, md, n, out_dev, e->tmax, D, st);
+    }
+    UD_CK(cudaGetLastError());
+
+    // ---- roll: metadata only
+    for (int i = 0; i < n; ++i) {
+        Slot& s = e->slots[ids[i]];
+        s.head += mh[i].T;
+        s.cache_len = std::min(s.cache_len + mh[i].T, L);
+        s.step += 1;
+        free_out_of_window(e, s);
+        if (frames_out) frames_out[i] = mh[i].keep;
+    }
+    return UD_OK;
+}
+
+// ---------------------------------------------------------------- weights
+struct WeightTable {
+    std::map<std::string, const ud_weight*> by_name;
+};
+
+ud_status need(const WeightTable& t, const std::string& name, std::vector<int64_t> shape, const float** out) {
+    auto it = t.by_name.find(name);
+    if (it == t.by_name.end()) return fail(UD_ERR_WEIGHTS, "missing weight " + name);
+    const ud_weight* w = it->second;
+    bool ok = w->ndim == static_cast<int>(shape.size()) && w->data;
+    for (size_t i = 0; ok && i < shape.size(); ++i) ok = w->shape[i] == shape[i];
+    if (!ok) return fail(UD_ERR_WEIGHTS, "weight " + name + " has the wrong shape");
+    *out = w->data;
+    return UD_OK;
+}
+
+ud_status upload_f32(ud_engine* e, const float* host, size_t n, float** out) {
+    UD_TRY(dalloc(e, out, n));
+    UD_CK(cudaMemcpy(*out, host, n * sizeof(float), cudaMemcpyHostToDevice));
+    return UD_OK;
+}
+
+// Device fp32 staging for conversions (largest single weight).
+struct Staging {
+    float* p = nullptr;
+    size_t cap = 0;
+};
+
+ud_status upload_gemm(ud_engine* e, Staging& stg, const std::vector<const float*>& parts, const std::vector<int>& part_rows,
+                      int K, WeightMat& W) {
+    int N = 0;
+    for (int r : part_rows) N += r;
+    W.N = N;
+    W.K = K;
+    const size_t n = static_cast<size_t>(N) * K;
+    if (e->bf) {
+        if (n > stg.cap) return fail(UD_ERR_WEIGHTS, "staging buffer too small");
+        size_t off = 0;
+        for (size_t i = 0; i < parts.size(); ++i) {
+            UD_CK(cudaMemcpy(stg.p + off, parts[i], sizeof(float) * part_rows[i] * K, cudaMemcpyHostToDevice));
+            off += static_cast<size_t>(part_rows[i]) * K;
+        }
+        void* p;
+        UD_TRY(dalloc_bytes(e, &p, n * 2));
+        f32_to_bf16(stg.p, static_cast<bf16*>(p), n, e->stream);
+        UD_CK(cudaStreamSynchronize(e->stream));
+        W.p = p;
+        if (tc_ok(N, K)) {
+            if (!make_tma_bf16(W.tma128, p, N, K, K, 128)) return fail(UD_ERR_CUDA, "tensor map for a weight failed");
+            W.has_tma = true;
+            if (N % 256 == 0) {
+                if (!make_tma_bf16(W.tma256, p, N, K, K, 256)) return fail(UD_ERR_CUDA, "tensor map for a weight failed");
+                W.has256 = true;
+            }
+        }
+    } else {
+        float* p;
+        UD_TRY(dalloc(e, &p, n));
+        size_t off = 0;
+        for (size_t i = 0; i < parts.size(); ++i) {
+            UD_CK(cudaMemcpy(p + off, parts[i], sizeof(float) * part_rows[i] * K, cudaMemcpyHostToDevice));
+            off += static_cast<size_t>(part_rows[i]) * K;
+        }
+        W.p = p;
+    }
+    return UD_OK;
+}
+
+// NeMo RelPositionalEncoding rows (fp32 as torch computes them) for rel in [lo, hi].
+std::vector<float> sinusoid_rows(int lo, int hi, int D) {
+    std::vector<float> pe(static_cast<size_t>(hi - lo + 1) * D);
+    const float k = static_cast<float>(-(std::log(10000.0) / D));
+    for (int r = lo; r <= hi; ++r) {
+        float* row = &pe[static_cast<size_t>(r - lo) * D];
+        for (int i = 0; i < D; i += 2) {
+            const float div = std::exp(static_cast<float>(i) * k);
+            const float ang = static_cast<float>(r) * div;
+            row[i] = std::sin(ang);
+            row[i + 1] = std::cos(ang);
+        }
+    }
+    return pe;
+}
+
+ud_status load_weights_impl(ud_engine* e, const ud_weight* table, int n) {
+    WeightTable t;
+    for (int i = 0; i < n; ++i) {
+        if (!table[i].name) return fail(UD_ERR_WEIGHTS, "weight without a name");
+        t.by_name[table[i].name] = &table[i];
+    }
+    const ud_config& c = e->cfg;
+    const int D = e->D, F = e->F, H = e->H, DK = D / H, C = e->C, L = e->L;
+    Staging stg;
+    stg.cap = std::max<size_t>({static_cast<size_t>(3) * D * D, static_cast<size_t>(F) * D,
+                                static_cast<size_t>(D) * C * e->F3, static_cast<size_t>(2) * D * D});
+    UD_TRY(dalloc(e, &stg.p, stg.cap));
+    const float* p = nullptr;
+    // subsampling
+    if (c.sub_channels) {
+        const std::string s = "encoder.pre_encode.";
+        UD_TRY(need(t, s + "conv.0.weight", {C, 1, 3, 3}, &p)); UD_TRY(upload_f32(e, p, C * 9, &e->c0_w));
+        UD_TRY(need(t, s + "conv.0.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c0_b));
+        UD_TRY(need(t, s + "conv.2.weight", {C, 1, 3, 3}, &p)); UD_TRY(upload_f32(e, p, C * 9, &e->c2_w));
+        UD_TRY(need(t, s + "conv.2.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c2_b));
+        UD_TRY(need(t, s + "conv.3.weight", {C, C, 1, 1}, &p)); UD_TRY(upload_gemm(e, stg, {p}, {C}, C, e->c3));
+        UD_TRY(need(t, s + "conv.3.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c3_b));
+        UD_TRY(need(t, s + "conv.5.weight", {C, 1, 3, 3}, &p)); UD_TRY(upload_f32(e, p, C * 9, &e->c5_w));
+        UD_TRY(need(t, s + "conv.5.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c5_b));
+        UD_TRY(need(t, s + "conv.6.weight", {C, C, 1, 1}, &p)); UD_TRY(upload_gemm(e, stg, {p}, {C}, C, e->c6));
+        UD_TRY(need(t, s + "conv.6.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c6_b));
+        // pre_encode.out: checkpoint columns are c*F3 + f (channel-major flatten); the engine's activations are
+        // channel-last, so permute to f*C + c (FastConformer.swift:78-94 does the same).
+        const int F3 = e->F3;
+        UD_TRY(need(t, s + "out.weight", {D, C * F3}, &p));
+        std::vector<float> perm(static_cast<size_t>(D) * C * F3);
+        for (int o = 0; o < D; ++o)
+            for (int ch = 0; ch < C; ++ch)
+                for (int f = 0; f < F3; ++f)
+                    perm[static_cast<size_t>(o) * C * F3 + f * C + ch] = p[static_cast<size_t>(o) * C * F3 + ch * F3 + f];
+        UD_TRY(upload_gemm(e, stg, {perm.data()}, {D}, C * F3, e->sub_out));
+        UD_TRY(need(t, s + "out.bias", {D}, &p)); UD_TRY(upload_f32(e, p, D, &e->out_b));
+    }
+    // layers
+    const int tmax = e->tmax;
+    const int n_rel = L + 2 * tmax - 1;
+    std::vector<float> pe = sinusoid_rows(-(tmax - 1), L + tmax - 1, D);
+    float *pe_d = nullptr, *ptab_f = nullptr;
+    UD_TRY(dalloc(e, &pe_d, pe.size()));
+    UD_TRY(dalloc(e, &ptab_f, pe.size()));
+    UD_CK(cudaMemcpy(pe_d, pe.data(), pe.size() * sizeof(float), cudaMemcpyHostToDevice));
+    e->layers.assign(c.n_layers, LayerW{});
+    for (int l = 0; l < c.n_layers; ++l) {
+        LayerW& w = e->layers[l];
+        const std::string s = "encoder.layers." + std::to_string(l) + ".";
+        auto vec = [&](const std::string& nm, int len, float** dst) -> ud_status {
+            const float* q;
+            UD_TRY(need(t, s + nm, {len}, &q));
+            return upload_f32(e, q, len, dst);
+        };
+        UD_TRY(vec("norm_feed_forward1.weight", D, &w.ln_ff1_g)); UD_TRY(vec("norm_feed_forward1.bias", D, &w.ln_ff1_b));
+        UD_TRY(vec("norm_self_att.weight", D, &w.ln_att_g)); UD_TRY(vec("norm_self_att.bias", D, &w.ln_att_b));
+        UD_TRY(vec("norm_conv.weight", D, &w.ln_conv_g)); UD_TRY(vec("norm_conv.bias", D, &w.ln_conv_b));
+        UD_TRY(vec("conv.batch_norm.weight", D, &w.ln_cbn_g)); UD_TRY(vec("conv.batch_norm.bias", D, &w.ln_cbn_b));
+        UD_TRY(vec("norm_feed_forward2.weight", D, &w.ln_ff2_g)); UD_TRY(vec("norm_feed_forward2.bias", D, &w.ln_ff2_b));
+        UD_TRY(vec("norm_out.weight", D, &w.ln_out_g)); UD_TRY(vec("norm_out.bias", D, &w.ln_out_b));
+        const float *a, *b2, *c3;
+        UD_TRY(need(t, s + "feed_forward1.linear1.weight", {F, D}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {F}, D, w.ff1_w1));
+        UD_TRY(need(t, s + "feed_forward1.linear2.weight", {D, F}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {D}, F, w.ff1_w2));
+        UD_TRY(need(t, s + "feed_forward2.linear1.weight", {F, D}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {F}, D, w.ff2_w1));
+        UD_TRY(need(t, s + "feed_forward2.linear2.weight", {D, F}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {D}, F, w.ff2_w2));
+        UD_TRY(need(t, s + "self_attn.linear_q.weight", {D, D}, &a));
+        UD_TRY(need(t, s + "self_attn.linear_k.weight", {D, D}, &b2));
+        UD_TRY(need(t, s + "self_attn.linear_v.weight", {D, D}, &c3));
+        UD_TRY(upload_gemm(e, stg, {a, b2, c3}, {D, D, D}, D, w.wqkv));
+        UD_TRY(need(t, s + "self_attn.linear_out.weight", {D, D}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {D}, D, w.wo));
+        UD_TRY(need(t, s + "conv.pointwise_conv1.weight", {2 * D, D, 1}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {2 * D}, D, w.pw1));
+        UD_TRY(need(t, s + "conv.pointwise_conv2.weight", {D, D, 1}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {D}, D, w.pw2));
+        UD_TRY(need(t, s + "conv.depthwise_conv.weight", {D, 1, e->KC}, &a)); UD_TRY(upload_f32(e, a, D * e->KC, &w.dw));
+        UD_TRY(need(t, s + "self_attn.pos_bias_u", {H, DK}, &a)); UD_TRY(upload_f32(e, a, D, &w.pos_u));
+        UD_TRY(need(t, s + "self_attn.pos_bias_v", {H, DK}, &a)); UD_TRY(upload_f32(e, a, D, &w.pos_v));
+        // Projected position table P = sinusoid(rel) . W_pos^T in fp32, stored in the engine dtype.
+        UD_TRY(need(t, s + "self_attn.linear_pos.weight", {D, D}, &a));
+        UD_CK(cudaMemcpy(stg.p, a, sizeof(float) * D * D, cudaMemcpyHostToDevice));
+        GemmEpilogue gp;
+        gp.out = ptab_f;
+        gp.ldo = D;
+        gemm_simt<float, float>(pe_d, D, stg.p, n_rel, D, D, gp, e->stream);
+        UD_TRY(dalloc_bytes(e, &w.ptab, static_cast<size_t>(n_rel) * D * e->esz));
+        if (e->bf) f32_to_bf16(ptab_f, static_cast<bf16*>(w.ptab), static_cast<size_t>(n_rel) * D, e->stream);
+        else UD_CK(cudaMemcpyAsync(w.ptab, ptab_f, sizeof(float) * n_rel * D, cudaMemcpyDeviceToDevice, e->stream));
+        UD_CK(cudaStreamSynchronize(e->stream));
+    }
+    // joint + RNN-T
+    if (c.joint_dim) {
+        const int J = c.joint_dim, V = c.vocab, Hp = c.pred_hidden;
+        UD_TRY(need(t, "joint.enc.weight", {J, D}, &p)); UD_TRY(upload_gemm(e, stg, {p}, {J}, D, e->jenc));
+        UD_TRY(need(t, "joint.enc.bias", {J}, &p)); UD_TRY(upload_f32(e, p, J, &e->jenc_b));
+        RnntWeights& r = e->rw;
+        float* q;
+        UD_TRY(need(t, "decoder.prediction.embed.weight", {V, Hp}, &p)); UD_TRY(upload_f32(e, p, static_cast<size_t>(V) * Hp, &q)); r.embed = q;
+        for (int l = 0; l < c.pred_layers; ++l) {
+            const std::string s = "decoder.prediction.dec_rnn.lstm.";
+            const std::string sl = std::to_string(l);
+            UD_TRY(need(t, s + "weight_ih_l" + sl, {4 * Hp, Hp}, &p)); UD_TRY(upload_f32(e, p, static_cast<size_t>(4) * Hp * Hp, &q)); r.w_ih[l] = q;
+            UD_TRY(need(t, s + "weight_hh_l" + sl, {4 * Hp, Hp}, &p)); UD_TRY(upload_f32(e, p, static_cast<size_t>(4) * Hp * Hp, &q)); r.w_hh[l] = q;
+            const float *bi, *bh;
+            UD_TRY(need(t, s + "bias_ih_l" + sl, {4 * Hp}, &bi));
+            UD_TRY(need(t, s + "bias_hh_l" + sl, {4 * Hp}, &bh));
+            std::vector<float> bsum(4 * Hp);
+            for (int i = 0; i < 4 * Hp; ++i) bsum[i] = bi[i] + bh[i];
+            UD_TRY(upload_f32(e, bsum.data(), bsum.size(), &q)); r.bias[l] = q;
+        }
+        UD_TRY(need(t, "joint.pred.weight", {J, Hp}, &p)); UD_TRY(upload_f32(e, p, static_cast<size_t>(J) * Hp, &q)); r.pred_w = q;
+        UD_TRY(need(t, "joint.pred.bias", {J}, &p)); UD_TRY(upload_f32(e, p, J, &q)); r.pred_b = q;
+        UD_TRY(need(t, "joint.joint_net.2.weight", {V, J}, &p)); UD_TRY(upload_f32(e, p, static_cast<size_t>(V) * J, &q)); r.out_w = q;
+        UD_TRY(need(t, "joint.joint_net.2.bias", {V}, &p)); UD_TRY(upload_f32(e, p, V, &q)); r.out_b = q;
+        r.layers = c.pred_layers;
+        r.Hp = Hp;
+        r.J = J;
+        r.V = V;
+        r.max_symbols = c.max_symbols;
+    }
+    UD_CK(cudaStreamSynchronize(e->stream));
+    UD_CK(cudaGetLastError());
+    e->loaded = true;
+    return UD_OK;
+}
+
+ud_status reset_slot_device(ud_engine* e, int slot) {
+    e->slots_h[0] = slot;
+    UD_CK(cudaMemcpyAsync(e->slots_d, e->slots_h, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    {
+        Launch L_(e, UD_KIND_CACHE);
+        if (e->bf) conv_slot_zero<bf16>(e->slots_d, 1, e->cg, e->stream);
+        else conv_slot_zero<float>(e->slots_d, 1, e->cg, e->stream);
+    }
+    if (e->cfg.joint_dim && e->rs.h) {
+        Launch L_(e, UD_KIND_RNNT);
+        rnnt_reset(e->rs, e->slots_d, 1, e->rw, e->stream);
+    }
+    UD_CK(cudaStreamSynchronize(e->stream));
+    return UD_OK;
+}
+
+// ---------------------------------------------------------------- safetensors
+struct StEntry {
+    std::string name, dtype;
+    std::vector<int64_t> shape;
+    uint64_t begin = 0, end = 0;
+};
+
+bool parse_safetensors_header(const std::string& js, std::vector<StEntry>& out) {
+    size_t i = 0;
+    auto ws = [&] { while (i < js.size() && (js[i] == ' ' || js[i] == '\n' || js[i] == '\r' || js[i] == '\t')) ++i; };
+    auto str = [&](std::string& s) -> bool {
+        ws();
+        if (i >= js.size() || js[i] != '"') return false;
+        ++i;
+        s.clear();
+        while (i < js.size() && js[i] != '"') {
+            if (js[i] == '\\' && i + 1 < js.size()) ++i;
+            s += js[i++];
+        }
+        if (i >= js.size()) return false;
+        ++i;
+        return true;
+    };
+    auto num = [&](int64_t& v) -> bool {
+        ws();
+        size_t st = i;
+        while (i < js.size() && (isdigit(static_cast<unsigned char>(js[i])) || js[i] == '-')) ++i;
+        if (st == i) return false;
+        v = std::stoll(js.substr(st, i - st));
+        return true;
+    };
+    auto skip_value = [&]() -> bool {
+        ws();
+        int depth = 0;
+        bool in_str = false;
+        for (; i < js.size(); ++i) {
+            const char ch = js[i];
+            if (in_str) {
+                if (ch == '\\') ++i;
+                else if (ch == '"') in_str = false;
+                continue;
+            }
+            if (ch == '"') in_str = true;
+            else if (ch == '{' || ch == '[') ++depth;
+            else if (ch == '}' || ch == ']') {
+                if (depth == 0) return true;
+                if (--depth == 0) { ++i; return true; }
+            } else if (ch == ',' && depth == 0) return true;
+        }
+        return false;
+    };
+    ws();
+    if (i >= js.size() || js[i] != '{') return false;
+    ++i;
+    while (true) {
+        ws();
+        if (i < js.size() && js[i] == '}') return true;
+        StEntry e;
+        if (!str(e.name)) return false;
+        ws();
+        if (i >= js.size() || js[i] != ':') return false;
+        ++i;
+        ws();
+        if (e.name == "__metadata__") {
+            if (!skip_value()) return false;
+        } else {
+            if (i >= js.size() || js[i] != '{') return false;
+            ++i;
+            while (true) {
+                ws();
+                if (js[i] == '}') { ++i; break; }
+                std::string key;
+                if (!str(key)) return false;
+                ws();
+                if (js[i] != ':') return false;
+                ++i;
+                if (key == "dtype") {
+                    if (!str(e.dtype)) return false;
+                } else if (key == "shape" || key == "data_offsets") {
+                    ws();
+                    if (js[i] != '[') return false;
+                    ++i;
+                    std::vector<int64_t> v;
+                    while (true) {
+                        ws();
+                        if (js[i] == ']') { ++i; break; }
+                        int64_t x;
+                        if (!num(x)) return false;
+                        v.push_back(x);
+                        ws();
+                        if (js[i] == ',') ++i;
+                    }
+                    if (key == "shape") e.shape = v;
+                    else if (v.size() == 2) { e.begin = v[0]; e.end = v[1]; }
+                } else if (!skip_value()) return false;
+                ws();
+                if (js[i] == ',') ++i;
+            }
+            out.push_back(e);
+        }
+        ws();
+        if (i < js.size() && js[i] == ',') ++i;
+    }
+}
+
+float half_to_float(uint16_t h) {
+    const uint32_t sign = (h >> 15) & 1, exp = (h >> 10) & 0x1f, man = h & 0x3ff;
+    float v;
+    if (exp == 0) v = std::ldexp(static_cast<float>(man), -24);
+    else if (exp == 31) v = man ? NAN : INFINITY;
+    else v = std::ldexp(static_cast<float>(man | 0x400), static_cast<int>(exp) - 25);
+    return sign ? -v : v;
+}
+
+}  // namespace
+
+// ================================================================= C ABI
+extern "C" {
+
+void ud_config_default(ud_config* c) {
+    if (!c) return;
+    c->n_layers = 24;
+    c->d_model = 1024;
+    c->n_heads = 8;
+    c->ff_dim = 4096;
+    c->conv_kernel = 9;
+    c->left_context = 70;
+    c->sub_channels = 256;
+    c->mel_bins = 128;
+    c->joint_dim = 640;
+    c->vocab = 1025;
+    c->pred_layers = 1;
+    c->pred_hidden = 640;
+    c->max_symbols = 10;
+    c->dtype = UD_DTYPE_BF16;
+    c->max_streams = 64;
+    c->max_batch = 64;
+    c->max_chunk_frames = 16;
+    c->page_frames = 16;
+    c->n_pages = 0;
+}
+
+const char* ud_status_string(ud_status s) {
+    switch (s) {
+        case UD_OK: return "ok";
+        case UD_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case UD_ERR_CUDA: return "CUDA error";
+        case UD_ERR_OUT_OF_MEMORY: return "out of memory";
+        case UD_ERR_NO_STREAM: return "no such stream";
+        case UD_ERR_POOL_EXHAUSTED: return "pool exhausted";
+        case UD_ERR_WEIGHTS: return "weights error";
+        case UD_ERR_NOT_READY: return "not ready";
+        case UD_ERR_DEVICE_TIMEOUT: return "device wait expired";
+        case UD_ERR_IO: return "I/O error";
+        case UD_ERR_UNSUPPORTED: return "unsupported";
+    }
+    return "unknown";
+}
+
+size_t ud_last_error(char* buf, size_t len) {
+    if (buf && len) {
+        const size_t n = std::min(len - 1, g_last_error.size());
+        std::memcpy(buf, g_last_error.data(), n);
+        buf[n] = 0;
+    }
+    return g_last_error.size();
+}
+
+ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
+    g_last_error.clear();
+    if (!cfg || !out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    const ud_config& c = *cfg;
+    if (c.n_heads <= 0 || c.d_model != c.n_heads * 128 ||
+        (c.n_heads != 1 && c.n_heads != 2 && c.n_heads != 4 && c.n_heads != 6 && c.n_heads != 8))
+        return fail(UD_ERR_UNSUPPORTED, "this build needs 128-wide heads and d_model in {128,256,512,768,1024}");
+    if (c.conv_kernel != 9) return fail(UD_ERR_UNSUPPORTED, "this build supports conv_kernel 9");
+    if (c.n_layers < 0 || c.ff_dim <= 0 || c.ff_dim % 128 != 0) return fail(UD_ERR_INVALID_ARGUMENT, "bad layer sizes");
+    if (c.left_context < 1 || c.max_chunk_frames < 1 || c.max_chunk_frames > 32)
+        return fail(UD_ERR_INVALID_ARGUMENT, "left_context / max_chunk_frames out of range");
+    if (c.page_frames < 1 || c.left_context + c.max_chunk_frames + c.page_frames - 1 > kPageSlots * c.page_frames)
+        return fail(UD_ERR_INVALID_ARGUMENT, "page ring too small for left_context + max_chunk_frames");
+    if (c.dtype != UD_DTYPE_F32 && c.dtype != UD_DTYPE_BF16) return fail(UD_ERR_INVALID_ARGUMENT, "bad dtype");
+    if (c.max_streams < 1 || c.max_batch < 1 || c.max_batch > c.max_streams)
+        return fail(UD_ERR_INVALID_ARGUMENT, "max_streams / max_batch out of range");
+    if (c.sub_channels && (c.sub_channels % 128 != 0 || c.mel_bins < 1))
+        return fail(UD_ERR_UNSUPPORTED, "sub_channels must be a multiple of 128");
+    if (c.joint_dim && (c.joint_dim % 128 != 0 || c.pred_hidden % 4 != 0 || c.pred_layers < 1 || c.pred_layers > 4 ||
+                        c.vocab < 2 || c.max_symbols < 1))
+        return fail(UD_ERR_UNSUPPORTED, "RNN-T head sizes not supported");
+
+    if (cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(UD_ERR_CUDA, "cudaSetDevice failed (no CUDA device?)");
+    }
+    cudaDeviceProp prop;
+    UD_CK(cudaGetDeviceProperties(&prop, device));
+    if (c.dtype == UD_DTYPE_BF16 && prop.major != 10)
+        return fail(UD_ERR_UNSUPPORTED, "the bf16 engine needs an sm_100 (B200) device");
+
+    ud_engine* e = new ud_engine();
+    e->cfg = c;
+    e->device = device;
+    e->num_sms = prop.multiProcessorCount;
+    e->bf = c.dtype == UD_DTYPE_BF16;
+    e->esz = e->bf ? 2 : 4;
+    e->tmax = c.max_chunk_frames;
+    e->L = c.left_context;
+    e->D = c.d_model;
+    e->H = c.n_heads;
+    e->F = c.ff_dim;
+    e->KC = c.conv_kernel;
+    e->C = c.sub_channels;
+    e->J = c.joint_dim;
+    e->F1 = nxt(c.mel_bins);
+    e->F2 = nxt(e->F1);
+    e->F3 = nxt(e->F2);
+    auto cleanup = [&](ud_status s) {
+        std::string keep = g_last_error;
+        ud_shutdown(e);
+        g_last_error = keep;
+        return s;
+    };
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return cleanup(fail(UD_ERR_CUDA, "cudaStreamCreate failed"));
+
+    const bool sub = c.sub_channels > 0;
+    if (sub) {
+        int r = 1;
+        while (sub_len(r + 1) <= e->tmax + 2) ++r;
+        e->max_rows_in = r;
+    } else {
+        e->max_rows_in = e->tmax;
+    }
+    e->in_width = sub ? c.mel_bins : e->D;
+    e->out_width = c.joint_dim ? c.joint_dim : e->D;
+    e->Mcap = c.max_batch * e->tmax;
+    const size_t Mc = e->Mcap, D = e->D, es = e->esz, B = c.max_batch;
+
+    // caches
+    const int PF = c.page_frames;
+    const int per_stream = (e->L + e->tmax + PF - 1 + PF - 1) / PF;
+    const int n_pages = c.n_pages > 0 ? c.n_pages : c.max_streams * per_stream;
+    ud_status s;
+    CacheGeom& cg = e->cg;
+    cg.n_layers = c.n_layers;
+    cg.n_pages = n_pages;
+    cg.page_frames = PF;
+    cg.D = e->D;
+    cg.L = e->L;
+    cg.conv_ring = c.conv_kernel - 1;
+    cg.max_streams = c.max_streams;
+    const size_t pool_bytes = static_cast<size_t>(std::max(c.n_layers, 1)) * n_pages * PF * D * es;
+    if ((s = dalloc_bytes(e, &cg.kpool, pool_bytes)) != UD_OK) return cleanup(s);
+    if ((s = dalloc_bytes(e, &cg.vpool, pool_bytes)) != UD_OK) return cleanup(s);
+    const size_t conv_bytes = static_cast<size_t>(std::max(c.n_layers, 1)) * c.max_streams * cg.conv_ring * D * es;
+    if ((s = dalloc_bytes(e, &cg.conv, conv_bytes)) != UD_OK) return cleanup(s);
+    if (cudaMemset(cg.conv, 0, conv_bytes) != cudaSuccess) return cleanup(fail(UD_ERR_CUDA, "cudaMemset failed"));
+    e->free_pages.reserve(n_pages);
+    for (int p = n_pages - 1; p >= 0; --p) e->free_pages.push_back(p);
+    e->slots.assign(c.max_streams, Slot{});
+    for (int i = c.max_streams - 1; i >= 0; --i) e->free_slots.push_back(i);
+
+    // workspace
+    if ((s = dalloc(e, &e->x, Mc * D)) != UD_OK) return cleanup(s);
+    if ((s = dalloc_bytes(e, &e->h, Mc * D * es)) != UD_OK) return cleanup(s);
+    if ((s = dalloc_bytes(e, &e->hid, Mc * e->F * es)) != UD_OK) return cleanup(s);
+    if ((s = dalloc_bytes(e, &e->qkv, Mc * 3 * D * es)) != UD_OK) return cleanup(s);
+    if ((s = dalloc_bytes(e, &e->att, Mc * D * es)) != UD_OK) return cleanup(s);
+    if ((s = dalloc_bytes(e, &e->pw, Mc * 2 * D * es)) != UD_OK) return cleanup(s);
+    if ((s = dalloc_bytes(e, &e->y, Mc * D * es)) != UD_OK) return cleanup(s);
+    if (c.joint_dim && (s = dalloc(e, &e->proj, Mc * c.joint_dim)) != UD_OK) return cleanup(s);
+    if (sub) {
+        const size_t T1 = nxt(e->max_rows_in), T2 = nxt(T1), T3 = nxt(T2), C = e->C;
+        if ((s = dalloc_bytes(e, &e->a1, B * T1 * e->F1 * C * es)) != UD_OK) return cleanup(s);
+        if ((s = dalloc_bytes(e, &e->a2, B * T2 * e->F2 * C * es)) != UD_OK) return cleanup(s);
+        if ((s = dalloc_bytes(e, &e->a3, B * T2 * e->F2 * C * es)) != UD_OK) return cleanup(s);
+        if ((s = dalloc_bytes(e, &e->a4, B * T3 * e->F3 * C * es)) != UD_OK) return cleanup(s);
+        if ((s = dalloc_bytes(e, &e->a5, B * T3 * e->F3 * C * es)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &e->subout, B * T3 * D)) != UD_OK) return cleanup(s);
+    }
+    const size_t in_elems = B * e->max_rows_in * e->in_width;
+    const size_t out_elems = B * e->tmax * e->out_width;
+    const size_t tok_elems = B * e->tmax * c.max_symbols;
+    if ((s = dalloc(e, &e->in_stage, in_elems)) != UD_OK) return cleanup(s);
+    if ((s = dalloc(e, &e->out_stage, out_elems)) != UD_OK) return cleanup(s);
+    if ((s = dalloc(e, &e->tok_dev, tok_elems)) != UD_OK) return cleanup(s);
+    if ((s = dalloc(e, &e->ntok_dev, B)) != UD_OK) return cleanup(s);
+    if ((s = halloc(e, &e->h_in, in_elems)) != UD_OK) return cleanup(s);
+    if ((s = halloc(e, &e->h_out, out_elems)) != UD_OK) return cleanup(s);
+    if ((s = halloc(e, &e->h_tok, tok_elems)) != UD_OK) return cleanup(s);
+    if ((s = halloc(e, &e->h_ntok, B)) != UD_OK) return cleanup(s);
+    const size_t meta_n = std::max<size_t>(B, c.max_streams);
+    for (int r = 0; r < ud_engine::kRing; ++r) {
+        if ((s = halloc(e, &e->meta_h[r], meta_n)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &e->meta_d[r], meta_n)) != UD_OK) return cleanup(s);
+        if (cudaEventCreateWithFlags(&e->meta_ev[r], cudaEventDisableTiming) != cudaSuccess)
+            return cleanup(fail(UD_ERR_CUDA, "cudaEventCreate failed"));
+    }
+    if ((s = halloc(e, &e->slots_h, meta_n)) != UD_OK) return cleanup(s);
+    if ((s = dalloc(e, &e->slots_d, meta_n)) != UD_OK) return cleanup(s);
+    if ((s = dalloc(e, &e->err_d, 1)) != UD_OK) return cleanup(s);
+    if ((s = halloc(e, &e->err_h, 1)) != UD_OK) return cleanup(s);
+    if (cudaMemset(e->err_d, 0, sizeof(int)) != cudaSuccess) return cleanup(fail(UD_ERR_CUDA, "cudaMemset failed"));
+    if (c.joint_dim) {
+        const size_t S = c.max_streams, Hp = c.pred_hidden, NLp = c.pred_layers;
+        RnntState& r = e->rs;
+        if ((s = dalloc(e, &r.h, S * NLp * Hp)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &r.c, S * NLp * Hp)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &r.pend_h, S * NLp * Hp)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &r.pend_c, S * NLp * Hp)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &r.pend_g, S * c.joint_dim)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &r.last_tok, S)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &r.pend_valid, S)) != UD_OK) return cleanup(s);
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(UD_ERR_CUDA, "device synchronize failed"));
+    *out = e;
+    return UD_OK;
+}
+
+ud_status ud_shutdown(ud_engine* e) {
+    if (!e) return UD_OK;
+    cudaSetDevice(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    for (void* p : e->allocs) cudaFree(p);
+    for (void* p : e->host_allocs) cudaFreeHost(p);
+    for (int r = 0; r < ud_engine::kRing; ++r)
+        if (e->meta_ev[r]) cudaEventDestroy(e->meta_ev[r]);
+    for (cudaEvent_t ev : e->prof_events) cudaEventDestroy(ev);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return UD_OK;
+}
+
+ud_status ud_load_weights(ud_engine* e, const ud_weight* table, int n) {
+    if (!e || !table || n <= 0) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (e->loaded) return fail(UD_ERR_INVALID_ARGUMENT, "weights already loaded");
+    UD_CK(cudaSetDevice(e->device));
+    return load_weights_impl(e, table, n);
+}
+
+ud_status ud_load_safetensors(ud_engine* e, const char* path) {
+    if (!e || !path) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(UD_ERR_IO, std::string("cannot open ") + path);
+    uint64_t hlen = 0;
+    if (std::fread(&hlen, 8, 1, f) != 1 || hlen > (1ull << 30)) {
+        std::fclose(f);
+        return fail(UD_ERR_IO, "bad safetensors header length");
+    }
+    std::string js(hlen, '\0');
+    if (std::fread(&js[0], 1, hlen, f) != hlen) {
+        std::fclose(f);
+        return fail(UD_ERR_IO, "short safetensors header");
+    }
+    std::vector<StEntry> ents;
+    if (!parse_safetensors_header(js, ents)) {
+        std::fclose(f);
+        return fail(UD_ERR_IO, "cannot parse safetensors header");
+    }
+    std::vector<std::vector<float>> data(ents.size());
+    std::vector<ud_weight> table(ents.size());
+    const uint64_t base = 8 + hlen;
+    for (size_t k = 0; k < ents.size(); ++k) {
+        const StEntry& en = ents[k];
+        int64_t count = 1;
+        for (int64_t d : en.shape) count *= d;
+        const int esz = en.dtype == "F32" ? 4 : (en.dtype == "F16" || en.dtype == "BF16") ? 2 : 0;
+        if (!esz || en.shape.size() > 4 || en.end - en.begin != static_cast<uint64_t>(count) * esz) {
+            std::fclose(f);
+            return fail(UD_ERR_IO, "unsupported tensor " + en.name + " (" + en.dtype + ")");
+        }
+        std::vector<uint8_t> raw(en.end - en.begin);
+        if (std::fseek(f, static_cast<long>(base + en.begin), SEEK_SET) != 0 ||
+            std::fread(raw.data(), 1, raw.size(), f) != raw.size()) {
+            std::fclose(f);
+            return fail(UD_ERR_IO, "short read of " + en.name);
+        }
+        data[k].resize(count);
+        for (int64_t i = 0; i < count; ++i) {
+            if (esz == 4) {
+                std::memcpy(&data[k][i], &raw[i * 4], 4);
+            } else {
+                uint16_t hv;
+                std::memcpy(&hv, &raw[i * 2], 2);
+                if (en.dtype == "F16") {
+                    data[k][i] = half_to_float(hv);
+                } else {
+                    const uint32_t bits = static_cast<uint32_t>(hv) << 16;
+                    std::memcpy(&data[k][i], &bits, 4);
+                }
+            }
+        }
+        table[k].name = ents[k].name.c_str();
+        table[k].data = data[k].data();
+        table[k].ndim = static_cast<int>(en.shape.size());
+        for (size_t d = 0; d < en.shape.size(); ++d) table[k].shape[d] = en.shape[d];
+    }
+    std::fclose(f);
+    return ud_load_weights(e, table.data(), static_cast<int>(table.size()));
+}
+
+ud_status ud_stream_open(ud_engine* e, int lookahead, ud_stream_id* out) {
+    if (!e || !out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (lookahead < 0) return fail(UD_ERR_INVALID_ARGUMENT, "negative lookahead");
+    if (e->free_slots.empty()) return fail(UD_ERR_POOL_EXHAUSTED, "no free stream slot");
+    UD_CK(cudaSetDevice(e->device));
+    const int id = e->free_slots.back();
+    Slot& s = e->slots[id];
+    s.reset();
+    s.lookahead = lookahead;
+    UD_TRY(reset_slot_device(e, id));
+    e->free_slots.pop_back();
+    s.open = true;
+    *out = id;
+    return UD_OK;
+}
+
+ud_status ud_stream_close(ud_engine* e, ud_stream_id id) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    if (id < 0 || id >= e->cfg.max_streams || !e->slots[id].open) return fail(UD_ERR_NO_STREAM, "unknown stream");
+    Slot& s = e->slots[id];
+    free_all_pages(e, s);
+    s.open = false;
+    e->free_slots.push_back(id);
+    return UD_OK;
+}
+
+ud_status ud_step_batch_device(ud_engine* e, int n, const ud_stream_id* ids, const float* mel_dev, int rows_stride,
+                               const int* n_rows, const int* valid_rows, const int* keep_all, float* proj_dev,
+                               int* frames_out, int32_t* tokens_dev, int* n_tokens_dev) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    if (tokens_dev && !n_tokens_dev) return fail(UD_ERR_INVALID_ARGUMENT, "n_tokens_dev is NULL");
+    return run_batch(e, n, ids, mel_dev, rows_stride, n_rows, valid_rows, keep_all, proj_dev, frames_out, tokens_dev,
+                     n_tokens_dev);
+}
+
+ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* const* mel, const int* n_rows,
+                        const int* valid_rows, const int* keep_all, float* proj_out, int* frames_out,
+                        int32_t* tokens_out, int* n_tokens_out) {
+    if (!e || !mel || !n_rows || !proj_out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (n < 1 || n > e->cfg.max_batch) return fail(UD_ERR_INVALID_ARGUMENT, "batch size out of range");
+    if (tokens_out && !n_tokens_out) return fail(UD_ERR_INVALID_ARGUMENT, "n_tokens_out is NULL");
+    UD_CK(cudaSetDevice(e->device));
+    int stride = 1;
+    for (int i = 0; i < n; ++i) {
+        if (!mel[i]) return fail(UD_ERR_INVALID_ARGUMENT, "NULL input rows");
+        if (n_rows[i] < 1 || n_rows[i] > e->max_rows_in)
+            return fail(UD_ERR_INVALID_ARGUMENT, "n_rows out of range");
+        stride = std::max(stride, n_rows[i]);
+    }
+    const int W = e->in_width;
+    // The pinned staging buffer may still be read by a previous asynchronous call.
+    UD_CK(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < n; ++i)
+        std::memcpy(e->h_in + static_cast<size_t>(i) * stride * W, mel[i], sizeof(float) * n_rows[i] * W);
+    UD_CK(cudaMemcpyAsync(e->in_stage, e->h_in, sizeof(float) * n * stride * W, cudaMemcpyHostToDevice, e->stream));
+    std::vector<int> frames(n);
+    UD_TRY(run_batch(e, n, ids, e->in_stage, stride, n_rows, valid_rows, keep_all, e->out_stage, frames.data(),
+                     tokens_out ? e->tok_dev : nullptr, e->ntok_dev));
+    const size_t out_n = static_cast<size_t>(n) * e->tmax * e->out_width;
+    UD_CK(cudaMemcpyAsync(e->h_out, e->out_stage, sizeof(float) * out_n, cudaMemcpyDeviceToHost, e->stream));
+    if (tokens_out) {
+        UD_CK(cudaMemcpyAsync(e->h_tok, e->tok_dev, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols,
+                              cudaMemcpyDeviceToHost, e->stream));
+        UD_CK(cudaMemcpyAsync(e->h_ntok, e->ntok_dev, sizeof(int) * n, cudaMemcpyDeviceToHost, e->stream));
+    }
+    UD_TRY(check_device_error(e));
+    std::memcpy(proj_out, e->h_out, sizeof(float) * out_n);
+    if (frames_out) std::memcpy(frames_out, frames.data(), sizeof(int) * n);
+    if (tokens_out) {
+        std::memcpy(tokens_out, e->h_tok, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols);
+        std::memcpy(n_tokens_out, e->h_ntok, sizeof(int) * n);
+    }
+    return UD_OK;
+}
+
+ud_status ud_stream_step(ud_engine* e, ud_stream_id id, const float* mel, int n_rows, int valid_rows, int keep_all,
+                         float* proj_out, int* frames_out) {
+    if (!e || !mel || !proj_out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    const float* ptrs[1] = {mel};
+    int fr = 0;
+    if (!e->loaded) return fail(UD_ERR_NOT_READY, "weights not loaded");
+    std::vector<float> tmp(static_cast<size_t>(e->tmax) * e->out_width);
+    UD_TRY(ud_step_batch(e, 1, &id, ptrs, &n_rows, &valid_rows, &keep_all, tmp.data(), &fr, nullptr, nullptr));
+    std::memcpy(proj_out, tmp.data(), sizeof(float) * fr * e->out_width);
+    if (frames_out) *frames_out = fr;
+    return UD_OK;
+}
+
+ud_status ud_rnnt_decode(ud_engine* e, ud_stream_id id, const float* f, int frames, int32_t* tokens_out,
+                         int* n_tokens_out) {
+    if (!e || !f || !tokens_out || !n_tokens_out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (!e->loaded) return fail(UD_ERR_NOT_READY, "weights not loaded");
+    if (!e->cfg.joint_dim) return fail(UD_ERR_INVALID_ARGUMENT, "no RNN-T head in this configuration");
+    UD_TRY(check_ids(e, 1, &id));
+    if (frames < 0 || frames > e->Mcap) return fail(UD_ERR_INVALID_ARGUMENT, "frames out of range");
+    *n_tokens_out = 0;
+    if (frames == 0) return UD_OK;
+    UD_CK(cudaSetDevice(e->device));
+    UD_CK(cudaStreamSynchronize(e->stream));
+    int mi = 0;
+    BatchEntry* mh = next_meta_host(e, &mi);
+    std::memset(&mh[0], 0, sizeof(BatchEntry));
+    mh[0].slot = id;
+    mh[0].keep = frames;
+    mh[0].T = frames;
+    UD_TRY(upload_meta(e, mi, 1));
+    UD_CK(cudaMemcpyAsync(e->proj, f, sizeof(float) * frames * e->J, cudaMemcpyHostToDevice, e->stream));
+    // The token buffer holds max_batch * tmax * max_symbols ids; one stream may use all of it.
+    const int cap = e->cfg.max_batch * e->tmax * e->cfg.max_symbols;
+    if (frames * e->cfg.max_symbols > cap) return fail(UD_ERR_INVALID_ARGUMENT, "too many frames for one call");
+    {
+        Launch L_(e, UD_KIND_RNNT);
+        rnnt_greedy(e->rw, e->rs, e->proj, e->J, e->meta_d[mi], 1, e->tok_dev, cap, e->ntok_dev, e->stream);
+    }
+    UD_CK(cudaGetLastError());
+    UD_CK(cudaMemcpyAsync(e->h_ntok, e->ntok_dev, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    UD_CK(cudaStreamSynchronize(e->stream));
+    const int nt = e->h_ntok[0];
+    UD_CK(cudaMemcpy(tokens_out, e->tok_dev, sizeof(int32_t) * nt, cudaMemcpyDeviceToHost));
+    *n_tokens_out = nt;
+    return UD_OK;
+}
+
+ud_status ud_cache_append(ud_engine* e, int n, const ud_stream_id* ids, int k, const void* kv_rows,
+                          const void* conv_rows) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_TRY(check_ids(e, n, ids));
+    if (k < 1 || k > e->tmax) return fail(UD_ERR_INVALID_ARGUMENT, "k out of range");
+    UD_CK(cudaSetDevice(e->device));
+    int mi = 0;
+    BatchEntry* mh = next_meta_host(e, &mi);
+    std::vector<std::pair<Slot*, int>> undo;
+    for (int i = 0; i < n; ++i) {
+        Slot& s = e->slots[ids[i]];
+        if (kv_rows) {
+            ud_status st = map_pages(e, s, k, undo);
+            if (st != UD_OK) {
+                undo_pages(e, undo);
+                return st;
+            }
+        }
+        std::memset(&mh[i], 0, sizeof(BatchEntry));
+        mh[i].slot = ids[i];
+        mh[i].head = s.head;
+        mh[i].cache_len = s.cache_len;
+        mh[i].T = k;
+        std::memcpy(mh[i].pages, s.pages, sizeof(mh[i].pages));
+    }
+    UD_TRY(upload_meta(e, mi, n));
+    {
+    Launch L_(e, UD_KIND_CACHE);
+    if (e->bf)
+        cache_append<bf16>(static_cast<const bf16*>(kv_rows), static_cast<const bf16*>(conv_rows), k, e->meta_d[mi], n,
+                           e->cg, e->err_d, e->stream);
+    else
+        cache_append<float>(static_cast<const float*>(kv_rows), static_cast<const float*>(conv_rows), k, e->meta_d[mi],
+                            n, e->cg, e->err_d, e->stream);
+    }
+    UD_CK(cudaGetLastError());
+    return UD_OK;
+}
+
+ud_status ud_cache_roll(ud_engine* e, int n, const ud_stream_id* ids, int k) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_TRY(check_ids(e, n, ids));
+    if (k < 1 || k > e->tmax) return fail(UD_ERR_INVALID_ARGUMENT, "k out of range");
+    for (int i = 0; i < n; ++i) {
+        Slot& s = e->slots[ids[i]];
+        s.head += k;
+        s.cache_len = std::min(s.cache_len + k, e->L);
+        free_out_of_window(e, s);
+    }
+    return UD_OK;
+}
+
+ud_status ud_cache_gather(ud_engine* e, int n, const ud_stream_id* ids, void* kv_out, void* conv_out) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_TRY(check_ids(e, n, ids));
+    UD_CK(cudaSetDevice(e->device));
+    int mi = 0;
+    BatchEntry* mh = next_meta_host(e, &mi);
+    for (int i = 0; i < n; ++i) {
+        const Slot& s = e->slots[ids[i]];
+        std::memset(&mh[i], 0, sizeof(BatchEntry));
+        mh[i].slot = ids[i];
+        mh[i].head = s.head;
+        mh[i].cache_len = s.cache_len;
+        std::memcpy(mh[i].pages, s.pages, sizeof(mh[i].pages));
+    }
+    UD_TRY(upload_meta(e, mi, n));
+    {
+    Launch L_(e, UD_KIND_CACHE);
+    if (e->bf)
+        cache_gather<bf16>(static_cast<bf16*>(kv_out), static_cast<bf16*>(conv_out), e->meta_d[mi], n, e->cg, e->err_d,
+                           e->stream);
+    else
+        cache_gather<float>(static_cast<float*>(kv_out), static_cast<float*>(conv_out), e->meta_d[mi], n, e->cg,
+                            e->err_d, e->stream);
+    }
+    UD_CK(cudaGetLastError());
+    return UD_OK;
+}
+
+ud_status ud_cache_evict(ud_engine* e, int n, const ud_stream_id* ids) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_TRY(check_ids(e, n, ids));
+    UD_CK(cudaSetDevice(e->device));
+    for (int i = 0; i < n; ++i) {
+        Slot& s = e->slots[ids[i]];
+        free_all_pages(e, s);
+        const int la = s.lookahead;
+        s.reset();
+        s.lookahead = la;
+        e->slots_h[i] = ids[i];
+    }
+    UD_CK(cudaStreamSynchronize(e->stream));
+    UD_CK(cudaMemcpyAsync(e->slots_d, e->slots_h, sizeof(int) * n, cudaMemcpyHostToDevice, e->stream));
+    {
+        Launch L_(e, UD_KIND_CACHE);
+        if (e->bf) conv_slot_zero<bf16>(e->slots_d, n, e->cg, e->stream);
+        else conv_slot_zero<float>(e->slots_d, n, e->cg, e->stream);
+    }
+    if (e->cfg.joint_dim && e->rs.h) {
+        Launch L_(e, UD_KIND_RNNT);
+        rnnt_reset(e->rs, e->slots_d, n, e->rw, e->stream);
+    }
+    UD_CK(cudaGetLastError());
+    return UD_OK;
+}
+
+ud_status ud_cache_read(ud_engine* e, ud_stream_id id, int layer, int kind, void* host_out) {
+    if (!e || !host_out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    UD_TRY(check_ids(e, 1, &id));
+    if (layer < 0 || layer >= e->cfg.n_layers || kind < 0 || kind > 2)
+        return fail(UD_ERR_INVALID_ARGUMENT, "layer or kind out of range");
+    UD_CK(cudaSetDevice(e->device));
+    const size_t kv = static_cast<size_t>(e->cfg.n_layers) * 2 * e->L * e->D * e->esz;
+    const size_t cv = static_cast<size_t>(e->cfg.n_layers) * e->cg.conv_ring * e->D * e->esz;
+    if (!e->gather_scratch) UD_TRY(dalloc_bytes(e, &e->gather_scratch, kv + cv));
+    uint8_t* g = static_cast<uint8_t*>(e->gather_scratch);
+    UD_TRY(ud_cache_gather(e, 1, &id, g, g + kv));
+    UD_TRY(check_device_error(e));
+    const size_t row = static_cast<size_t>(e->D) * e->esz;
+    if (kind < 2)
+        UD_CK(cudaMemcpy(host_out, g + (static_cast<size_t>(layer) * 2 + kind) * e->L * row, e->L * row,
+                         cudaMemcpyDeviceToHost));
+    else
+        UD_CK(cudaMemcpy(host_out, g + kv + static_cast<size_t>(layer) * e->cg.conv_ring * row, e->cg.conv_ring * row,
+                         cudaMemcpyDeviceToHost));
+    return UD_OK;
+}
+
+ud_status ud_stream_info(ud_engine* e, ud_stream_id id, int* cache_len, int* head, int* step) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_TRY(check_ids(e, 1, &id));
+    const Slot& s = e->slots[id];
+    if (cache_len) *cache_len = s.cache_len;
+    if (head) *head = s.head;
+    if (step) *step = s.step;
+    return UD_OK;
+}
+
+ud_status ud_get_cuda_stream(ud_engine* e, void** stream_out) {
+    if (!e || !stream_out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    *stream_out = e->stream;
+    return UD_OK;
+}
+
+ud_status ud_pool_info(ud_engine* e, int* free_pages, int* total_pages, int* elem_bytes) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    if (free_pages) *free_pages = static_cast<int>(e->free_pages.size());
+    if (total_pages) *total_pages = e->cg.n_pages;
+    if (elem_bytes) *elem_bytes = e->esz;
+    return UD_OK;
+}
+
+ud_status ud_synchronize(ud_engine* e) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_CK(cudaSetDevice(e->device));
+    UD_CK(cudaGetLastError());
+    return check_device_error(e);
+}
+
+ud_status ud_launch_count(ud_engine* e, int64_t* out) {
+    if (!e || !out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = e->launches;
+    return UD_OK;
+}
+
+ud_status ud_debug_gemm(ud_engine* e, const void* A, const void* W, int M, int N, int K, const float* bias, int act,
+                        float out_scale, const float* residual, float res_scale, void* Cout, int out_bf16) {
+    if (!e || !A || !W || !Cout || M < 1 || N < 1 || K < 1) return fail(UD_ERR_INVALID_ARGUMENT, "bad argument");
+    if (act < 0 || act > 2) return fail(UD_ERR_INVALID_ARGUMENT, "bad activation");
+    UD_CK(cudaSetDevice(e->device));
+    WeightMat wm;
+    wm.p = const_cast<void*>(W);
+    wm.N = N;
+    wm.K = K;
+    if (e->bf && tc_ok(N, K)) {
+        if (!make_tma_bf16(wm.tma128, W, N, K, K, 128)) return fail(UD_ERR_CUDA, "tensor map failed");
+        wm.has_tma = true;
+        if (N % 256 == 0 && make_tma_bf16(wm.tma256, W, N, K, K, 256)) wm.has256 = true;
+    }
+    GemmEpilogue g;
+    g.bias = bias;
+    g.act = act;
+    g.out_scale = out_scale;
+    g.residual = residual;
+    g.ldr = N;
+    g.res_scale = res_scale;
+    g.out = Cout;
+    g.ldo = N;
+    g.out_bf16 = out_bf16;
+    UD_TRY(gemm(e, A, K, M, wm, g));
+    UD_CK(cudaGetLastError());
+    return check_device_error(e);
+}
+
+ud_status ud_debug_wait_probe(ud_engine* e, uint64_t limit_ns) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    if (limit_ns > 10000000000ull) return fail(UD_ERR_INVALID_ARGUMENT, "limit above 10 s");
+    UD_CK(cudaSetDevice(e->device));
+    {
+        Launch L_(e, UD_KIND_OTHER);
+        test_wait_timeout(e->err_d, limit_ns, e->stream);
+    }
+    UD_CK(cudaGetLastError());
+    return check_device_error(e);
+}
+
+ud_status ud_profile_enable(ud_engine* e, int enable) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_CK(cudaSetDevice(e->device));
+    prof_flush(e);
+    e->prof = enable != 0;
+    for (int k = 0; k < UD_KIND_COUNT; ++k) {
+        e->prof_ms[k] = 0.0;
+        e->prof_n[k] = 0;
+    }
+    return UD_OK;
+}
+
+ud_status ud_profile_read(ud_engine* e, int kind, double* ms_total, int64_t* launches) {
+    if (!e || kind < 0 || kind >= UD_KIND_COUNT) return fail(UD_ERR_INVALID_ARGUMENT, "bad argument");
+    UD_CK(cudaSetDevice(e->device));
+    prof_flush(e);
+    if (ms_total) *ms_total = e->prof_ms[kind];
+    if (launches) *launches = e->prof_n[kind];
+    return UD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,147 @@
+// Launch interfaces of the libud kernels (host side). All kernels are sm_100a.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ud {
+
+using bf16 = __nv_bfloat16;
+
+enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_SILU = 2 };
+
+// C = out_scale * act(A . W^T + bias) + res_scale * R   (the contract of the reference's Step.gemm,
+// Sources/DictatorEngine/Core/Kernels.swift:79-113, minus alpha which Nemotron never sets).
+struct GemmEpilogue {
+    const float* bias = nullptr;     // [N] or null
+    int act = ACT_NONE;
+    float out_scale = 1.f;
+    const float* residual = nullptr; // fp32 [M, ldr] or null; may alias out (read before write, same thread)
+    int ldr = 0;
+    float res_scale = 1.f;
+    void* out = nullptr;             // fp32 or bf16 [M, ldo]
+    int ldo = 0;
+    int out_bf16 = 0;
+};
+
+// ---- tcgen05 GEMM (bf16 x bf16 -> fp32 in TMEM), A [M, K] row-major (lda), W [N, K] row-major.
+// Requirements: K % 64 == 0, N % 128 == 0, lda/ldw multiples of 8 elements, 16-byte aligned bases.
+struct TmaMatrix {
+    CUtensorMap map;
+    const void* base = nullptr;
+    int rows = 0, cols = 0, ld = 0, box_rows = 0;
+};
+bool make_tma_bf16(TmaMatrix& t, const void* base, int rows, int cols, int ld, int box_rows);
+int gemm_tc_pick_bn(int M, int N, int num_sms);
+void gemm_tc(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, int bn, const GemmEpilogue& epi,
+             int* dev_err, int num_sms, cudaStream_t s);
+
+// ---- SIMT GEMM for few rows (M small) and for the fp32 engine. TA/TW in {float, bf16}.
+template <typename TA, typename TW>
+void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s);
+
+// ---- LayerNorm over rows of width D (eps 1e-5). x fp32 [M, D] -> y (TO) [M, D].
+template <typename TO>
+void layer_norm(const float* x, const float* g, const float* b, TO* y, int M, int D, cudaStream_t s);
+// x <- LN1(x) (fp32, in place), y <- LN2(x) in TO: a layer's norm_out fused with the next layer's norm_ff1.
+template <typename TO>
+void layer_norm2(float* x, const float* g1, const float* b1, const float* g2, const float* b2, TO* y, int M, int D,
+                 cudaStream_t s);
+
+// ---- Per-stream step metadata, uploaded once per batched step.
+constexpr int kPageSlots = 8;     // page-table slots per stream (ring of pages)
+struct BatchEntry {
+    int slot;        // stream slot (index into per-slot arrays: conv cache, decoder state)
+    int row_off;     // first row of this stream's frames in the packed [M, D] activations
+    int T;           // frames this step
+    int valid_t;     // valid frames (<= T)
+    int cache_len;   // cached frames before this step (<= L)
+    int head;        // absolute frame index of the first new frame (= frames appended so far)
+    int drop;        // subsampled frames dropped from the front (0 first step, 2 later)
+    int valid_mel;   // valid mel rows
+    int n_rows;      // mel rows
+    int keep;        // frames kept for the joint / decoder
+    int tok_off;     // offset of this stream's token output
+    int pad;
+    int pages[kPageSlots];  // physical page per ring slot (-1 = unmapped)
+};
+
+struct CacheGeom {
+    void* kpool;      // [n_layers][n_pages][page_frames][D] (engine dtype)
+    void* vpool;
+    void* conv;       // [n_layers][max_streams][conv_ring][D]
+    int n_layers, n_pages, page_frames, D, L, conv_ring, max_streams;
+};
+
+// ---- Rel-pos attention over [cached window ; new chunk] with the fused append of the new K/V rows.
+template <typename T>
+void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const float* bias_u, const float* bias_v,
+                      const BatchEntry* meta, int n, int tmax_batch, const CacheGeom& cg, int layer, T* out,
+                      int ldo, int n_heads, int* dev_err, cudaStream_t s);
+
+// ---- Conv module core: GLU -> pad mask -> [conv cache ; new] -> depthwise k -> LN -> SiLU, cache update.
+template <typename T>
+void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, const float* ln_b,
+                 const BatchEntry* meta, int n, int tmax_batch, const CacheGeom& cg, int layer, int K, T* out,
+                 int ldo, cudaStream_t s);
+
+// ---- Subsampling (causal dw-striding x8, channel-last activations [b][t][f][c]).
+template <typename T>
+void sub_conv0(const float* mel, int rows_stride, int mel_bins, const BatchEntry* meta, int n, int Tin,
+               const float* w, const float* b, T* out, int T1, int F1, int C, cudaStream_t s);
+template <typename T>
+void sub_dwconv(const T* in, int Tin, int Fin, const int* in_valid_by_stage, int stage, const BatchEntry* meta,
+                int n, const float* w, const float* b, T* out, int Tout, int Fout, int C, cudaStream_t s);
+template <typename T>
+void sub_select(const float* sub_out, int T3, const float* out_bias, const BatchEntry* meta, int n, float* x,
+                int D, cudaStream_t s);
+
+// ---- Cache ops (microbenchmark / tests). rows are engine dtype.
+template <typename T>
+void cache_append(const T* kv_rows, const T* conv_rows, int k, const BatchEntry* meta, int n, const CacheGeom& cg,
+                  int* dev_err, cudaStream_t s);
+template <typename T>
+void cache_gather(T* kv_out, T* conv_out, const BatchEntry* meta, int n, const CacheGeom& cg, int* dev_err,
+                  cudaStream_t s);
+template <typename T>
+void conv_slot_zero(const int* slots, int n, const CacheGeom& cg, cudaStream_t s);
+
+// ---- RNN-T greedy (fused prediction LSTM + joint + argmax loop), one CTA per stream.
+struct RnntWeights {
+    const float* embed;    // [V, Hp]
+    const float* w_ih[4];  // [4Hp, Hp]
+    const float* w_hh[4];  // [4Hp, Hp]
+    const float* bias[4];  // [4Hp] = b_ih + b_hh
+    const float* pred_w;   // [J, Hp]
+    const float* pred_b;   // [J]
+    const float* out_w;    // [V, J]
+    const float* out_b;    // [V]
+    int layers, Hp, J, V, max_symbols;
+};
+struct RnntState {         // per slot
+    float* h;              // [slots][layers][Hp]
+    float* c;
+    float* pend_g;         // [slots][J]
+    float* pend_h;         // [slots][layers][Hp]
+    float* pend_c;
+    int* last_tok;         // [slots]
+    int* pend_valid;       // [slots]
+};
+void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, int ld_proj, const BatchEntry* meta,
+                 int n, int32_t* tokens, int tok_stride, int* n_tokens, cudaStream_t s);
+void rnnt_reset(const RnntState& st, const int* slots, int n, const RnntWeights& w, cudaStream_t s);
+
+void pack_frames(const float* frames, int rows_stride, const BatchEntry* meta, int n, int tmax, float* x, int D,
+                 cudaStream_t s);
+void scatter_rows(const float* src, const BatchEntry* meta, int n, float* dst, int tmax, int W, cudaStream_t s);
+size_t relpos_attention_smem_bytes(int tmax_batch, int L, int elem_bytes);
+size_t rnnt_smem_bytes(const RnntWeights& w);
+
+// ---- misc
+void fill_f32(float* p, float v, size_t n, cudaStream_t s);
+void f32_to_bf16(const float* in, bf16* out, size_t n, cudaStream_t s);
+void test_wait_timeout(int* dev_err, uint64_t limit_ns, cudaStream_t s);
+
+}  // namespace ud

@@ -1,0 +1,134 @@
+// LayerNorm over rows (eps 1e-5), one warp per row, fp32 statistics (two passes over registers).
+// Replaces layer_norm_f32 (Sources/DictatorEngine/Metal/20_conformer.metal:26-49); `layer_norm2` fuses a
+// layer's norm_out with the next layer's norm_feed_forward1 (FastConformer.swift:320 then :276).
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ud {
+namespace {
+
+// D = 128 * NV: each lane holds NV float4 of its row (D <= 1024).
+#define UD_LN_DISPATCH(KERNEL, ...)                                                              \
+    switch (D / 128) {                                                                           \
+        case 1: KERNEL<TO, 1><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
+        case 2: KERNEL<TO, 2><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
+        case 4: KERNEL<TO, 4><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
+        case 6: KERNEL<TO, 6><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
+        default: KERNEL<TO, 8><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                  \
+    }
+
+template <typename TO>
+__device__ __forceinline__ void store4(TO* p, const float* v) {
+    if constexpr (std::is_same<TO, float>::value) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+        __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(p) = u;
+    }
+}
+
+template <int NV>
+__device__ __forceinline__ void row_stats(const float (&v)[NV][4], int D, float& mean, float& rstd) {
+    constexpr int nv = NV;
+    float s = 0.f;
+    for (int i = 0; i < nv; ++i) s += v[i][0] + v[i][1] + v[i][2] + v[i][3];
+    mean = warp_sum(s) / static_cast<float>(D);
+    float q = 0.f;
+    for (int i = 0; i < nv; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float d = v[i][j] - mean;
+            q += d * d;
+        }
+    const float var = warp_sum(q) / static_cast<float>(D);
+    rstd = rsqrtf(var + 1e-5f);
+}
+
+template <typename TO, int NV>
+__global__ void __launch_bounds__(256) ln_kernel(const float* x, const float* __restrict__ g,
+                                                 const float* __restrict__ b, TO* y, int M, int D) {
+    // x and y may alias (in-place): each warp reads its whole row before writing it.
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + warp;
+    if (row >= M) return;
+    constexpr int nv = NV;
+    const float* xr = x + static_cast<size_t>(row) * D;
+    float v[NV][4];
+    for (int i = 0; i < nv; ++i) {
+        float4 t = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
+        v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
+    }
+    float mean, rstd;
+    row_stats<NV>(v, D, mean, rstd);
+    TO* yr = y + static_cast<size_t>(row) * D;
+    for (int i = 0; i < nv; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * g[c + j] + b[c + j];
+        store4<TO>(yr + c, o);
+    }
+}
+
+template <typename TO, int NV>
+__global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const float* __restrict__ g1,
+                                                  const float* __restrict__ b1, const float* __restrict__ g2,
+                                                  const float* __restrict__ b2, TO* __restrict__ y, int M, int D) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + warp;
+    if (row >= M) return;
+    constexpr int nv = NV;
+    float* xr = x + static_cast<size_t>(row) * D;
+    float v[NV][4];
+    for (int i = 0; i < nv; ++i) {
+        float4 t = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
+        v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
+    }
+    float mean, rstd;
+    row_stats<NV>(v, D, mean, rstd);
+    for (int i = 0; i < nv; ++i) {
+        const int c = (i * 32 + lane) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = (v[i][j] - mean) * rstd * g1[c + j] + b1[c + j];
+        *reinterpret_cast<float4*>(xr + c) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+    }
+    row_stats<NV>(v, D, mean, rstd);
+    TO* yr = y + static_cast<size_t>(row) * D;
+    for (int i = 0; i < nv; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * g2[c + j] + b2[c + j];
+        store4<TO>(yr + c, o);
+    }
+}
+
+}  // namespace
+
+template <typename TO>
+void layer_norm(const float* x, const float* g, const float* b, TO* y, int M, int D, cudaStream_t s) {
+    if (M <= 0) return;
+    UD_LN_DISPATCH(ln_kernel, x, g, b, y, M, D);
+}
+
+template <typename TO>
+void layer_norm2(float* x, const float* g1, const float* b1, const float* g2, const float* b2, TO* y, int M, int D,
+                 cudaStream_t s) {
+    if (M <= 0) return;
+    UD_LN_DISPATCH(ln2_kernel, x, g1, b1, g2, b2, y, M, D);
+}
+
+template void layer_norm<float>(const float*, const float*, const float*, float*, int, int, cudaStream_t);
+template void layer_norm<bf16>(const float*, const float*, const float*, bf16*, int, int, cudaStream_t);
+template void layer_norm2<float>(float*, const float*, const float*, const float*, const float*, float*, int, int,
+                                 cudaStream_t);
+template void layer_norm2<bf16>(float*, const float*, const float*, const float*, const float*, bf16*, int, int,
+                                cudaStream_t);
+
+}  // namespace ud

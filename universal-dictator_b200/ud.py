@@ -1,0 +1,363 @@
+"""ctypes binding of libud.so (include/ud.h), mirroring the reference's encoder protocol.
+
+The reference's host side is Swift:
+    protocol NemotronEncoder { var schedule: NemotronSchedule; func step(mel:nRows:validRows:keepAll:) throws
+                               -> (proj: [Float], frames: Int) }      Sources/DictatorCore/Nemotron/NemotronStreamer.swift:6-12
+    struct NemotronSchedule                                           Sources/DictatorCore/Nemotron/NemotronSchedule.swift:7-16
+    enum EngineError: Error                                           Sources/DictatorCore/Errors.swift:3-10
+This module exposes the same names and argument meanings over the C ABI: `CudaNemotronEncoder.step`
+returns (proj [frames, joint_dim] float32, frames) and raises `EngineError` where the Swift code throws.
+`Engine` adds the batched path, the cache operations and the RNN-T decoder.
+
+The library is loaded from this directory (libud.so, built by build.py); there is no fallback: if the
+library or a CUDA device is missing, construction raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Mapping, Sequence
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "libud.so"
+
+UD_OK = 0
+STATUS = {0: "ok", 1: "invalid argument", 2: "CUDA error", 3: "out of memory", 4: "no such stream",
+          5: "pool exhausted", 6: "weights error", 7: "not ready", 8: "device wait expired", 9: "I/O error",
+          10: "unsupported"}
+DTYPE_F32, DTYPE_BF16 = 0, 1
+KINDS = ["gemm_tc", "gemm_simt", "attention", "conv", "norm", "subsample", "rnnt", "cache", "other"]
+
+# Every symbol include/ud.h declares (the test suite checks the library exports exactly these).
+ABI_SYMBOLS = [
+    "ud_config_default", "ud_init", "ud_shutdown", "ud_load_weights", "ud_load_safetensors", "ud_stream_open",
+    "ud_stream_close", "ud_stream_step", "ud_step_batch", "ud_step_batch_device", "ud_rnnt_decode",
+    "ud_cache_append", "ud_cache_roll", "ud_cache_gather", "ud_cache_evict", "ud_cache_read", "ud_stream_info",
+    "ud_get_cuda_stream", "ud_pool_info", "ud_synchronize", "ud_launch_count", "ud_debug_gemm",
+    "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
+    "ud_status_string",
+]
+
+
+class EngineError(RuntimeError):
+    """A non-OK ud_status (the Swift EngineError / GPU failure of the reference)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+
+
+class Config(C.Structure):
+    _fields_ = [(n, C.c_int) for n in (
+        "n_layers", "d_model", "n_heads", "ff_dim", "conv_kernel", "left_context", "sub_channels", "mel_bins",
+        "joint_dim", "vocab", "pred_layers", "pred_hidden", "max_symbols", "dtype", "max_streams", "max_batch",
+        "max_chunk_frames", "page_frames", "n_pages")]
+
+
+class Weight(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("data", C.POINTER(C.c_float)), ("ndim", C.c_int), ("shape", C.c_int64 * 4)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FileNotFoundError(f"{LIB_PATH} is missing: build it with universal-dictator_b200/build.py")
+        L = C.CDLL(str(LIB_PATH))
+        P, I, F, VP = C.POINTER, C.c_int, C.c_float, C.c_void_p
+        eng = C.c_void_p
+        sig = {
+            "ud_config_default": (None, [P(Config)]),
+            "ud_init": (I, [P(Config), I, P(eng)]),
+            "ud_shutdown": (I, [eng]),
+            "ud_load_weights": (I, [eng, P(Weight), I]),
+            "ud_load_safetensors": (I, [eng, C.c_char_p]),
+            "ud_stream_open": (I, [eng, I, P(C.c_int32)]),
+            "ud_stream_close": (I, [eng, C.c_int32]),
+            "ud_stream_step": (I, [eng, C.c_int32, P(F), I, I, I, P(F), P(I)]),
+            "ud_step_batch": (I, [eng, I, P(C.c_int32), P(P(F)), P(I), P(I), P(I), P(F), P(I), P(C.c_int32), P(I)]),
+            "ud_step_batch_device": (I, [eng, I, P(C.c_int32), VP, I, P(I), P(I), P(I), VP, P(I), VP, VP]),
+            "ud_rnnt_decode": (I, [eng, C.c_int32, P(F), I, P(C.c_int32), P(I)]),
+            "ud_cache_append": (I, [eng, I, P(C.c_int32), I, VP, VP]),
+            "ud_cache_roll": (I, [eng, I, P(C.c_int32), I]),
+            "ud_cache_gather": (I, [eng, I, P(C.c_int32), VP, VP]),
+            "ud_cache_evict": (I, [eng, I, P(C.c_int32)]),
+            "ud_cache_read": (I, [eng, C.c_int32, I, I, VP]),
+            "ud_stream_info": (I, [eng, C.c_int32, P(I), P(I), P(I)]),
+            "ud_get_cuda_stream": (I, [eng, P(VP)]),
+            "ud_pool_info": (I, [eng, P(I), P(I), P(I)]),
+            "ud_synchronize": (I, [eng]),
+            "ud_launch_count": (I, [eng, P(C.c_int64)]),
+            "ud_debug_gemm": (I, [eng, VP, VP, I, I, I, VP, I, F, VP, F, VP, I]),
+            "ud_debug_wait_probe": (I, [eng, C.c_uint64]),
+            "ud_profile_enable": (I, [eng, I]),
+            "ud_profile_read": (I, [eng, I, P(C.c_double), P(C.c_int64)]),
+            "ud_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
+            "ud_status_string": (C.c_char_p, [I]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    lib().ud_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int):
+    if status != UD_OK:
+        raise EngineError(status, last_error())
+
+
+def default_config(**kw) -> Config:
+    c = Config()
+    lib().ud_config_default(C.byref(c))
+    for k, v in kw.items():
+        if not hasattr(c, k):
+            raise KeyError(k)
+        setattr(c, k, int(v))
+    return c
+
+
+def _ptr(a: np.ndarray, ctype=C.c_float):
+    return a.ctypes.data_as(C.POINTER(ctype))
+
+
+def _i32(seq) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(seq, dtype=np.int32))
+
+
+@dataclass(frozen=True)
+class NemotronSchedule:
+    """NemotronSchedule.swift:7-16."""
+
+    lookahead: int
+    left_context: int = 70
+    pre_encode_cache: int = 9
+    drop_extra: int = 2
+
+    @property
+    def first_chunk(self) -> int:
+        return 1 + 8 * self.lookahead
+
+    @property
+    def chunk(self) -> int:
+        return 8 + 8 * self.lookahead
+
+    @property
+    def out_frames_per_chunk(self) -> int:
+        return self.lookahead + 1
+
+    @property
+    def chunk_ms(self) -> int:
+        return 80 * (self.lookahead + 1)
+
+
+class Engine:
+    """One libud engine: one CUDA device, one CUDA stream, shared weights, a pool of stream slots."""
+
+    def __init__(self, config: Config | None = None, device: int = 0, **kw):
+        self.cfg = config if config is not None else default_config(**kw)
+        h = C.c_void_p()
+        check(lib().ud_init(C.byref(self.cfg), device, C.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().ud_shutdown(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    # ---------------------------------------------------------------- weights
+    def load_weights(self, sd: Mapping[str, object]):
+        keep = []
+        table = (Weight * len(sd))()
+        for i, (name, t) in enumerate(sd.items()):
+            a = t.detach().cpu().float().numpy() if hasattr(t, "detach") else np.asarray(t, np.float32)
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            nm = name.encode()
+            keep += [a, nm]
+            table[i].name = nm
+            table[i].data = _ptr(a)
+            table[i].ndim = a.ndim
+            for d in range(a.ndim):
+                table[i].shape[d] = a.shape[d]
+        check(lib().ud_load_weights(self.h, table, len(sd)))
+
+    def load_safetensors(self, path: str | Path):
+        check(lib().ud_load_safetensors(self.h, str(path).encode()))
+
+    # ---------------------------------------------------------------- streams
+    def open(self, lookahead: int) -> int:
+        sid = C.c_int32()
+        check(lib().ud_stream_open(self.h, lookahead, C.byref(sid)))
+        return sid.value
+
+    def close_stream(self, sid: int):
+        check(lib().ud_stream_close(self.h, sid))
+
+    def info(self, sid: int) -> tuple[int, int, int]:
+        cl, hd, st = C.c_int(), C.c_int(), C.c_int()
+        check(lib().ud_stream_info(self.h, sid, C.byref(cl), C.byref(hd), C.byref(st)))
+        return cl.value, hd.value, st.value
+
+    @property
+    def out_width(self) -> int:
+        return self.cfg.joint_dim or self.cfg.d_model
+
+    def step(self, sid: int, mel: np.ndarray, n_rows: int, valid_rows: int, keep_all: bool):
+        mel = np.ascontiguousarray(mel, dtype=np.float32)
+        out = np.zeros((self.cfg.max_chunk_frames, self.out_width), np.float32)
+        fr = C.c_int()
+        check(lib().ud_stream_step(self.h, sid, _ptr(mel), n_rows, valid_rows, int(keep_all), _ptr(out), C.byref(fr)))
+        return out[:fr.value].copy(), fr.value
+
+    def step_batch(self, ids: Sequence[int], mels: Sequence[np.ndarray], n_rows: Sequence[int],
+                   valid_rows: Sequence[int], keep_all: Sequence[bool], decode: bool = False):
+        """Host-buffer batched step. Returns (list of proj arrays, frames, list of token lists or None)."""
+        n = len(ids)
+        arrs = [np.ascontiguousarray(m, dtype=np.float32) for m in mels]
+        ptrs = (C.POINTER(C.c_float) * n)(*[_ptr(a) for a in arrs])
+        tm, W = self.cfg.max_chunk_frames, self.out_width
+        out = np.zeros((n, tm, W), np.float32)
+        frames = np.zeros(n, np.int32)
+        ids_a, nr, vr, ka = _i32(ids), _i32(n_rows), _i32(valid_rows), _i32([int(k) for k in keep_all])
+        toks = np.zeros((n, tm * self.cfg.max_symbols), np.int32) if decode else None
+        ntok = np.zeros(n, np.int32) if decode else None
+        check(lib().ud_step_batch(self.h, n, _ptr(ids_a, C.c_int32), ptrs, _ptr(nr, C.c_int), _ptr(vr, C.c_int),
+                                  _ptr(ka, C.c_int), _ptr(out), _ptr(frames, C.c_int),
+                                  _ptr(toks, C.c_int32) if decode else None, _ptr(ntok, C.c_int) if decode else None))
+        projs = [out[i, :frames[i]].copy() for i in range(n)]
+        tok_lists = [toks[i, :ntok[i]].tolist() for i in range(n)] if decode else None
+        return projs, frames.tolist(), tok_lists
+
+    def step_batch_device(self, ids, mel_dev_ptr: int, rows_stride: int, n_rows, valid_rows, keep_all,
+                          proj_dev_ptr: int, tokens_dev_ptr: int | None = None, ntok_dev_ptr: int | None = None):
+        """Device-resident batched step, asynchronous on the engine stream. Returns frames (host)."""
+        n = len(ids)
+        frames = np.zeros(n, np.int32)
+        ids_a, nr, vr, ka = _i32(ids), _i32(n_rows), _i32(valid_rows), _i32([int(k) for k in keep_all])
+        check(lib().ud_step_batch_device(self.h, n, _ptr(ids_a, C.c_int32), C.c_void_p(mel_dev_ptr), rows_stride,
+                                         _ptr(nr, C.c_int), _ptr(vr, C.c_int), _ptr(ka, C.c_int),
+                                         C.c_void_p(proj_dev_ptr), _ptr(frames, C.c_int),
+                                         C.c_void_p(tokens_dev_ptr) if tokens_dev_ptr else None,
+                                         C.c_void_p(ntok_dev_ptr) if ntok_dev_ptr else None))
+        return frames.tolist()
+
+    def rnnt_decode(self, sid: int, f: np.ndarray) -> list[int]:
+        f = np.ascontiguousarray(f, dtype=np.float32)
+        toks = np.zeros(max(1, f.shape[0] * self.cfg.max_symbols), np.int32)
+        nt = C.c_int()
+        check(lib().ud_rnnt_decode(self.h, sid, _ptr(f), f.shape[0], _ptr(toks, C.c_int32), C.byref(nt)))
+        return toks[:nt.value].tolist()
+
+    # ---------------------------------------------------------------- caches
+    def cache_append(self, ids, k: int, kv_dev_ptr: int | None, conv_dev_ptr: int | None):
+        a = _i32(ids)
+        check(lib().ud_cache_append(self.h, len(a), _ptr(a, C.c_int32), k,
+                                    C.c_void_p(kv_dev_ptr) if kv_dev_ptr else None,
+                                    C.c_void_p(conv_dev_ptr) if conv_dev_ptr else None))
+
+    def cache_roll(self, ids, k: int):
+        a = _i32(ids)
+        check(lib().ud_cache_roll(self.h, len(a), _ptr(a, C.c_int32), k))
+
+    def cache_gather(self, ids, kv_dev_ptr: int | None, conv_dev_ptr: int | None):
+        a = _i32(ids)
+        check(lib().ud_cache_gather(self.h, len(a), _ptr(a, C.c_int32),
+                                    C.c_void_p(kv_dev_ptr) if kv_dev_ptr else None,
+                                    C.c_void_p(conv_dev_ptr) if conv_dev_ptr else None))
+
+    def cache_evict(self, ids):
+        a = _i32(ids)
+        check(lib().ud_cache_evict(self.h, len(a), _ptr(a, C.c_int32)))
+
+    def cache_read(self, sid: int, layer: int, kind: int) -> np.ndarray:
+        """One stream's window of one layer: kind 0 K / 1 V -> [L, d], kind 2 conv -> [k-1, d]; raw dtype
+        (float32, or bf16 returned as uint16 bit patterns)."""
+        rows = self.cfg.left_context if kind < 2 else self.cfg.conv_kernel - 1
+        dt = np.uint16 if self.cfg.dtype == DTYPE_BF16 else np.float32
+        out = np.zeros((rows, self.cfg.d_model), dt)
+        check(lib().ud_cache_read(self.h, sid, layer, kind, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def pool_info(self) -> tuple[int, int, int]:
+        f, t, e = C.c_int(), C.c_int(), C.c_int()
+        check(lib().ud_pool_info(self.h, C.byref(f), C.byref(t), C.byref(e)))
+        return f.value, t.value, e.value
+
+    def cuda_stream(self) -> int:
+        p = C.c_void_p()
+        check(lib().ud_get_cuda_stream(self.h, C.byref(p)))
+        return p.value or 0
+
+    def synchronize(self):
+        check(lib().ud_synchronize(self.h))
+
+    def profile(self, enable: bool):
+        check(lib().ud_profile_enable(self.h, int(enable)))
+
+    def profile_read(self) -> dict[str, tuple[float, int]]:
+        """{kind: (total device ms, launches)} since profiling was enabled."""
+        out = {}
+        for k, name in enumerate(KINDS):
+            ms, n = C.c_double(), C.c_int64()
+            check(lib().ud_profile_read(self.h, k, C.byref(ms), C.byref(n)))
+            out[name] = (ms.value, n.value)
+        return out
+
+    def launch_count(self) -> int:
+        v = C.c_int64()
+        check(lib().ud_launch_count(self.h, C.byref(v)))
+        return v.value
+
+    def debug_gemm(self, A_ptr, W_ptr, M, N, K, C_ptr, bias_ptr=None, act=0, out_scale=1.0, res_ptr=None,
+                   res_scale=1.0, out_bf16=False):
+        check(lib().ud_debug_gemm(self.h, C.c_void_p(A_ptr), C.c_void_p(W_ptr), M, N, K,
+                                  C.c_void_p(bias_ptr) if bias_ptr else None, act, out_scale,
+                                  C.c_void_p(res_ptr) if res_ptr else None, res_scale, C.c_void_p(C_ptr),
+                                  int(out_bf16)))
+
+
+def wait_probe(engine: "Engine", limit_ns: int):
+    check(lib().ud_debug_wait_probe(engine.h, limit_ns))
+
+
+class CudaNemotronEncoder:
+    """NemotronEncoder conformer over libud: one object = one stream's caches (NemotronStreamer.swift:6-12)."""
+
+    def __init__(self, engine: Engine, schedule: NemotronSchedule):
+        self.engine = engine
+        self.schedule = schedule
+        self.sid = engine.open(schedule.lookahead)
+
+    def step(self, mel: np.ndarray, n_rows: int, valid_rows: int, keep_all: bool):
+        return self.engine.step(self.sid, mel, n_rows, valid_rows, keep_all)
+
+    def close(self):
+        if self.sid is not None:
+            self.engine.close_stream(self.sid)
+            self.sid = None
