@@ -199,9 +199,10 @@ def run_reference(args, world, rank):
 
 def workload_config(args):
     return {"workload": f"C3: {args.streams} synchronous streams/GPU, [70,{args.lookahead}] (T={args.lookahead + 1}, "
-                        f"{9 + 8 + 8 * args.lookahead}-row mel chunks), 24-layer FastConformer + joint.enc + RNN-T greedy",
+                        f"{9 + 8 + 8 * args.lookahead}-row mel chunks), subsampling + 24-layer FastConformer + joint.enc"
+                        + (" + RNN-T greedy" if args.decode else ""),
             "streams_per_gpu": args.streams, "lookahead": args.lookahead, "n_layers": 24, "d_model": 1024,
-            "cache": "paged rings, 16-frame pages", "decode": not args.no_decode,
+            "cache": "paged rings, 16-frame pages", "decode": args.decode,
             "l2": "inputs larger than L2 (1.16 GB of weights and the per-stream caches stream through each step)",
             "parallelism": f"stream-sharded x{args.gpus}, no collectives"}
 
@@ -214,7 +215,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--streams", type=int, default=256)
     ap.add_argument("--lookahead", type=int, default=13)
-    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode", action="store_true",
+                    help="also run greedy RNN-T decoding in each step (configs 2 and 4; C3 is the encoder step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -258,7 +260,7 @@ def main():
     ntok = torch.empty(n, device=dev, dtype=torch.int32)
     torch.cuda.synchronize()
     sched = chunk_schedule(R, TOTAL_ROWS)
-    decode = not args.no_decode
+    decode = args.decode
     state = {"i": 0}
 
     def step():

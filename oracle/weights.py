@@ -128,3 +128,18 @@ def round_bf16(sd: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
         else:
             out[k] = v
     return out
+
+
+def sharpen_joint(sd: dict[str, torch.Tensor], dims: ModelDims, seed: int, joint_std: float = 0.25,
+                  embed_std: float = 1.0) -> dict[str, torch.Tensor]:
+    """Test-weight variant with a sharp joint: joint.enc and joint.joint_net.2 drawn with `joint_std` and the
+    embedding with `embed_std` (blank row zero) from their own generator, the LSTM left at its small init.
+    Logit margins are then large (well above 0.5) while the prediction recurrence stays well conditioned."""
+    g = torch.Generator().manual_seed(seed)
+    out = dict(sd)
+    out["joint.joint_net.2.weight"] = torch.randn(dims.vocab, dims.joint_dim, generator=g) * joint_std
+    out["joint.enc.weight"] = torch.randn(dims.joint_dim, dims.d_model, generator=g) * joint_std
+    emb = torch.randn(dims.vocab, dims.pred_hidden, generator=g) * embed_std
+    emb[dims.blank] = 0
+    out["decoder.prediction.embed.weight"] = emb
+    return out

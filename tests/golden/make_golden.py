@@ -32,7 +32,7 @@ import torch
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 
-from oracle.weights import BLOCK1, NEMOTRON, ModelDims, make_weights  # noqa: E402
+from oracle.weights import BLOCK1, NEMOTRON, ModelDims, make_weights, sharpen_joint  # noqa: E402
 from oracle.stream_step import chunk_plan, next_len, sub_len  # noqa: E402
 
 
@@ -175,18 +175,21 @@ def gen_offline_subsample(cs, rows=81):
     print(f"wrote offline_subsample.npz: rows={rows} -> {n}")
 
 
-def gen_greedy(cs, seed, std, T, name, blank_offset=0.0):
+def gen_greedy(cs, seed, std, T, name, blank_offset=0.0, sharp_seed=0):
     """check_spec.greedy over seeded frames. `blank_offset` is added to the blank logit's bias so that
-    blank wins some decisions (with plain random weights every frame emits the 10-symbol maximum)."""
+    blank wins some decisions (with plain random weights every frame emits the 10-symbol maximum);
+    `sharp_seed` > 0 swaps in a sharp joint (oracle.weights.sharpen_joint) for large logit margins."""
     dims = ModelDims(n_layers=0, sub_channels=0, pred_layers=2)     # check_spec.greedy hard-codes 2 layers
     sd = make_weights(dims, seed=seed, std=std)
+    if sharp_seed:
+        sd = sharpen_joint(sd, dims, sharp_seed)
     sd["joint.joint_net.2.bias"][dims.blank] += blank_offset
     g = torch.Generator().manual_seed(seed + 100)
     enc = torch.randn(T, dims.d_model, generator=g)
     with torch.no_grad():
         toks = cs.greedy(enc, sd, max_symbols=10, blank=dims.blank)
     np.savez_compressed(HERE / name, enc=enc.numpy(), tokens=np.asarray(toks, np.int32), seed=seed, std=std,
-                        blank_offset=blank_offset)
+                        blank_offset=blank_offset, sharp_seed=sharp_seed)
     print(f"wrote {name}: {len(toks)} tokens over {T} frames")
 
 
@@ -201,7 +204,7 @@ def main():
     gen_offline_subsample(cs)
     gen_greedy(cs, seed=0, std=0.02, T=24, name="greedy_std002.npz")
     gen_greedy(cs, seed=0, std=0.02, T=24, name="greedy_std002_blank.npz", blank_offset=0.5)
-    gen_greedy(cs, seed=3, std=0.25, T=24, name="greedy_std025_blank.npz", blank_offset=60.0)
+    gen_greedy(cs, seed=3, std=0.02, T=24, name="greedy_sharp_joint.npz", blank_offset=100.0, sharp_seed=77)
     # [70,13] with two layers: first chunk 105 rows (T=14, no drop), steady 121 rows (T=14 after dropping 2),
     # and a short final chunk with fewer valid rows than rows (keep_all, validT < T).
     gen_stream(na, ModelDims(n_layers=2), lookahead=13, total_rows=369, valid_frames=360, name="stream_70_13_l2.npz")

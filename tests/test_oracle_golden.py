@@ -11,7 +11,7 @@ import torch
 
 from oracle.rnnt import RNNT, DecoderState
 from oracle.stream_step import Encoder, StreamState, chunk_plan, sub_len
-from oracle.weights import BLOCK1, NEMOTRON, ModelDims, make_weights
+from oracle.weights import BLOCK1, NEMOTRON, ModelDims, make_weights, sharpen_joint
 
 
 def rel(a, b):
@@ -88,11 +88,13 @@ def test_stream_steps_match_reference_step(golden_dir, name):
         assert rel(st.conv[li], g[f"conv_l{li}"]) < 1e-5
 
 
-@pytest.mark.parametrize("name", ["greedy_std002.npz", "greedy_std002_blank.npz", "greedy_std025_blank.npz"])
+@pytest.mark.parametrize("name", ["greedy_std002.npz", "greedy_std002_blank.npz", "greedy_sharp_joint.npz"])
 def test_greedy_matches_check_spec(golden_dir, name):
     g = np.load(golden_dir / name)
     dims = ModelDims(n_layers=0, sub_channels=0, pred_layers=2)
     sd = make_weights(dims, seed=int(g["seed"]), std=float(g["std"]))
+    if int(g["sharp_seed"]):
+        sd = sharpen_joint(sd, dims, int(g["sharp_seed"]))
     sd["joint.joint_net.2.bias"][dims.blank] += float(g["blank_offset"])
     r = RNNT(sd, dims)
     f = r.enc_proj(torch.from_numpy(g["enc"]))

@@ -205,6 +205,266 @@ __global__ void __launch_bounds__(256) relpos_attn_kernel(const T* __restrict__ 
     }
 }
 
+// ---------------------------------------------------------------- tensor-core variant (bf16, T <= 16)
+// The same attention with mma.sync m16n8k16 (bf16 in, fp32 accumulate):
+//   AC    = (Q + u) [16 x dk] . K^T [dk x nk]           score content term
+//   BDraw = (Q + v) [16 x dk] . P^T [dk x np]           position term for every rel in the window
+//   S[i, j] = (AC[i, j] + BDraw[i, (L + i - j) - rel_min]) / sqrt(dk), softmax over visible keys (fp32)
+//   O     = softmax [16 x nk] (bf16) . V [nk x dk]
+// One CTA (4 warps) per (stream, head); K, V and the needed P rows are staged in shared memory with
+// cp.async; fragments come from ldmatrix (row stride 136 elements: conflict-free, 16-byte aligned rows).
+namespace tc {
+
+constexpr int TM = 16;
+constexpr int RSB = 136;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+struct Lay {
+    int nkp, npp, psw;  // padded key rows (x16), padded position rows (x16), softmax-row stride
+    size_t qu, qv, k, v, p, ac, bd, pb, total;
+    __host__ __device__ Lay(int L) {
+        nkp = (L + TM + 15) / 16 * 16;
+        npp = (TM + L + TM - 1 + 15) / 16 * 16;
+        psw = nkp + 8;
+        size_t o = 0;
+        qu = o; o += sizeof(bf16) * TM * RSB;
+        qv = o; o += sizeof(bf16) * TM * RSB;
+        k = o;  o += sizeof(bf16) * nkp * RSB;
+        v = o;  o += sizeof(bf16) * nkp * RSB;
+        p = o;  o += sizeof(bf16) * npp * RSB;
+        ac = o; o += sizeof(float) * TM * nkp;
+        bd = o; o += sizeof(float) * TM * npp;
+        pb = o; o += sizeof(bf16) * TM * psw;
+        total = (o + 127) / 128 * 128;
+    }
+};
+
+__global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ qkv, int ld_qkv,
+                                                      const bf16* __restrict__ ptab, int tmax,
+                                                      const float* __restrict__ bias_u,
+                                                      const float* __restrict__ bias_v,
+                                                      const BatchEntry* __restrict__ meta, const CacheGeom cg,
+                                                      int layer, bf16* __restrict__ out, int ldo, int* err) {
+    constexpr int DKk = 128;
+    const int b = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const BatchEntry& me = meta[b];
+    const int T_ = me.T, L = cg.L, D = cg.D, PF = cg.page_frames;
+    const int row_off = me.row_off, head = me.head;
+    const int lo = L - me.cache_len, hi = L + me.valid_t;
+    const int nk = hi > lo ? hi - lo : 0;
+    const int rel_min = L - hi + 1;
+    const int np = nk > 0 ? T_ + nk - 1 : 0;
+    const int hoff = h * DKk;
+    const Lay lay(L);
+
+    extern __shared__ __align__(128) uint8_t sm[];
+    bf16* QU = reinterpret_cast<bf16*>(sm + lay.qu);
+    bf16* QV = reinterpret_cast<bf16*>(sm + lay.qv);
+    bf16* Ks = reinterpret_cast<bf16*>(sm + lay.k);
+    bf16* Vs = reinterpret_cast<bf16*>(sm + lay.v);
+    bf16* Ps = reinterpret_cast<bf16*>(sm + lay.p);
+    float* AC = reinterpret_cast<float*>(sm + lay.ac);
+    float* BD = reinterpret_cast<float*>(sm + lay.bd);
+    bf16* Pb = reinterpret_cast<bf16*>(sm + lay.pb);
+
+    // ---- stage K, V (visible window) and P rows with cp.async; zero the padding rows.
+    const bf16* kpool = reinterpret_cast<const bf16*>(cg.kpool);
+    const bf16* vpool = reinterpret_cast<const bf16*>(cg.vpool);
+    for (int idx = tid; idx < nk * 16; idx += 128) {
+        const int r = idx >> 4, c = (idx & 15) * 8;
+        const int j = lo + r;
+        const bf16 *ks, *vs;
+        if (j < L) {
+            const int f = head - L + j;
+            const int page = me.pages[(f / PF) % kPageSlots];
+            if (page < 0 || page >= cg.n_pages) {
+                report_error(err, DEV_BAD_PAGE);
+                *reinterpret_cast<uint4*>(Ks + r * RSB + c) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(Vs + r * RSB + c) = make_uint4(0u, 0u, 0u, 0u);
+                continue;
+            }
+            const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
+            ks = kpool + off;
+            vs = vpool + off;
+        } else {
+            const bf16* src = qkv + static_cast<size_t>(row_off + (j - L)) * ld_qkv + hoff + c;
+            ks = src + D;
+            vs = src + 2 * D;
+        }
+        cp_async16(Ks + r * RSB + c, ks);
+        cp_async16(Vs + r * RSB + c, vs);
+    }
+    for (int idx = tid; idx < np * 16; idx += 128) {
+        const int r = idx >> 4, c = (idx & 15) * 8;
+        cp_async16(Ps + r * RSB + c, ptab + static_cast<size_t>(rel_min + r + tmax - 1) * D + hoff + c);
+    }
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int idx = tid; idx < (lay.nkp - nk) * 16; idx += 128) {
+        const int r = nk + (idx >> 4), c = (idx & 15) * 8;
+        *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
+        *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
+    }
+    for (int idx = tid; idx < (lay.npp - np) * 16; idx += 128) {
+        const int r = np + (idx >> 4), c = (idx & 15) * 8;
+        *reinterpret_cast<uint4*>(Ps + r * RSB + c) = z;
+    }
+    // queries with the position biases, rounded to bf16 (rows >= T are zero)
+    for (int idx = tid; idx < TM * 16; idx += 128) {
+        const int i = idx >> 4, c = (idx & 15) * 8;
+        float q[8];
+        if (i < T_) {
+            load16<bf16>(qkv + static_cast<size_t>(row_off + i) * ld_qkv + hoff + c, q);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) q[e] = 0.f;
+        }
+        float a[8], bb[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            a[e] = i < T_ ? q[e] + bias_u[hoff + c + e] : 0.f;
+            bb[e] = i < T_ ? q[e] + bias_v[hoff + c + e] : 0.f;
+        }
+        store16<bf16>(QU + i * RSB + c, a);
+        store16<bf16>(QV + i * RSB + c, bb);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+
+    // ---- AC and BDraw: jobs of two n-tiles (16 columns), round-robin over the 4 warps.
+    {
+        uint32_t aq[8][4], av[8][4];
+        const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            ldsm_x4(aq[ks], QU + arow * RSB + ks * 16 + acol);
+            ldsm_x4(av[ks], QV + arow * RSB + ks * 16 + acol);
+        }
+        const int n_ac = (nk + 15) / 16, n_bd = (np + 15) / 16;
+        const int g = lane >> 2, t4 = lane & 3;
+        const int brow = (lane & 7) + ((lane >> 4) << 3), bcol = ((lane >> 3) & 1) * 8;
+        for (int job = warp; job < n_ac + n_bd; job += 4) {
+            const bool is_ac = job < n_ac;
+            const int n0 = (is_ac ? job : job - n_ac) * 16;
+            const bf16* Bs = is_ac ? Ks : Ps;
+            float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                uint32_t bfr[4];
+                ldsm_x4(bfr, Bs + (n0 + brow) * RSB + ks * 16 + bcol);
+                const uint32_t* a = is_ac ? aq[ks] : av[ks];
+                mma16816(c0, a, bfr[0], bfr[1]);
+                mma16816(c1, a, bfr[2], bfr[3]);
+            }
+            float* dst = is_ac ? AC : BD;
+            const int w = is_ac ? lay.nkp : lay.npp;
+            dst[g * w + n0 + 2 * t4] = c0[0];
+            dst[g * w + n0 + 2 * t4 + 1] = c0[1];
+            dst[(g + 8) * w + n0 + 2 * t4] = c0[2];
+            dst[(g + 8) * w + n0 + 2 * t4 + 1] = c0[3];
+            dst[g * w + n0 + 8 + 2 * t4] = c1[0];
+            dst[g * w + n0 + 8 + 2 * t4 + 1] = c1[1];
+            dst[(g + 8) * w + n0 + 8 + 2 * t4] = c1[2];
+            dst[(g + 8) * w + n0 + 8 + 2 * t4 + 1] = c1[3];
+        }
+    }
+    __syncthreads();
+
+    // ---- softmax rows (fp32), probabilities to bf16
+    const float scale = rsqrtf(static_cast<float>(DKk));
+    for (int i = warp; i < TM; i += 4) {
+        bf16* prow = Pb + i * lay.psw;
+        if (i >= T_ || nk == 0) {
+            for (int jj = lane; jj < lay.nkp; jj += 32) prow[jj] = __float2bfloat16_rn(0.f);
+            continue;
+        }
+        const float* acr = AC + i * lay.nkp;
+        const float* bdr = BD + i * lay.npp + i + nk - 1;   // BDraw column for key jj is (i + nk - 1 - jj)
+        float m = -INFINITY;
+        for (int jj = lane; jj < nk; jj += 32) m = fmaxf(m, (acr[jj] + bdr[-jj]) * scale);
+        m = warp_max(m);
+        float sum = 0.f;
+        for (int jj = lane; jj < nk; jj += 32) sum += expf((acr[jj] + bdr[-jj]) * scale - m);
+        sum = warp_sum(sum);
+        const float inv = 1.f / sum;
+        for (int jj = lane; jj < lay.nkp; jj += 32)
+            prow[jj] = __float2bfloat16_rn(jj < nk ? expf((acr[jj] + bdr[-jj]) * scale - m) * inv : 0.f);
+    }
+    __syncthreads();
+
+    // ---- O = P . V: warp w owns output columns [32w, 32w + 32)
+    {
+        float acc[4][4] = {};
+        const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+        const int vrow = (lane & 7) + ((lane >> 3) & 1) * 8, vcol = (lane >> 4) * 8;
+        const int ksteps = (nk + 15) / 16;
+        for (int ks = 0; ks < ksteps; ++ks) {
+            uint32_t a[4];
+            ldsm_x4(a, Pb + arow * lay.psw + ks * 16 + acol);
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+                const int n0 = warp * 32 + pr * 16;
+                uint32_t bfr[4];
+                ldsm_x4_t(bfr, Vs + (ks * 16 + vrow) * RSB + n0 + vcol);
+                mma16816(acc[pr * 2], a, bfr[0], bfr[1]);
+                mma16816(acc[pr * 2 + 1], a, bfr[2], bfr[3]);
+            }
+        }
+        const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+            const int col = hoff + warp * 32 + nt * 8 + 2 * t4;
+            if (g < T_)
+                *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g) * ldo + col) =
+                    __floats2bfloat162_rn(acc[nt][0], acc[nt][1]);
+            if (g + 8 < T_)
+                *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g + 8) * ldo + col) =
+                    __floats2bfloat162_rn(acc[nt][2], acc[nt][3]);
+        }
+    }
+
+    // ---- append this chunk's K/V rows at frames head + t
+    bf16* kw = reinterpret_cast<bf16*>(cg.kpool);
+    bf16* vw = reinterpret_cast<bf16*>(cg.vpool);
+    for (int idx = tid; idx < T_ * 16; idx += 128) {
+        const int t = idx >> 4, c = (idx & 15) * 8;
+        const int f = head + t;
+        const int page = me.pages[(f / PF) % kPageSlots];
+        if (page < 0 || page >= cg.n_pages) {
+            report_error(err, DEV_BAD_PAGE);
+            continue;
+        }
+        const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
+        const bf16* src = qkv + static_cast<size_t>(row_off + t) * ld_qkv + hoff + c;
+        *reinterpret_cast<uint4*>(kw + off) = *reinterpret_cast<const uint4*>(src + D);
+        *reinterpret_cast<uint4*>(vw + off) = *reinterpret_cast<const uint4*>(src + 2 * D);
+    }
+}
+
+}  // namespace tc
+
 }  // namespace
 
 template <typename T>
@@ -212,6 +472,21 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
                       const BatchEntry* meta, int n, int tmax_batch, const CacheGeom& cg, int layer, T* out, int ldo,
                       int n_heads, int* dev_err, cudaStream_t s) {
     if (n <= 0) return;
+    if constexpr (std::is_same<T, bf16>::value) {
+        if (tmax_batch <= tc::TM) {
+            const tc::Lay lay(cg.L);
+            static size_t tc_attr = 0;
+            if (lay.total > tc_attr) {
+                cudaFuncSetAttribute(tc::attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(lay.total));
+                tc_attr = lay.total;
+            }
+            dim3 grid(n, n_heads);
+            tc::attn_tc_kernel<<<grid, 128, lay.total, s>>>(qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer,
+                                                            out, ldo, dev_err);
+            return;
+        }
+    }
     const AttnSmem<T> lay(tmax_batch, cg.L);
     static size_t attr_set = 0;
     if (lay.total > 48 * 1024 && lay.total > attr_set) {

@@ -108,7 +108,7 @@ __global__ void conv_zero_kernel(const int* __restrict__ slots, const CacheGeom 
 template <typename T>
 void cache_append(const T* kv_rows, const T* conv_rows, int k, const BatchEntry* meta, int n, const CacheGeom& cg,
                   int* dev_err, cudaStream_t s) {
-    if (n <= 0 || k <= 0) return;
+    if (n <= 0 || k <= 0 || cg.n_layers <= 0) return;
     dim3 grid(n, cg.n_layers);
     append_kernel<T><<<grid, 256, 0, s>>>(kv_rows, conv_rows, k, meta, cg, dev_err);
 }
@@ -116,14 +116,14 @@ void cache_append(const T* kv_rows, const T* conv_rows, int k, const BatchEntry*
 template <typename T>
 void cache_gather(T* kv_out, T* conv_out, const BatchEntry* meta, int n, const CacheGeom& cg, int* dev_err,
                   cudaStream_t s) {
-    if (n <= 0) return;
+    if (n <= 0 || cg.n_layers <= 0) return;
     dim3 grid(n, cg.n_layers);
     gather_kernel<T><<<grid, 256, 0, s>>>(kv_out, conv_out, meta, cg, dev_err);
 }
 
 template <typename T>
 void conv_slot_zero(const int* slots, int n, const CacheGeom& cg, cudaStream_t s) {
-    if (n <= 0) return;
+    if (n <= 0 || cg.n_layers <= 0) return;
     dim3 grid(n, cg.n_layers);
     conv_zero_kernel<T><<<grid, 256, 0, s>>>(slots, cg);
 }

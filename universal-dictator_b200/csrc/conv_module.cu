@@ -12,8 +12,25 @@
 namespace ud {
 namespace {
 
+template <typename T> struct Pair;
+template <> struct Pair<float> {
+    using V = float2;
+    static __device__ __forceinline__ float2 ld(const float* p) { return *reinterpret_cast<const float2*>(p); }
+    static __device__ __forceinline__ void st(float* p, float a, float b) { *reinterpret_cast<float2*>(p) = make_float2(a, b); }
+};
+template <> struct Pair<bf16> {
+    static __device__ __forceinline__ float2 ld(const bf16* p) {
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    }
+    static __device__ __forceinline__ void st(bf16* p, float a, float b) {
+        *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+    }
+};
+
+// Each thread owns a channel pair; the time loop reads only the GLU input and this thread's ring rows, so
+// loads of different frames are independent (restrict pointers) and stay in flight together.
 template <typename T, int KW>
-__global__ void __launch_bounds__(256) conv_module_kernel(const T* __restrict__ pw, int ld_pw,
+__global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ pw, int ld_pw,
                                                           const float* __restrict__ dw, const float* __restrict__ g,
                                                           const float* __restrict__ beta,
                                                           const BatchEntry* __restrict__ meta, const CacheGeom cg,
@@ -23,30 +40,46 @@ __global__ void __launch_bounds__(256) conv_module_kernel(const T* __restrict__ 
     const int b = blockIdx.x;
     const BatchEntry& me = meta[b];
     const int D = cg.D, T_ = me.T, vt = me.valid_t, head = me.head, row_off = me.row_off;
-    T* ring = reinterpret_cast<T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
+    T* __restrict__ ring = reinterpret_cast<T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
 
-    for (int c = threadIdx.x; c < D; c += blockDim.x) {
-        float w[KW], win[KW];
+    for (int c = threadIdx.x * 2; c < D; c += blockDim.x * 2) {
+        float w0[KW], w1[KW], a[KW], bq[KW];
 #pragma unroll
-        for (int k = 0; k < KW; ++k) w[k] = dw[c * KW + k];
+        for (int k = 0; k < KW; ++k) {
+            w0[k] = dw[c * KW + k];
+            w1[k] = dw[(c + 1) * KW + k];
+        }
 #pragma unroll
-        for (int i = 0; i < R; ++i) win[i] = to_f<T>(ring[((head + i) % R) * D + c]);  // frame head - R + i
+        for (int i = 0; i < R; ++i) {  // frame head - R + i
+            const float2 v = Pair<T>::ld(ring + ((head + i) % R) * D + c);
+            a[i] = v.x;
+            bq[i] = v.y;
+        }
+#pragma unroll 4
         for (int t = 0; t < T_; ++t) {
-            float gv = 0.f;
+            float g0 = 0.f, g1 = 0.f;
             if (t < vt) {
-                const T* pr = pw + static_cast<size_t>(row_off + t) * ld_pw;
-                const float a = to_f<T>(pr[c]), gate = to_f<T>(pr[D + c]);
-                gv = a / (1.f + expf(-gate));
+                const T* pr = pw + static_cast<size_t>(row_off + t) * ld_pw + c;
+                const float2 val = Pair<T>::ld(pr), gate = Pair<T>::ld(pr + D);
+                g0 = val.x / (1.f + expf(-gate.x));
+                g1 = val.y / (1.f + expf(-gate.y));
             }
-            win[R] = gv;
-            float acc = 0.f;
+            a[R] = g0;
+            bq[R] = g1;
+            float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-            for (int k = 0; k < KW; ++k) acc = fmaf(w[k], win[k], acc);
-            ys[t * D + c] = acc;
+            for (int k = 0; k < KW; ++k) {
+                y0 = fmaf(w0[k], a[k], y0);
+                y1 = fmaf(w1[k], bq[k], y1);
+            }
+            *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(y0, y1);
             // Ring row (head + t) % R held frame head + t - R, already consumed above.
-            if (t >= T_ - R) ring[((head + t) % R) * D + c] = from_f<T>(gv);
+            if (t >= T_ - R) Pair<T>::st(ring + ((head + t) % R) * D + c, g0, g1);
 #pragma unroll
-            for (int k = 0; k < R; ++k) win[k] = win[k + 1];
+            for (int k = 0; k < R; ++k) {
+                a[k] = a[k + 1];
+                bq[k] = bq[k + 1];
+            }
         }
     }
     __syncthreads();
@@ -54,18 +87,24 @@ __global__ void __launch_bounds__(256) conv_module_kernel(const T* __restrict__ 
     for (int t = warp; t < T_; t += nwarps) {
         const float* yr = ys + t * D;
         float s = 0.f;
-        for (int c = lane; c < D; c += 32) s += yr[c];
+        for (int c = lane * 4; c < D; c += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(yr + c);
+            s += v.x + v.y + v.z + v.w;
+        }
         const float mean = warp_sum(s) / static_cast<float>(D);
         float q = 0.f;
-        for (int c = lane; c < D; c += 32) {
-            const float d = yr[c] - mean;
-            q += d * d;
+        for (int c = lane * 4; c < D; c += 128) {
+            const float4 v = *reinterpret_cast<const float4*>(yr + c);
+            q += (v.x - mean) * (v.x - mean) + (v.y - mean) * (v.y - mean) + (v.z - mean) * (v.z - mean) +
+                 (v.w - mean) * (v.w - mean);
         }
         const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(D) + 1e-5f);
         T* orow = out + static_cast<size_t>(row_off + t) * ldo;
-        for (int c = lane; c < D; c += 32) {
-            const float v = (yr[c] - mean) * rstd * g[c] + beta[c];
-            orow[c] = from_f<T>(v / (1.f + expf(-v)));
+        for (int c = lane * 2; c < D; c += 64) {
+            const float2 v = *reinterpret_cast<const float2*>(yr + c);
+            const float z0 = (v.x - mean) * rstd * g[c] + beta[c];
+            const float z1 = (v.y - mean) * rstd * g[c + 1] + beta[c + 1];
+            Pair<T>::st(orow + c, z0 / (1.f + expf(-z0)), z1 / (1.f + expf(-z1)));
         }
     }
 }
@@ -83,7 +122,7 @@ void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, con
                              static_cast<int>(smem));
         attr_set = smem;
     }
-    conv_module_kernel<T, 9><<<n, 256, smem, s>>>(pw, ld_pw, dw, ln_g, ln_b, meta, cg, layer, out, ldo);
+    conv_module_kernel<T, 9><<<n, 512, smem, s>>>(pw, ld_pw, dw, ln_g, ln_b, meta, cg, layer, out, ldo);
 }
 
 template void conv_module<float>(const float*, int, const float*, const float*, const float*, const BatchEntry*, int,

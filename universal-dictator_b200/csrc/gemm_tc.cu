@@ -3,11 +3,13 @@
 // Replaces the reference's gemm2_nt (Sources/DictatorEngine/Metal/12_gemm2.metal:47-123, 32x64 tiles on
 // Apple simdgroup 8x8 MMA) and gemv_nt (11_gemv.metal:45-128) for batched streams, where M = streams x T.
 //
-// Structure (one CTA per SM, 192 threads):
+// Structure (one CTA per SM, 320 threads):
 //   warp 0      TMA producer: A tile 128x64 and W tile BNx64 per stage, 128-byte swizzle, one mbarrier per stage
 //   warp 1      TMEM allocator and single-thread MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per stage,
 //               tcgen05.commit frees the stage; a second commit publishes the finished accumulator
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 16 columns, bias / activation / scale / residual, store
+//   warps 2..9  epilogue: two warps per TMEM lane quadrant (32 rows), each taking half of the tile's columns;
+//               tcgen05.ld 32 lanes x 32 columns, bias / activation / scale / residual (prefetched one chunk
+//               ahead), 16-byte stores
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the epilogue of tile i overlaps the
 // main loop of tile i+1. Every mbarrier wait is bounded; on expiry the kernel records an error code in
 // the engine's device error word, all roles leave their loops, and TMEM is freed before the CTA exits.
@@ -21,7 +23,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
 
 template <int BN>
 struct TcCfg {
@@ -33,40 +36,45 @@ struct TcCfg {
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 };
 
-__device__ __forceinline__ void epilogue_store16(const GemmEpilogue& epi, int row, int col, float* v) {
+// Applies the epilogue to 32 consecutive columns of one row; `r` holds the residual values (if any).
+__device__ __forceinline__ void epilogue_store32(const GemmEpilogue& epi, int row, int col, float* v, const float* r) {
     if (epi.bias) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-            float4 b = *reinterpret_cast<const float4*>(epi.bias + col + j);
+        for (int j = 0; j < 32; j += 4) {
+            const float4 b = *reinterpret_cast<const float4*>(epi.bias + col + j);
             v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
         }
     }
     if (epi.act == ACT_RELU) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], 0.f);
+        for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
     } else if (epi.act == ACT_SILU) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = silu(v[j]);
+        for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] *= epi.out_scale;
+    for (int j = 0; j < 32; ++j) v[j] *= epi.out_scale;
     if (epi.residual) {
-        const float* r = epi.residual + static_cast<size_t>(row) * epi.ldr + col;
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-            float4 x = *reinterpret_cast<const float4*>(r + j);
-            v[j] += epi.res_scale * x.x; v[j + 1] += epi.res_scale * x.y;
-            v[j + 2] += epi.res_scale * x.z; v[j + 3] += epi.res_scale * x.w;
-        }
+        for (int j = 0; j < 32; ++j) v[j] = fmaf(epi.res_scale, r[j], v[j]);
     }
     if (epi.out_bf16) {
         bf16* o = reinterpret_cast<bf16*>(epi.out) + static_cast<size_t>(row) * epi.ldo + col;
-        store16<bf16>(o, v);
-        store16<bf16>(o + 8, v + 8);
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) store16<bf16>(o + j, v + j);
     } else {
         float* o = reinterpret_cast<float*>(epi.out) + static_cast<size_t>(row) * epi.ldo + col;
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) store16<float>(o + j, v + j);
+        for (int j = 0; j < 32; j += 4) store16<float>(o + j, v + j);
+    }
+}
+
+__device__ __forceinline__ void load_residual32(const GemmEpilogue& epi, int row, int col, float* r) {
+    const float* p = epi.residual + static_cast<size_t>(row) * epi.ldr + col;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(p + j);
+        r[j] = x.x; r[j + 1] = x.y; r[j + 2] = x.z; r[j + 3] = x.w;
     }
 }
 
@@ -100,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 4);
+            mbar_init(&acc_empty[a], kEpiWarps);
         }
         *abort_flag = 0;
         fence_mbarrier_init();
@@ -160,7 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_done:;
         }
     } else {
-        const int q = warp & 3;  // TMEM lane quadrant accessible to this warp
+        const int q = warp & 3;                       // TMEM lane quadrant accessible to this warp
+        const int half = (warp - 2) >> 2;             // which half of the tile's columns
+        const int cbeg = half * (BN / 2), cend = cbeg + BN / 2;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -171,12 +181,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const int row = mb * BM + q * 32 + lane;
+            const bool live = row < M;
+            const bool res = epi.residual != nullptr && live;
             const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+            float rnext[32];
+            if (res) load_residual32(epi, row, nb * BN + cbeg, rnext);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
-                float v[16];
-                tmem_ld16(t_row + static_cast<uint32_t>(c0), v);
-                if (row < M) epilogue_store16(epi, row, nb * BN + c0, v);
+            for (int c0 = cbeg; c0 < cend; c0 += 32) {
+                float v[32], rcur[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) rcur[j] = rnext[j];
+                if (res && c0 + 32 < cend) load_residual32(epi, row, nb * BN + c0 + 32, rnext);
+                tmem_ld32(t_row + static_cast<uint32_t>(c0), v);
+                if (live) epilogue_store32(epi, row, nb * BN + c0, v, rcur);
             }
             tc_fence_before();
             __syncwarp();
