@@ -50,11 +50,12 @@ __global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ 
             w1[k] = dw[(c + 1) * KW + k];
         }
 #pragma unroll
-        for (int i = 0; i < R; ++i) {  // frame head - R + i
+        for (int i = 0; i < R; ++i) {  // frame head - R + i, read before any ring row is rewritten
             const float2 v = Pair<T>::ld(ring + ((head + i) % R) * D + c);
             a[i] = v.x;
             bq[i] = v.y;
         }
+        // Pass 1: GLU of every frame (independent loads, all in flight), into ys; the last R frames to the ring.
 #pragma unroll 4
         for (int t = 0; t < T_; ++t) {
             float g0 = 0.f, g1 = 0.f;
@@ -64,8 +65,14 @@ __global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ 
                 g0 = val.x / (1.f + expf(-gate.x));
                 g1 = val.y / (1.f + expf(-gate.y));
             }
-            a[R] = g0;
-            bq[R] = g1;
+            *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(g0, g1);
+            if (t >= T_ - R) Pair<T>::st(ring + ((head + t) % R) * D + c, g0, g1);
+        }
+        // Pass 2: causal depthwise conv over [ring ; new], in place (ys[t] is read before it is overwritten).
+        for (int t = 0; t < T_; ++t) {
+            const float2 gv = *reinterpret_cast<const float2*>(ys + t * D + c);
+            a[R] = gv.x;
+            bq[R] = gv.y;
             float y0 = 0.f, y1 = 0.f;
 #pragma unroll
             for (int k = 0; k < KW; ++k) {
@@ -73,8 +80,6 @@ __global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ 
                 y1 = fmaf(w1[k], bq[k], y1);
             }
             *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(y0, y1);
-            // Ring row (head + t) % R held frame head + t - R, already consumed above.
-            if (t >= T_ - R) Pair<T>::st(ring + ((head + t) % R) * D + c, g0, g1);
 #pragma unroll
             for (int k = 0; k < R; ++k) {
                 a[k] = a[k + 1];

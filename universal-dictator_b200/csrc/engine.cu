@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -125,6 +126,15 @@ struct ud_engine {
     int* err_h = nullptr;
     int64_t launches = 0;
     std::map<std::tuple<const void*, int, int, int>, TmaMatrix> amaps;
+    // CUDA graphs of the steady step, keyed by batch shape; metadata lives in a fixed device buffer for them
+    struct GraphEntry {
+        cudaGraphExec_t exec;
+        int64_t kernels;
+    };
+    bool graphs_on = true;
+    BatchEntry* meta_graph_d = nullptr;
+    std::map<std::tuple<int, int, int, int, int>, GraphEntry> graphs;
+    std::map<std::tuple<int, int, int, int, int>, int> graph_seen;
     // per-kernel-class timing
     bool prof = false;
     std::vector<cudaEvent_t> prof_events;
@@ -344,66 +354,12 @@ ud_status check_ids(ud_engine* e, int n, const ud_stream_id* ids) {
 }
 
 // ---------------------------------------------------------------- the batched step
-ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* in_dev, int rows_stride,
-                    const int* n_rows, const int* valid_rows, const int* keep_all, float* out_dev, int* frames_out,
-                    int32_t* tokens_dev, int* ntok_dev) {
-    if (!e->loaded) return fail(UD_ERR_NOT_READY, "weights not loaded");
-    UD_TRY(check_ids(e, n, ids));
-    if (!n_rows || !valid_rows || !in_dev || !out_dev) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
-    if (tokens_dev && !e->cfg.joint_dim) return fail(UD_ERR_INVALID_ARGUMENT, "no RNN-T head in this configuration");
+// Enqueues every kernel of one batched step on the engine stream (also the body of a captured graph).
+ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tmax_b, int rows_max, const float* in_dev,
+                       int rows_stride, float* out_dev, int32_t* tokens_dev, int* ntok_dev) {
     const bool sub = e->cfg.sub_channels > 0;
-    const int L = e->L, D = e->D;
-    int mi = 0;
-    BatchEntry* mh = next_meta_host(e, &mi);
-    int M = 0, tmax_b = 0, rows_max = 0;
-    for (int i = 0; i < n; ++i) {
-        Slot& s = e->slots[ids[i]];
-        const int nr = n_rows[i], vr = valid_rows[i];
-        if (nr < 1 || nr > rows_stride || nr > e->max_rows_in || vr < 0 || vr > nr)
-            return fail(UD_ERR_INVALID_ARGUMENT, "n_rows/valid_rows out of range for stream " + std::to_string(ids[i]));
-        int drop = 0, T, vt, keep;
-        if (sub) {
-            drop = s.step == 0 ? 0 : 2;
-            T = sub_len(nr) - drop;
-            vt = std::max(0, std::min(sub_len(vr) - drop, T));
-            keep = (keep_all && keep_all[i]) ? vt : std::min(vt, s.lookahead + 1);
-        } else {
-            T = nr;
-            vt = vr;
-            keep = T;
-        }
-        if (T < 1 || T > e->tmax)
-            return fail(UD_ERR_INVALID_ARGUMENT, "chunk of " + std::to_string(T) + " frames outside [1, max_chunk_frames]");
-        BatchEntry& b = mh[i];
-        b.slot = ids[i];
-        b.row_off = M;
-        b.T = T;
-        b.valid_t = vt;
-        b.cache_len = s.cache_len;
-        b.head = s.head;
-        b.drop = drop;
-        b.valid_mel = vr;
-        b.n_rows = nr;
-        b.keep = keep;
-        b.tok_off = i * e->tmax * e->cfg.max_symbols;
-        b.pad = 0;
-        M += T;
-        tmax_b = std::max(tmax_b, T);
-        rows_max = std::max(rows_max, nr);
-    }
-    std::vector<std::pair<Slot*, int>> undo;
-    for (int i = 0; i < n; ++i) {
-        ud_status st = map_pages(e, e->slots[ids[i]], mh[i].T, undo);
-        if (st != UD_OK) {
-            undo_pages(e, undo);
-            return st;
-        }
-        std::memcpy(mh[i].pages, e->slots[ids[i]].pages, sizeof(mh[i].pages));
-    }
-    UD_TRY(upload_meta(e, mi, n));
-    const BatchEntry* md = e->meta_d[mi];
+    const int D = e->D;
     cudaStream_t st = e->stream;
-
     // ---- encoder input: subsampling, or frames as given
     if (sub) {
         const int Tin = rows_max, T1 = nxt(Tin), T2 = nxt(T1), T3 = nxt(T2), C = e->C;
@@ -525,6 +481,109 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
     } else {
         Launch L_(e, UD_KIND_OTHER);
         scatter_rows(e->x, md, n, out_dev, e->tmax, D, st);
+    }
+    return UD_OK;
+}
+
+ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* in_dev, int rows_stride,
+                    const int* n_rows, const int* valid_rows, const int* keep_all, float* out_dev, int* frames_out,
+                    int32_t* tokens_dev, int* ntok_dev, bool graph_ok) {
+    if (!e->loaded) return fail(UD_ERR_NOT_READY, "weights not loaded");
+    UD_TRY(check_ids(e, n, ids));
+    if (!n_rows || !valid_rows || !in_dev || !out_dev) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (tokens_dev && !e->cfg.joint_dim) return fail(UD_ERR_INVALID_ARGUMENT, "no RNN-T head in this configuration");
+    const bool sub = e->cfg.sub_channels > 0;
+    const int L = e->L, D = e->D;
+    int mi = 0;
+    BatchEntry* mh = next_meta_host(e, &mi);
+    int M = 0, tmax_b = 0, rows_max = 0;
+    for (int i = 0; i < n; ++i) {
+        Slot& s = e->slots[ids[i]];
+        const int nr = n_rows[i], vr = valid_rows[i];
+        if (nr < 1 || nr > rows_stride || nr > e->max_rows_in || vr < 0 || vr > nr)
+            return fail(UD_ERR_INVALID_ARGUMENT, "n_rows/valid_rows out of range for stream " + std::to_string(ids[i]));
+        int drop = 0, T, vt, keep;
+        if (sub) {
+            drop = s.step == 0 ? 0 : 2;
+            T = sub_len(nr) - drop;
+            vt = std::max(0, std::min(sub_len(vr) - drop, T));
+            keep = (keep_all && keep_all[i]) ? vt : std::min(vt, s.lookahead + 1);
+        } else {
+            T = nr;
+            vt = vr;
+            keep = T;
+        }
+        if (T < 1 || T > e->tmax)
+            return fail(UD_ERR_INVALID_ARGUMENT, "chunk of " + std::to_string(T) + " frames outside [1, max_chunk_frames]");
+        BatchEntry& b = mh[i];
+        b.slot = ids[i];
+        b.row_off = M;
+        b.T = T;
+        b.valid_t = vt;
+        b.cache_len = s.cache_len;
+        b.head = s.head;
+        b.drop = drop;
+        b.valid_mel = vr;
+        b.n_rows = nr;
+        b.keep = keep;
+        b.tok_off = i * e->tmax * e->cfg.max_symbols;
+        b.pad = 0;
+        M += T;
+        tmax_b = std::max(tmax_b, T);
+        rows_max = std::max(rows_max, nr);
+    }
+    std::vector<std::pair<Slot*, int>> undo;
+    for (int i = 0; i < n; ++i) {
+        ud_status st = map_pages(e, e->slots[ids[i]], mh[i].T, undo);
+        if (st != UD_OK) {
+            undo_pages(e, undo);
+            return st;
+        }
+        std::memcpy(mh[i].pages, e->slots[ids[i]].pages, sizeof(mh[i].pages));
+    }
+    const std::tuple<int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0};
+    const bool use_graph = graph_ok && e->graphs_on && !e->prof;
+    if (!use_graph) {
+        UD_TRY(upload_meta(e, mi, n));
+        UD_TRY(enqueue_step(e, e->meta_d[mi], n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev, ntok_dev));
+    } else {
+        // Metadata for the graph's fixed buffer; the pinned source slot is protected by the ring's event.
+        UD_CK(cudaMemcpyAsync(e->meta_graph_d, mh, sizeof(BatchEntry) * n, cudaMemcpyHostToDevice, e->stream));
+        UD_CK(cudaEventRecord(e->meta_ev[mi], e->stream));
+        e->meta_i = (mi + 1) % ud_engine::kRing;
+        auto it = e->graphs.find(key);
+        if (it == e->graphs.end() && e->graph_seen[key] >= 1) {
+            if (e->graphs.size() >= 16) {
+                for (auto& g : e->graphs) cudaGraphExecDestroy(g.second.exec);
+                e->graphs.clear();
+            }
+            const int64_t before = e->launches;
+            UD_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+            const ud_status cs = enqueue_step(e, e->meta_graph_d, n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev,
+                                              tokens_dev, ntok_dev);
+            cudaGraph_t graph = nullptr;
+            const cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
+            const int64_t kernels = e->launches - before;
+            e->launches = before;
+            if (cs != UD_OK || ce != cudaSuccess) {
+                if (graph) cudaGraphDestroy(graph);
+                cudaGetLastError();
+                return cs != UD_OK ? cs : fail(UD_ERR_CUDA, std::string("stream capture failed: ") + cudaGetErrorString(ce));
+            }
+            cudaGraphExec_t exec = nullptr;
+            const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            if (ie != cudaSuccess) return fail(UD_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+            it = e->graphs.emplace(key, ud_engine::GraphEntry{exec, kernels}).first;
+        }
+        if (it != e->graphs.end()) {
+            UD_CK(cudaGraphLaunch(it->second.exec, e->stream));
+            e->launches += it->second.kernels;
+        } else {
+            e->graph_seen[key] += 1;
+            UD_TRY(enqueue_step(e, e->meta_graph_d, n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev,
+                                ntok_dev));
+        }
     }
     UD_CK(cudaGetLastError());
 
@@ -1063,6 +1122,8 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
         if (cudaEventCreateWithFlags(&e->meta_ev[r], cudaEventDisableTiming) != cudaSuccess)
             return cleanup(fail(UD_ERR_CUDA, "cudaEventCreate failed"));
     }
+    if ((s = dalloc(e, &e->meta_graph_d, meta_n)) != UD_OK) return cleanup(s);
+    if (const char* g = std::getenv("UD_GRAPHS")) e->graphs_on = std::atoi(g) != 0;
     if ((s = halloc(e, &e->slots_h, meta_n)) != UD_OK) return cleanup(s);
     if ((s = dalloc(e, &e->slots_d, meta_n)) != UD_OK) return cleanup(s);
     if ((s = dalloc(e, &e->err_d, 1)) != UD_OK) return cleanup(s);
@@ -1093,6 +1154,7 @@ ud_status ud_shutdown(ud_engine* e) {
     for (int r = 0; r < ud_engine::kRing; ++r)
         if (e->meta_ev[r]) cudaEventDestroy(e->meta_ev[r]);
     for (cudaEvent_t ev : e->prof_events) cudaEventDestroy(ev);
+    for (auto& g : e->graphs) cudaGraphExecDestroy(g.second.exec);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
     return UD_OK;
@@ -1197,8 +1259,29 @@ ud_status ud_step_batch_device(ud_engine* e, int n, const ud_stream_id* ids, con
                                int* frames_out, int32_t* tokens_dev, int* n_tokens_dev) {
     if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
     if (tokens_dev && !n_tokens_dev) return fail(UD_ERR_INVALID_ARGUMENT, "n_tokens_dev is NULL");
-    return run_batch(e, n, ids, mel_dev, rows_stride, n_rows, valid_rows, keep_all, proj_dev, frames_out, tokens_dev,
-                     n_tokens_dev);
+    if (!mel_dev || !proj_dev || !n_rows) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (n < 1 || n > e->cfg.max_batch) return fail(UD_ERR_INVALID_ARGUMENT, "batch size out of range");
+    UD_CK(cudaSetDevice(e->device));
+    int rows_max = 1;
+    for (int i = 0; i < n; ++i) {
+        if (n_rows[i] < 1 || n_rows[i] > e->max_rows_in || n_rows[i] > rows_stride)
+            return fail(UD_ERR_INVALID_ARGUMENT, "n_rows out of range");
+        rows_max = std::max(rows_max, n_rows[i]);
+    }
+    // Stage the input into the engine's fixed buffer (the step, or its captured graph, reads it from there).
+    const size_t W = e->in_width;
+    UD_CK(cudaMemcpy2DAsync(e->in_stage, sizeof(float) * W * e->max_rows_in, mel_dev, sizeof(float) * W * rows_stride,
+                            sizeof(float) * W * rows_max, n, cudaMemcpyDeviceToDevice, e->stream));
+    UD_TRY(run_batch(e, n, ids, e->in_stage, e->max_rows_in, n_rows, valid_rows, keep_all, e->out_stage, frames_out,
+                     tokens_dev ? e->tok_dev : nullptr, e->ntok_dev, true));
+    UD_CK(cudaMemcpyAsync(proj_dev, e->out_stage, sizeof(float) * n * e->tmax * e->out_width, cudaMemcpyDeviceToDevice,
+                          e->stream));
+    if (tokens_dev) {
+        UD_CK(cudaMemcpyAsync(tokens_dev, e->tok_dev, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols,
+                              cudaMemcpyDeviceToDevice, e->stream));
+        UD_CK(cudaMemcpyAsync(n_tokens_dev, e->ntok_dev, sizeof(int) * n, cudaMemcpyDeviceToDevice, e->stream));
+    }
+    return UD_OK;
 }
 
 ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* const* mel, const int* n_rows,
@@ -1208,22 +1291,24 @@ ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const floa
     if (n < 1 || n > e->cfg.max_batch) return fail(UD_ERR_INVALID_ARGUMENT, "batch size out of range");
     if (tokens_out && !n_tokens_out) return fail(UD_ERR_INVALID_ARGUMENT, "n_tokens_out is NULL");
     UD_CK(cudaSetDevice(e->device));
-    int stride = 1;
+    const int stride = e->max_rows_in;
+    int rows_max = 1;
     for (int i = 0; i < n; ++i) {
         if (!mel[i]) return fail(UD_ERR_INVALID_ARGUMENT, "NULL input rows");
         if (n_rows[i] < 1 || n_rows[i] > e->max_rows_in)
             return fail(UD_ERR_INVALID_ARGUMENT, "n_rows out of range");
-        stride = std::max(stride, n_rows[i]);
+        rows_max = std::max(rows_max, n_rows[i]);
     }
     const int W = e->in_width;
     // The pinned staging buffer may still be read by a previous asynchronous call.
     UD_CK(cudaStreamSynchronize(e->stream));
     for (int i = 0; i < n; ++i)
         std::memcpy(e->h_in + static_cast<size_t>(i) * stride * W, mel[i], sizeof(float) * n_rows[i] * W);
-    UD_CK(cudaMemcpyAsync(e->in_stage, e->h_in, sizeof(float) * n * stride * W, cudaMemcpyHostToDevice, e->stream));
+    UD_CK(cudaMemcpy2DAsync(e->in_stage, sizeof(float) * W * stride, e->h_in, sizeof(float) * W * stride,
+                            sizeof(float) * W * rows_max, n, cudaMemcpyHostToDevice, e->stream));
     std::vector<int> frames(n);
     UD_TRY(run_batch(e, n, ids, e->in_stage, stride, n_rows, valid_rows, keep_all, e->out_stage, frames.data(),
-                     tokens_out ? e->tok_dev : nullptr, e->ntok_dev));
+                     tokens_out ? e->tok_dev : nullptr, e->ntok_dev, true));
     const size_t out_n = static_cast<size_t>(n) * e->tmax * e->out_width;
     UD_CK(cudaMemcpyAsync(e->h_out, e->out_stage, sizeof(float) * out_n, cudaMemcpyDeviceToHost, e->stream));
     if (tokens_out) {

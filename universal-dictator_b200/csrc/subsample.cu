@@ -16,66 +16,83 @@ namespace {
 
 __device__ __forceinline__ int nxt(int t) { return t / 2 + 1; }
 
+// One CTA per (stream, output row): the three input mel rows and all taps in shared memory, a thread per
+// (output frequency, 8-channel group), 16-byte stores of the channel-last output.
 template <typename T>
-__global__ void conv0_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
-                             const BatchEntry* __restrict__ meta, int Tin, const float* __restrict__ w,
-                             const float* __restrict__ bias, T* __restrict__ out, int T1, int F1, int C) {
-    extern __shared__ float xs[];  // [3][mel_bins + 3], frequency index shifted by the left pad of 2
+__global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
+                                                    const BatchEntry* __restrict__ meta, int Tin,
+                                                    const float* __restrict__ w, const float* __restrict__ bias,
+                                                    T* __restrict__ out, int T1, int F1, int C) {
+    constexpr int VW = Vec16<T>::N;
+    extern __shared__ float sm0[];
+    float* xs = sm0;                        // [3][mel_bins + 3], frequency index shifted by the left pad of 2
+    const int W = mel_bins + 3;
+    float* ws = xs + 3 * W;                 // [9][C] taps, channel fastest
+    float* bs = ws + 9 * C;                 // [C]
     const int b = blockIdx.x, t = blockIdx.y;
     const int vm = meta[b].valid_mel;
     const int v1 = nxt(vm);
-    const int W = mel_bins + 3;
     for (int i = threadIdx.x; i < 3 * W; i += blockDim.x) {
         const int r = i / W, q = i % W - 2;
         const int row = 2 * t - 2 + r;
         const bool ok = row >= 0 && row < vm && row < Tin && q >= 0 && q < mel_bins;
         xs[i] = ok ? mel[(static_cast<size_t>(b) * rows_stride + row) * mel_bins + q] : 0.f;
     }
+    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x) ws[(i % 9) * C + i / 9] = w[i];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) bs[i] = bias[i];
     __syncthreads();
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float wc[9];
+    const int groups = C / VW;
+    T* orow = out + (static_cast<size_t>(b) * T1 + t) * F1 * C;
+    for (int idx = threadIdx.x; idx < F1 * groups; idx += blockDim.x) {
+        const int f = idx / groups, c = (idx % groups) * VW;
+        float acc[VW];
 #pragma unroll
-        for (int k = 0; k < 9; ++k) wc[k] = w[c * 9 + k];
-        const float bc = bias[c];
-        T* o = out + (static_cast<size_t>(b) * T1 + t) * F1 * C + c;
-        for (int f = 0; f < F1; ++f) {
-            float acc = bc;
+        for (int e = 0; e < VW; ++e) acc[e] = bs[c + e];
 #pragma unroll
-            for (int kh = 0; kh < 3; ++kh)
+        for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
-                for (int kw = 0; kw < 3; ++kw) acc = fmaf(wc[kh * 3 + kw], xs[kh * W + 2 * f + kw], acc);
-            o[static_cast<size_t>(f) * C] = from_f<T>(t < v1 ? fmaxf(acc, 0.f) : 0.f);
-        }
+            for (int kw = 0; kw < 3; ++kw) {
+                const float xv = xs[kh * W + 2 * f + kw];
+#pragma unroll
+                for (int e = 0; e < VW; ++e) acc[e] = fmaf(ws[(kh * 3 + kw) * C + c + e], xv, acc[e]);
+            }
+#pragma unroll
+        for (int e = 0; e < VW; ++e) acc[e] = t < v1 ? fmaxf(acc[e], 0.f) : 0.f;
+        store16<T>(orow + static_cast<size_t>(f) * C + c, acc);
     }
 }
 
+// One CTA per (stream, output row); a thread per (output frequency, 8-channel group), 16-byte loads.
 template <typename T>
-__global__ void dwconv_kernel(const T* __restrict__ in, int Tin, int Fin, int stage,
-                              const BatchEntry* __restrict__ meta, const float* __restrict__ w,
-                              const float* __restrict__ bias, T* __restrict__ out, int Tout, int Fout, int C) {
+__global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, int Tin, int Fin, int stage,
+                                                     const BatchEntry* __restrict__ meta, const float* __restrict__ w,
+                                                     const float* __restrict__ bias, T* __restrict__ out, int Tout,
+                                                     int Fout, int C) {
+    constexpr int VW = Vec16<T>::N;
     const int b = blockIdx.x, t = blockIdx.y;
     const int v1 = nxt(meta[b].valid_mel);
     const int vin = stage == 1 ? v1 : nxt(v1);
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float wc[9];
+    const int groups = C / VW;
+    for (int idx = threadIdx.x; idx < Fout * groups; idx += blockDim.x) {
+        const int f = idx / groups, c = (idx % groups) * VW;
+        float acc[VW];
 #pragma unroll
-        for (int k = 0; k < 9; ++k) wc[k] = w[c * 9 + k];
-        const float bc = bias[c];
-        for (int f = 0; f < Fout; ++f) {
-            float acc = bc;
+        for (int e = 0; e < VW; ++e) acc[e] = bias[c + e];
 #pragma unroll
-            for (int kh = 0; kh < 3; ++kh) {
-                const int r = 2 * t + kh - 2;
-                if (r < 0 || r >= Tin || r >= vin) continue;
+        for (int kh = 0; kh < 3; ++kh) {
+            const int r = 2 * t + kh - 2;
+            if (r < 0 || r >= Tin || r >= vin) continue;
 #pragma unroll
-                for (int kw = 0; kw < 3; ++kw) {
-                    const int q = 2 * f + kw - 2;
-                    if (q < 0 || q >= Fin) continue;
-                    acc = fmaf(wc[kh * 3 + kw], to_f<T>(in[((static_cast<size_t>(b) * Tin + r) * Fin + q) * C + c]), acc);
-                }
+            for (int kw = 0; kw < 3; ++kw) {
+                const int q = 2 * f + kw - 2;
+                if (q < 0 || q >= Fin) continue;
+                float x[VW];
+                load16<T>(in + ((static_cast<size_t>(b) * Tin + r) * Fin + q) * C + c, x);
+#pragma unroll
+                for (int e = 0; e < VW; ++e) acc[e] = fmaf(w[(c + e) * 9 + kh * 3 + kw], x[e], acc[e]);
             }
-            out[((static_cast<size_t>(b) * Tout + t) * Fout + f) * C + c] = from_f<T>(acc);
         }
+        store16<T>(out + ((static_cast<size_t>(b) * Tout + t) * Fout + f) * C + c, acc);
     }
 }
 
@@ -120,8 +137,8 @@ template <typename T>
 void sub_conv0(const float* mel, int rows_stride, int mel_bins, const BatchEntry* meta, int n, int Tin, const float* w,
                const float* b, T* out, int T1, int F1, int C, cudaStream_t s) {
     dim3 grid(n, T1);
-    conv0_kernel<T><<<grid, 256, sizeof(float) * 3 * (mel_bins + 3), s>>>(mel, rows_stride, mel_bins, meta, Tin, w, b,
-                                                                         out, T1, F1, C);
+    const size_t smem = sizeof(float) * (3 * (mel_bins + 3) + 10 * C);
+    conv0_kernel<T><<<grid, 256, smem, s>>>(mel, rows_stride, mel_bins, meta, Tin, w, b, out, T1, F1, C);
 }
 
 template <typename T>
