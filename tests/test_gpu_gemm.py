@@ -5,6 +5,8 @@ tolerance 1e-4*sqrt(K) + 1e-5 absolute on inputs in [-1, 1) (`:43`), full epilog
 scale, residual with scale, `:66-91`). The engine shapes (M = streams x T up to 3584, N in {256, 640, 1024, 2048,
 3072, 4096}, K in {256, 1024, 4096, 4352}) exercise both tcgen05 tile widths (BN 128 and 256)."""
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -18,10 +20,17 @@ TC_SHAPES = [(17, 256, 256), (129, 640, 1024), (200, 3072, 1024), (333, 2048, 10
              (1024, 4096, 1024), (3584, 1024, 4096), (3584, 4096, 1024)]
 
 
-@pytest.fixture(scope="module", params=[ud.DTYPE_BF16, ud.DTYPE_F32], ids=["bf16", "f32"])
+@pytest.fixture(scope="module", params=["bf16", "bf16-1cta", "f32"])
 def eng(request):
-    e = ud.Engine(ud.default_config(n_layers=0, sub_channels=0, joint_dim=0, max_streams=1, max_batch=1,
-                                    dtype=request.param))
+    """bf16: tcgen05 with 2-CTA pairs where M >= 256 and N % 256 == 0; bf16-1cta: the one-CTA kernel only;
+    f32: the FFMA kernels."""
+    if request.param == "bf16-1cta":
+        os.environ["UD_TC2"] = "0"
+    try:
+        e = ud.Engine(ud.default_config(n_layers=0, sub_channels=0, joint_dim=0, max_streams=1, max_batch=1,
+                                        dtype=ud.DTYPE_F32 if request.param == "f32" else ud.DTYPE_BF16))
+    finally:
+        os.environ.pop("UD_TC2", None)
     yield e
     e.close()
 

@@ -242,26 +242,31 @@ __device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b
 }
 
 struct Lay {
-    int nkp, npp, psw;  // padded key rows (x16), padded position rows (x16), softmax-row stride
+    int nkp, npp, psw, acw, bdw;  // padded key rows (x16), padded position rows (x16), row strides
     size_t qu, qv, k, v, p, ac, bd, pb, total;
     __host__ __device__ Lay(int L) {
         nkp = (L + TM + 15) / 16 * 16;
         npp = (TM + L + TM - 1 + 15) / 16 * 16;
         psw = nkp + 8;
+        acw = nkp + 8;   // == 8 (mod 32) for 16-multiples of 32k+... : float2 stores of the mma D fragment are
+        bdw = npp + 8;   // conflict-free per half-warp when the row stride is 8 or 24 (mod 32)
         size_t o = 0;
         qu = o; o += sizeof(bf16) * TM * RSB;
         qv = o; o += sizeof(bf16) * TM * RSB;
         k = o;  o += sizeof(bf16) * nkp * RSB;
         v = o;  o += sizeof(bf16) * nkp * RSB;
         p = o;  o += sizeof(bf16) * npp * RSB;
-        ac = o; o += sizeof(float) * TM * nkp;
-        bd = o; o += sizeof(float) * TM * npp;
+        ac = o; o += sizeof(float) * TM * acw;
+        bd = o; o += sizeof(float) * TM * bdw;
         pb = o; o += sizeof(bf16) * TM * psw;
         total = (o + 127) / 128 * 128;
     }
 };
 
-__global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ qkv, int ld_qkv,
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+
+__global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __restrict__ qkv, int ld_qkv,
                                                       const bf16* __restrict__ ptab, int tmax,
                                                       const float* __restrict__ bias_u,
                                                       const float* __restrict__ bias_v,
@@ -290,22 +295,15 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ q
     float* BD = reinterpret_cast<float*>(sm + lay.bd);
     bf16* Pb = reinterpret_cast<bf16*>(sm + lay.pb);
 
-    // ---- stage K, V (visible window) and P rows with cp.async; zero the padding rows.
+    // ---- stage K and P (group 0) and V (group 1) with cp.async; zero the padding rows.
     const bf16* kpool = reinterpret_cast<const bf16*>(cg.kpool);
     const bf16* vpool = reinterpret_cast<const bf16*>(cg.vpool);
-    for (int idx = tid; idx < nk * 16; idx += 128) {
-        const int r = idx >> 4, c = (idx & 15) * 8;
+    auto key_src = [&](int r, int c, const bf16*& ks, const bf16*& vs) -> bool {
         const int j = lo + r;
-        const bf16 *ks, *vs;
         if (j < L) {
             const int f = head - L + j;
             const int page = me.pages[(f / PF) % kPageSlots];
-            if (page < 0 || page >= cg.n_pages) {
-                report_error(err, DEV_BAD_PAGE);
-                *reinterpret_cast<uint4*>(Ks + r * RSB + c) = make_uint4(0u, 0u, 0u, 0u);
-                *reinterpret_cast<uint4*>(Vs + r * RSB + c) = make_uint4(0u, 0u, 0u, 0u);
-                continue;
-            }
+            if (page < 0 || page >= cg.n_pages) return false;
             const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
             ks = kpool + off;
             vs = vpool + off;
@@ -314,25 +312,45 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ q
             ks = src + D;
             vs = src + 2 * D;
         }
+        return true;
+    };
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int idx = tid; idx < nk * 16; idx += kAttnThreads) {
+        const int r = idx >> 4, c = (idx & 15) * 8;
+        const bf16 *ks, *vs;
+        if (!key_src(r, c, ks, vs)) {
+            report_error(err, DEV_BAD_PAGE);
+            *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
+            continue;
+        }
         cp_async16(Ks + r * RSB + c, ks);
-        cp_async16(Vs + r * RSB + c, vs);
     }
-    for (int idx = tid; idx < np * 16; idx += 128) {
+    for (int idx = tid; idx < np * 16; idx += kAttnThreads) {
         const int r = idx >> 4, c = (idx & 15) * 8;
         cp_async16(Ps + r * RSB + c, ptab + static_cast<size_t>(rel_min + r + tmax - 1) * D + hoff + c);
     }
-    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-    for (int idx = tid; idx < (lay.nkp - nk) * 16; idx += 128) {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int idx = tid; idx < nk * 16; idx += kAttnThreads) {
+        const int r = idx >> 4, c = (idx & 15) * 8;
+        const bf16 *ks, *vs;
+        if (!key_src(r, c, ks, vs)) {
+            *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
+            continue;
+        }
+        cp_async16(Vs + r * RSB + c, vs);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int idx = tid; idx < (lay.nkp - nk) * 16; idx += kAttnThreads) {
         const int r = nk + (idx >> 4), c = (idx & 15) * 8;
         *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
         *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
     }
-    for (int idx = tid; idx < (lay.npp - np) * 16; idx += 128) {
+    for (int idx = tid; idx < (lay.npp - np) * 16; idx += kAttnThreads) {
         const int r = np + (idx >> 4), c = (idx & 15) * 8;
         *reinterpret_cast<uint4*>(Ps + r * RSB + c) = z;
     }
     // queries with the position biases, rounded to bf16 (rows >= T are zero)
-    for (int idx = tid; idx < TM * 16; idx += 128) {
+    for (int idx = tid; idx < TM * 16; idx += kAttnThreads) {
         const int i = idx >> 4, c = (idx & 15) * 8;
         float q[8];
         if (i < T_) {
@@ -350,7 +368,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ q
         store16<bf16>(QU + i * RSB + c, a);
         store16<bf16>(QV + i * RSB + c, bb);
     }
-    cp_async_wait_all();
+    asm volatile("cp.async.wait_group 1;" ::: "memory");   // K and P have landed; V may still be in flight
     __syncthreads();
 
     // ---- AC and BDraw: jobs of two n-tiles (16 columns), round-robin over the 4 warps.
@@ -365,7 +383,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ q
         const int n_ac = (nk + 15) / 16, n_bd = (np + 15) / 16;
         const int g = lane >> 2, t4 = lane & 3;
         const int brow = (lane & 7) + ((lane >> 4) << 3), bcol = ((lane >> 3) & 1) * 8;
-        for (int job = warp; job < n_ac + n_bd; job += 4) {
+        for (int job = warp; job < n_ac + n_bd; job += kAttnWarps) {
             const bool is_ac = job < n_ac;
             const int n0 = (is_ac ? job : job - n_ac) * 16;
             const bf16* Bs = is_ac ? Ks : Ps;
@@ -379,63 +397,74 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ q
                 mma16816(c1, a, bfr[2], bfr[3]);
             }
             float* dst = is_ac ? AC : BD;
-            const int w = is_ac ? lay.nkp : lay.npp;
-            dst[g * w + n0 + 2 * t4] = c0[0];
-            dst[g * w + n0 + 2 * t4 + 1] = c0[1];
-            dst[(g + 8) * w + n0 + 2 * t4] = c0[2];
-            dst[(g + 8) * w + n0 + 2 * t4 + 1] = c0[3];
-            dst[g * w + n0 + 8 + 2 * t4] = c1[0];
-            dst[g * w + n0 + 8 + 2 * t4 + 1] = c1[1];
-            dst[(g + 8) * w + n0 + 8 + 2 * t4] = c1[2];
-            dst[(g + 8) * w + n0 + 8 + 2 * t4 + 1] = c1[3];
+            const int w = is_ac ? lay.acw : lay.bdw;
+            *reinterpret_cast<float2*>(dst + g * w + n0 + 2 * t4) = make_float2(c0[0], c0[1]);
+            *reinterpret_cast<float2*>(dst + (g + 8) * w + n0 + 2 * t4) = make_float2(c0[2], c0[3]);
+            *reinterpret_cast<float2*>(dst + g * w + n0 + 8 + 2 * t4) = make_float2(c1[0], c1[1]);
+            *reinterpret_cast<float2*>(dst + (g + 8) * w + n0 + 8 + 2 * t4) = make_float2(c1[2], c1[3]);
         }
     }
     __syncthreads();
 
     // ---- softmax rows (fp32), probabilities to bf16
     const float scale = rsqrtf(static_cast<float>(DKk));
-    for (int i = warp; i < TM; i += 4) {
+    for (int i = warp; i < TM; i += kAttnWarps) {
         bf16* prow = Pb + i * lay.psw;
         if (i >= T_ || nk == 0) {
             for (int jj = lane; jj < lay.nkp; jj += 32) prow[jj] = __float2bfloat16_rn(0.f);
             continue;
         }
-        const float* acr = AC + i * lay.nkp;
-        const float* bdr = BD + i * lay.npp + i + nk - 1;   // BDraw column for key jj is (i + nk - 1 - jj)
+        const float* acr = AC + i * lay.acw;
+        const float* bdr = BD + i * lay.bdw + i + nk - 1;   // BDraw column for key jj is (i + nk - 1 - jj)
+        constexpr int kPer = 4;                              // nkp <= 128 keys: at most 4 per lane
+        float sv[kPer];
         float m = -INFINITY;
-        for (int jj = lane; jj < nk; jj += 32) m = fmaxf(m, (acr[jj] + bdr[-jj]) * scale);
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int jj = lane + 32 * u;
+            sv[u] = jj < nk ? (acr[jj] + bdr[-jj]) * scale : -INFINITY;
+            m = fmaxf(m, sv[u]);
+        }
         m = warp_max(m);
         float sum = 0.f;
-        for (int jj = lane; jj < nk; jj += 32) sum += expf((acr[jj] + bdr[-jj]) * scale - m);
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int jj = lane + 32 * u;
+            sv[u] = jj < nk ? __expf(sv[u] - m) : 0.f;
+            sum += sv[u];
+        }
         sum = warp_sum(sum);
         const float inv = 1.f / sum;
-        for (int jj = lane; jj < lay.nkp; jj += 32)
-            prow[jj] = __float2bfloat16_rn(jj < nk ? expf((acr[jj] + bdr[-jj]) * scale - m) * inv : 0.f);
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int jj = lane + 32 * u;
+            if (jj < lay.nkp) prow[jj] = __float2bfloat16_rn(sv[u] * inv);
+        }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");   // V
     __syncthreads();
 
-    // ---- O = P . V: warp w owns output columns [32w, 32w + 32)
+    // ---- O = P . V: warp w owns output columns [16w, 16w + 16)
     {
-        float acc[4][4] = {};
+        float acc[2][4] = {};
         const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
         const int vrow = (lane & 7) + ((lane >> 3) & 1) * 8, vcol = (lane >> 4) * 8;
         const int ksteps = (nk + 15) / 16;
         for (int ks = 0; ks < ksteps; ++ks) {
             uint32_t a[4];
             ldsm_x4(a, Pb + arow * lay.psw + ks * 16 + acol);
-#pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-                const int n0 = warp * 32 + pr * 16;
+            {
+                const int n0 = warp * 16;
                 uint32_t bfr[4];
                 ldsm_x4_t(bfr, Vs + (ks * 16 + vrow) * RSB + n0 + vcol);
-                mma16816(acc[pr * 2], a, bfr[0], bfr[1]);
-                mma16816(acc[pr * 2 + 1], a, bfr[2], bfr[3]);
+                mma16816(acc[0], a, bfr[0], bfr[1]);
+                mma16816(acc[1], a, bfr[2], bfr[3]);
             }
         }
         const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const int col = hoff + warp * 32 + nt * 8 + 2 * t4;
+        for (int nt = 0; nt < 2; ++nt) {
+            const int col = hoff + warp * 16 + nt * 8 + 2 * t4;
             if (g < T_)
                 *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g) * ldo + col) =
                     __floats2bfloat162_rn(acc[nt][0], acc[nt][1]);
@@ -448,7 +477,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const bf16* __restrict__ q
     // ---- append this chunk's K/V rows at frames head + t
     bf16* kw = reinterpret_cast<bf16*>(cg.kpool);
     bf16* vw = reinterpret_cast<bf16*>(cg.vpool);
-    for (int idx = tid; idx < T_ * 16; idx += 128) {
+    for (int idx = tid; idx < T_ * 16; idx += kAttnThreads) {
         const int t = idx >> 4, c = (idx & 15) * 8;
         const int f = head + t;
         const int page = me.pages[(f / PF) % kPageSlots];
@@ -473,7 +502,7 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
                       int n_heads, int* dev_err, cudaStream_t s) {
     if (n <= 0) return;
     if constexpr (std::is_same<T, bf16>::value) {
-        if (tmax_batch <= tc::TM) {
+        if (tmax_batch <= tc::TM && cg.L + tc::TM <= 128) {
             const tc::Lay lay(cg.L);
             static size_t tc_attr = 0;
             if (lay.total > tc_attr) {
@@ -482,7 +511,7 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
                 tc_attr = lay.total;
             }
             dim3 grid(n, n_heads);
-            tc::attn_tc_kernel<<<grid, 128, lay.total, s>>>(qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer,
+            tc::attn_tc_kernel<<<grid, tc::kAttnThreads, lay.total, s>>>(qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer,
                                                             out, ldo, dev_err);
             return;
         }

@@ -132,6 +132,7 @@ struct ud_engine {
         int64_t kernels;
     };
     bool graphs_on = true;
+    bool tc2_on = true;  // 2-CTA tcgen05 tiles for M >= 256, N % 256 == 0
     BatchEntry* meta_graph_d = nullptr;
     std::map<std::tuple<int, int, int, int, int>, GraphEntry> graphs;
     std::map<std::tuple<int, int, int, int, int>, int> graph_seen;
@@ -244,8 +245,13 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
                     return fail(UD_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
                 it = e->amaps.emplace(key, t).first;
             }
-            const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;
-            gemm_tc(it->second, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms, e->stream);
+            if (e->tc2_on && M >= 256 && W.N % 256 == 0) {
+                gemm_tc2(it->second, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, e->stream);
+            } else {
+                const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;
+                gemm_tc(it->second, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms,
+                        e->stream);
+            }
         }
     } else {
         gemm_simt<float, float>(static_cast<const float*>(A), lda, static_cast<const float*>(W.p), M, W.N, W.K, epi,
@@ -1124,6 +1130,7 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
     }
     if ((s = dalloc(e, &e->meta_graph_d, meta_n)) != UD_OK) return cleanup(s);
     if (const char* g = std::getenv("UD_GRAPHS")) e->graphs_on = std::atoi(g) != 0;
+    if (const char* g = std::getenv("UD_TC2")) e->tc2_on = std::atoi(g) != 0;
     if ((s = halloc(e, &e->slots_h, meta_n)) != UD_OK) return cleanup(s);
     if ((s = dalloc(e, &e->slots_d, meta_n)) != UD_OK) return cleanup(s);
     if ((s = dalloc(e, &e->err_d, 1)) != UD_OK) return cleanup(s);

@@ -1,0 +1,263 @@
+// Persistent 2-CTA tcgen05 GEMM (cta_group::2) for sm_100a: the same C = epilogue(A . W^T) contract as
+// gemm_tc.cu, with each CTA pair of a cluster computing a 256 x BN tile.
+//
+// Per pair and stage (64 along K): CTA r stages rows [128 r, 128 r + 128) of the A tile and rows
+// [BN/2 r, BN/2 (r+1)) of the W tile in its own shared memory (TMA, 128-byte swizzle). Both CTAs' loads complete
+// on the leader's (rank 0) stage barrier; the leader's single MMA thread issues tcgen05.mma.cta_group::2
+// (M = 256, N = BN, K = 16), which reads A and W halves from both CTAs and accumulates each CTA's 128 rows in
+// its own TMEM. Commits signal both CTAs' stage-free and accumulator-ready barriers; each CTA's 8 epilogue warps
+// drain their TMEM rows and report back to the leader. Per CTA and stage that is 32 KB of shared memory for
+// 128 x BN x 64 multiply-adds: half the operand bytes per FLOP of the one-CTA kernel, so six stages cover the
+// TMA round trip. Every wait is bounded, as in gemm_tc.cu.
+#include "common.cuh"
+#include "gemm_epi.cuh"
+#include "kernels.h"
+
+namespace ud {
+namespace {
+
+constexpr int BM2 = 256;  // rows per CTA pair
+constexpr int BK = 64;
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+
+template <int BN>
+struct Tc2Cfg {
+    static constexpr int STAGES = 6;
+    static constexpr int A_BYTES = 128 * BK * 2;        // this CTA's half of the A tile
+    static constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on the (possibly peer) barrier.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                                                 int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tc2_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives on the barrier at this offset in both CTAs of the pair once the issued MMAs complete.
+__device__ __forceinline__ void tc2_commit_both(uint64_t* bar) {
+    const uint16_t mask = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(mask)
+        : "memory");
+}
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW, int M, int N,
+                    int K, const GemmEpilogue epi, int* err) {
+    using C = Tc2Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);  // used in the leader
+    uint64_t* empty = full + C::STAGES;
+    uint64_t* acc_full = empty + C::STAGES;
+    uint64_t* acc_empty = acc_full + 2;                                                  // used in the leader
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    volatile int* abort_v = abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    const int num_m = (M + BM2 - 1) / BM2;
+    const int num_tiles = num_m * (N / BN);
+    const int num_kb = K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 2 * kEpiWarps);
+        }
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        prefetch_tensormap(&mapA);
+        prefetch_tensormap(&mapW);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(C::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+                const int mb = tile % num_m, nb = tile / num_m;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, DEV_TIMEOUT_EMPTY, abort_v)) goto producer_done;
+                    const uint32_t leader_full = peer_addr(smem_u32(&full[stage]), 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+                    tma_load_2d_pair(sA + stage * C::A_BYTES, &mapA, leader_full, kb * BK, mb * BM2 + rank * 128);
+                    tma_load_2d_pair(sB + stage * C::B_BYTES, &mapW, leader_full, kb * BK, nb * BN + rank * (BN / 2));
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+        producer_done:;
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = idesc_bf16_f32(BM2, BN);
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+                if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, err, DEV_TIMEOUT_ACC_EMPTY, abort_v)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_bounded(&full[stage], phase, err, DEV_TIMEOUT_FULL, abort_v)) goto mma_done;
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+                    const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        tc2_mma_bf16(d_tmem, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
+                                     (kb | k) != 0 ? 1u : 0u);
+                    }
+                    tc2_commit_both(&empty[stage]);
+                    if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+                }
+                tc2_commit_both(&acc_full[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+        mma_done:;
+        }
+    } else {
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int cbeg = half * (BN / 2), cend = cbeg + BN / 2;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+            const int mb = tile % num_m, nb = tile / num_m;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait_bounded(&acc_full[acc], acc_phase, err, DEV_TIMEOUT_ACC_FULL, abort_v) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const int row = mb * BM2 + static_cast<int>(rank) * 128 + q * 32 + lane;
+            const bool live = row < M;
+            const bool res = epi.residual != nullptr && live;
+            const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+            float rnext[32];
+            if (res) load_residual32(epi, row, nb * BN + cbeg, rnext);
+#pragma unroll 1
+            for (int c0 = cbeg; c0 < cend; c0 += 32) {
+                float v[32], rcur[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) rcur[j] = rnext[j];
+                if (res && c0 + 32 < cend) load_residual32(epi, row, nb * BN + c0 + 32, rnext);
+                tmem_ld32(t_row + static_cast<uint32_t>(c0), v);
+                if (live) epilogue_store32(epi, row, nb * BN + c0, v, rcur);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(peer_addr(smem_u32(&acc_empty[acc]), 0));
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();  // no CTA frees TMEM while its peer's MMAs or epilogue may still touch the pair's state
+    if (*abort_v) __nanosleep(100000);
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
+                     : "memory");
+    }
+}
+
+template <int BN>
+void launch2(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const GemmEpilogue& epi, int* err,
+             int num_sms, cudaStream_t s) {
+    using C = Tc2Cfg<BN>;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(gemm_tc2_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        attr = true;
+    }
+    // Persistent grid: no more pairs than can be resident at once (clusters are placed within GPCs).
+    static int max_pairs = -1;
+    if (max_pairs < 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(num_sms, 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BN>, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = num_sms / 2;
+        }
+        max_pairs = n < num_sms / 2 ? n : num_sms / 2;
+    }
+    const int tiles = ((M + BM2 - 1) / BM2) * (N / BN);
+    const int pairs = tiles < max_pairs ? tiles : max_pairs;
+    gemm_tc2_kernel<BN><<<2 * pairs, kThreads, C::SMEM, s>>>(A.map, W.map, M, N, K, epi, err);
+}
+
+}  // namespace
+
+void gemm_tc2(const TmaMatrix& A, const TmaMatrix& W_half, int M, int N, int K, int bn, const GemmEpilogue& epi,
+              int* dev_err, int num_sms, cudaStream_t s) {
+    if (bn == 256)
+        launch2<256>(A, W_half, M, N, K, epi, dev_err, num_sms, s);
+    else
+        launch2<128>(A, W_half, M, N, K, epi, dev_err, num_sms, s);
+}
+
+}  // namespace ud

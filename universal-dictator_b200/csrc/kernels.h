@@ -38,6 +38,11 @@ int gemm_tc_pick_bn(int M, int N, int num_sms);
 void gemm_tc(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, int bn, const GemmEpilogue& epi,
              int* dev_err, int num_sms, cudaStream_t s);
 
+// 2-CTA variant (cluster of 2, cta_group::2), 256 x bn tiles per CTA pair; bn must be 256 and W's tensor map
+// must have 128-row boxes (each CTA loads half of the W tile). M >= 256 recommended.
+void gemm_tc2(const TmaMatrix& A, const TmaMatrix& W_half, int M, int N, int K, int bn, const GemmEpilogue& epi,
+              int* dev_err, int num_sms, cudaStream_t s);
+
 // ---- SIMT GEMM for few rows (M small) and for the fp32 engine. TA/TW in {float, bf16}.
 template <typename TA, typename TW>
 void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s);

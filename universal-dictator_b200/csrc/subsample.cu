@@ -16,19 +16,16 @@ namespace {
 
 __device__ __forceinline__ int nxt(int t) { return t / 2 + 1; }
 
-// One CTA per (stream, output row): the three input mel rows and all taps in shared memory, a thread per
-// (output frequency, 8-channel group), 16-byte stores of the channel-last output.
+// One CTA per (stream, output row). Each thread owns one 8-channel group (its 72 taps in registers) and steps
+// over output frequencies; the three input mel rows sit in shared memory and are read as broadcasts.
 template <typename T>
 __global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
                                                     const BatchEntry* __restrict__ meta, int Tin,
                                                     const float* __restrict__ w, const float* __restrict__ bias,
                                                     T* __restrict__ out, int T1, int F1, int C) {
     constexpr int VW = Vec16<T>::N;
-    extern __shared__ float sm0[];
-    float* xs = sm0;                        // [3][mel_bins + 3], frequency index shifted by the left pad of 2
+    extern __shared__ float xs[];           // [3][mel_bins + 3], frequency index shifted by the left pad of 2
     const int W = mel_bins + 3;
-    float* ws = xs + 3 * W;                 // [9][C] taps, channel fastest
-    float* bs = ws + 9 * C;                 // [C]
     const int b = blockIdx.x, t = blockIdx.y;
     const int vm = meta[b].valid_mel;
     const int v1 = nxt(vm);
@@ -38,31 +35,41 @@ __global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ me
         const bool ok = row >= 0 && row < vm && row < Tin && q >= 0 && q < mel_bins;
         xs[i] = ok ? mel[(static_cast<size_t>(b) * rows_stride + row) * mel_bins + q] : 0.f;
     }
-    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x) ws[(i % 9) * C + i / 9] = w[i];
-    for (int i = threadIdx.x; i < C; i += blockDim.x) bs[i] = bias[i];
     __syncthreads();
     const int groups = C / VW;
+    const int lanes_f = blockDim.x / groups;  // threads sharing a channel group, each taking every lanes_f-th f
+    const int g = threadIdx.x % groups, f0 = threadIdx.x / groups;
+    if (f0 >= lanes_f) return;
+    const int c = g * VW;
+    float wr[9][VW], br[VW];
+#pragma unroll
+    for (int e = 0; e < VW; ++e) {
+        br[e] = bias[c + e];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wr[k][e] = w[(c + e) * 9 + k];
+    }
     T* orow = out + (static_cast<size_t>(b) * T1 + t) * F1 * C;
-    for (int idx = threadIdx.x; idx < F1 * groups; idx += blockDim.x) {
-        const int f = idx / groups, c = (idx % groups) * VW;
+    const bool live = t < v1;
+    for (int f = f0; f < F1; f += lanes_f) {
         float acc[VW];
 #pragma unroll
-        for (int e = 0; e < VW; ++e) acc[e] = bs[c + e];
+        for (int e = 0; e < VW; ++e) acc[e] = br[e];
 #pragma unroll
         for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
             for (int kw = 0; kw < 3; ++kw) {
                 const float xv = xs[kh * W + 2 * f + kw];
 #pragma unroll
-                for (int e = 0; e < VW; ++e) acc[e] = fmaf(ws[(kh * 3 + kw) * C + c + e], xv, acc[e]);
+                for (int e = 0; e < VW; ++e) acc[e] = fmaf(wr[kh * 3 + kw][e], xv, acc[e]);
             }
 #pragma unroll
-        for (int e = 0; e < VW; ++e) acc[e] = t < v1 ? fmaxf(acc[e], 0.f) : 0.f;
+        for (int e = 0; e < VW; ++e) acc[e] = live ? fmaxf(acc[e], 0.f) : 0.f;
         store16<T>(orow + static_cast<size_t>(f) * C + c, acc);
     }
 }
 
-// One CTA per (stream, output row); a thread per (output frequency, 8-channel group), 16-byte loads.
+// One CTA per (stream, output row); each thread owns one 8-channel group (taps in registers), steps over output
+// frequencies, and reads its inputs with 16-byte loads.
 template <typename T>
 __global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, int Tin, int Fin, int stage,
                                                      const BatchEntry* __restrict__ meta, const float* __restrict__ w,
@@ -73,11 +80,21 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, i
     const int v1 = nxt(meta[b].valid_mel);
     const int vin = stage == 1 ? v1 : nxt(v1);
     const int groups = C / VW;
-    for (int idx = threadIdx.x; idx < Fout * groups; idx += blockDim.x) {
-        const int f = idx / groups, c = (idx % groups) * VW;
+    const int lanes_f = blockDim.x / groups;
+    const int g = threadIdx.x % groups, f0 = threadIdx.x / groups;
+    if (f0 >= lanes_f) return;
+    const int c = g * VW;
+    float wr[9][VW], br[VW];
+#pragma unroll
+    for (int e = 0; e < VW; ++e) {
+        br[e] = bias[c + e];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) wr[k][e] = w[(c + e) * 9 + k];
+    }
+    for (int f = f0; f < Fout; f += lanes_f) {
         float acc[VW];
 #pragma unroll
-        for (int e = 0; e < VW; ++e) acc[e] = bias[c + e];
+        for (int e = 0; e < VW; ++e) acc[e] = br[e];
 #pragma unroll
         for (int kh = 0; kh < 3; ++kh) {
             const int r = 2 * t + kh - 2;
@@ -89,7 +106,7 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, i
                 float x[VW];
                 load16<T>(in + ((static_cast<size_t>(b) * Tin + r) * Fin + q) * C + c, x);
 #pragma unroll
-                for (int e = 0; e < VW; ++e) acc[e] = fmaf(w[(c + e) * 9 + kh * 3 + kw], x[e], acc[e]);
+                for (int e = 0; e < VW; ++e) acc[e] = fmaf(wr[kh * 3 + kw][e], x[e], acc[e]);
             }
         }
         store16<T>(out + ((static_cast<size_t>(b) * Tout + t) * Fout + f) * C + c, acc);
@@ -137,7 +154,7 @@ template <typename T>
 void sub_conv0(const float* mel, int rows_stride, int mel_bins, const BatchEntry* meta, int n, int Tin, const float* w,
                const float* b, T* out, int T1, int F1, int C, cudaStream_t s) {
     dim3 grid(n, T1);
-    const size_t smem = sizeof(float) * (3 * (mel_bins + 3) + 10 * C);
+    const size_t smem = sizeof(float) * (3 * (mel_bins + 3));
     conv0_kernel<T><<<grid, 256, smem, s>>>(mel, rows_stride, mel_bins, meta, Tin, w, b, out, T1, F1, C);
 }
 
