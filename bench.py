@@ -207,6 +207,85 @@ def workload_config(args):
             "parallelism": f"stream-sharded x{args.gpus}, no collectives"}
 
 
+def run_cache_bench(args, world, rank, local):
+    """Config 5: the cache-op microbenchmark. Per step, for B streams and all 24 layers: append k new frames of
+    projected K and V plus conv rows after each stream's head, roll (metadata), gather every stream's 70-frame
+    K/V window and 8 conv rows into contiguous buffers, then evict and refill 5% of the streams. Stream ids are
+    a fresh random permutation every step. GB/s = algorithmic bytes (oracle/cache_ring.py
+    bytes_per_stream_step x B) / device time."""
+    import ud
+    from oracle.cache_ring import bytes_per_stream_step
+
+    B, k, NL, D, L = args.cache_streams, args.cache_k, 24, 1024, 70
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    cfg = ud.default_config(n_layers=NL, sub_channels=0, joint_dim=0, max_streams=B, max_batch=B,
+                            max_chunk_frames=max(k, 2))
+    eng = ud.Engine(cfg, device=local)
+    ids = [eng.open(0) for _ in range(B)]
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    kv_new = torch.randn(B, NL, 2, k, D, device=dev, generator=gen).to(torch.bfloat16)
+    cv_new = torch.randn(B, NL, k, D, device=dev, generator=gen).to(torch.bfloat16)
+    kv_out = torch.empty(B, NL, 2, L, D, device=dev, dtype=torch.bfloat16)
+    cv_out = torch.empty(B, NL, 8, D, device=dev, dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(rank)
+    stream = torch.cuda.ExternalStream(eng.cuda_stream(), device=dev)
+
+    def step():
+        perm = [int(i) for i in rng.permutation(ids)]
+        eng.cache_append(perm, k, kv_new.data_ptr(), cv_new.data_ptr())
+        eng.cache_roll(perm, k)
+        eng.cache_gather(perm, kv_out.data_ptr(), cv_out.data_ptr())
+        ev = [int(i) for i in rng.choice(ids, size=max(1, B // 20), replace=False)]
+        eng.cache_evict(ev)
+
+    for _ in range(args.warmup):
+        step()
+    eng.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = eng.launch_count()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        e1.synchronize()
+    launches = eng.launch_count() - l0
+    ms = e0.elapsed_time(e1)
+    t = ms
+    if dist:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    per_step = B * bytes_per_stream_step(NL, D, 2, k) + (B // 20) * NL * 8 * D * 2  # + conv-slot zeroing on refill
+    gbs = per_step * args.steps * world / (t / 1e3) / 1e9
+    hbm, _, _, src = peaks()
+    if rank == 0:
+        print(json.dumps({"metric": "cache-op HBM GB/s (append+roll+gather, 24 layers)", "value": gbs, "unit": "GB/s",
+                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic",
+                          "config": {"workload": f"C5: {B} streams/GPU, k={k} frames/step, 24 layers x 70 x 1024 K/V "
+                                                 "rings + 8-row conv rings, random permutation, 5% evict+refill",
+                                     "bytes_per_step": per_step},
+                          "gpu_launches": launches,
+                          "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                       "frac": gbs / hbm, "traffic": None, "note": f"peak = {src} HBM copy"},
+                          "clocks": clk.summary()}), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -219,6 +298,10 @@ def main():
                     help="also run greedy RNN-T decoding in each step (configs 2 and 4; C3 is the encoder step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
+                    help="c3: the encoder step (default); c5: the cache-op microbenchmark")
+    ap.add_argument("--cache-streams", type=int, default=1024, help="c5: streams per GPU")
+    ap.add_argument("--cache-k", type=int, default=14, help="c5: frames appended per stream per step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -226,6 +309,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
+    if args.workload == "c5":
+        run_cache_bench(args, world, rank, local)
+        return
     if args.impl == "reference":
         res = run_reference(args, world, rank)
         if res is not None:

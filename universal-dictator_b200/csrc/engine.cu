@@ -111,8 +111,6 @@ struct ud_engine {
     void* gather_scratch = nullptr;
 
     float* h_in = nullptr;
-    float* h_out = nullptr;
-    int32_t* h_tok = nullptr;
     int* h_ntok = nullptr;
 
     static constexpr int kRing = 4;
@@ -705,13 +703,20 @@ ud_status load_weights_impl(ud_engine* e, const ud_weight* table, int n) {
     // subsampling
     if (c.sub_channels) {
         const std::string s = "encoder.pre_encode.";
-        UD_TRY(need(t, s + "conv.0.weight", {C, 1, 3, 3}, &p)); UD_TRY(upload_f32(e, p, C * 9, &e->c0_w));
+        // 3x3 taps go to the device tap-major ([9][C]) so each thread's channel group is contiguous.
+        auto taps = [&](const float* src, float** dst) -> ud_status {
+            std::vector<float> tr(static_cast<size_t>(9) * C);
+            for (int ch = 0; ch < C; ++ch)
+                for (int k = 0; k < 9; ++k) tr[static_cast<size_t>(k) * C + ch] = src[ch * 9 + k];
+            return upload_f32(e, tr.data(), tr.size(), dst);
+        };
+        UD_TRY(need(t, s + "conv.0.weight", {C, 1, 3, 3}, &p)); UD_TRY(taps(p, &e->c0_w));
         UD_TRY(need(t, s + "conv.0.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c0_b));
-        UD_TRY(need(t, s + "conv.2.weight", {C, 1, 3, 3}, &p)); UD_TRY(upload_f32(e, p, C * 9, &e->c2_w));
+        UD_TRY(need(t, s + "conv.2.weight", {C, 1, 3, 3}, &p)); UD_TRY(taps(p, &e->c2_w));
         UD_TRY(need(t, s + "conv.2.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c2_b));
         UD_TRY(need(t, s + "conv.3.weight", {C, C, 1, 1}, &p)); UD_TRY(upload_gemm(e, stg, {p}, {C}, C, e->c3));
         UD_TRY(need(t, s + "conv.3.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c3_b));
-        UD_TRY(need(t, s + "conv.5.weight", {C, 1, 3, 3}, &p)); UD_TRY(upload_f32(e, p, C * 9, &e->c5_w));
+        UD_TRY(need(t, s + "conv.5.weight", {C, 1, 3, 3}, &p)); UD_TRY(taps(p, &e->c5_w));
         UD_TRY(need(t, s + "conv.5.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c5_b));
         UD_TRY(need(t, s + "conv.6.weight", {C, C, 1, 1}, &p)); UD_TRY(upload_gemm(e, stg, {p}, {C}, C, e->c6));
         UD_TRY(need(t, s + "conv.6.bias", {C}, &p)); UD_TRY(upload_f32(e, p, C, &e->c6_b));
@@ -1118,8 +1123,6 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
     if ((s = dalloc(e, &e->tok_dev, tok_elems)) != UD_OK) return cleanup(s);
     if ((s = dalloc(e, &e->ntok_dev, B)) != UD_OK) return cleanup(s);
     if ((s = halloc(e, &e->h_in, in_elems)) != UD_OK) return cleanup(s);
-    if ((s = halloc(e, &e->h_out, out_elems)) != UD_OK) return cleanup(s);
-    if ((s = halloc(e, &e->h_tok, tok_elems)) != UD_OK) return cleanup(s);
     if ((s = halloc(e, &e->h_ntok, B)) != UD_OK) return cleanup(s);
     const size_t meta_n = std::max<size_t>(B, c.max_streams);
     for (int r = 0; r < ud_engine::kRing; ++r) {
@@ -1309,27 +1312,33 @@ ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const floa
     const int W = e->in_width;
     // The pinned staging buffer may still be read by a previous asynchronous call.
     UD_CK(cudaStreamSynchronize(e->stream));
-    for (int i = 0; i < n; ++i)
-        std::memcpy(e->h_in + static_cast<size_t>(i) * stride * W, mel[i], sizeof(float) * n_rows[i] * W);
-    UD_CK(cudaMemcpy2DAsync(e->in_stage, sizeof(float) * W * stride, e->h_in, sizeof(float) * W * stride,
-                            sizeof(float) * W * rows_max, n, cudaMemcpyHostToDevice, e->stream));
+    // Rows of all streams in one caller buffer at a fixed stride: one strided copy straight from it (a DMA when
+    // the caller's memory is pinned). Otherwise gather through the pinned staging buffer.
+    bool uniform = true;
+    const ptrdiff_t sstride = n > 1 ? mel[1] - mel[0] : static_cast<ptrdiff_t>(W) * stride;
+    for (int i = 1; i < n && uniform; ++i) uniform = mel[i] - mel[0] == sstride * i;
+    uniform = uniform && sstride >= static_cast<ptrdiff_t>(W) * rows_max;
+    if (uniform) {
+        UD_CK(cudaMemcpy2DAsync(e->in_stage, sizeof(float) * W * stride, mel[0], sizeof(float) * sstride,
+                                sizeof(float) * W * rows_max, n, cudaMemcpyHostToDevice, e->stream));
+    } else {
+        for (int i = 0; i < n; ++i)
+            std::memcpy(e->h_in + static_cast<size_t>(i) * stride * W, mel[i], sizeof(float) * n_rows[i] * W);
+        UD_CK(cudaMemcpy2DAsync(e->in_stage, sizeof(float) * W * stride, e->h_in, sizeof(float) * W * stride,
+                                sizeof(float) * W * rows_max, n, cudaMemcpyHostToDevice, e->stream));
+    }
     std::vector<int> frames(n);
     UD_TRY(run_batch(e, n, ids, e->in_stage, stride, n_rows, valid_rows, keep_all, e->out_stage, frames.data(),
                      tokens_out ? e->tok_dev : nullptr, e->ntok_dev, true));
     const size_t out_n = static_cast<size_t>(n) * e->tmax * e->out_width;
-    UD_CK(cudaMemcpyAsync(e->h_out, e->out_stage, sizeof(float) * out_n, cudaMemcpyDeviceToHost, e->stream));
+    UD_CK(cudaMemcpyAsync(proj_out, e->out_stage, sizeof(float) * out_n, cudaMemcpyDeviceToHost, e->stream));
     if (tokens_out) {
-        UD_CK(cudaMemcpyAsync(e->h_tok, e->tok_dev, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols,
+        UD_CK(cudaMemcpyAsync(tokens_out, e->tok_dev, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols,
                               cudaMemcpyDeviceToHost, e->stream));
-        UD_CK(cudaMemcpyAsync(e->h_ntok, e->ntok_dev, sizeof(int) * n, cudaMemcpyDeviceToHost, e->stream));
+        UD_CK(cudaMemcpyAsync(n_tokens_out, e->ntok_dev, sizeof(int) * n, cudaMemcpyDeviceToHost, e->stream));
     }
     UD_TRY(check_device_error(e));
-    std::memcpy(proj_out, e->h_out, sizeof(float) * out_n);
     if (frames_out) std::memcpy(frames_out, frames.data(), sizeof(int) * n);
-    if (tokens_out) {
-        std::memcpy(tokens_out, e->h_tok, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols);
-        std::memcpy(n_tokens_out, e->h_ntok, sizeof(int) * n);
-    }
     return UD_OK;
 }
 

@@ -16,6 +16,7 @@ namespace {
 
 __device__ __forceinline__ int nxt(int t) { return t / 2 + 1; }
 
+// Taps are stored tap-major, w[k * C + c] (transposed from the checkpoint's [C][1][3][3] at load).
 // One CTA per (stream, output row). Each thread owns one 8-channel group (its 72 taps in registers) and steps
 // over output frequencies; the three input mel rows sit in shared memory and are read as broadcasts.
 template <typename T>
@@ -43,11 +44,17 @@ __global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ me
     const int c = g * VW;
     float wr[9][VW], br[VW];
 #pragma unroll
-    for (int e = 0; e < VW; ++e) {
-        br[e] = bias[c + e];
-#pragma unroll
-        for (int k = 0; k < 9; ++k) wr[k][e] = w[(c + e) * 9 + k];
+    for (int e = 0; e < VW; e += 4) {
+        const float4 bb = *reinterpret_cast<const float4*>(bias + c + e);
+        br[e] = bb.x; br[e + 1] = bb.y; br[e + 2] = bb.z; br[e + 3] = bb.w;
     }
+#pragma unroll
+    for (int k = 0; k < 9; ++k)   // taps stored tap-major [9][C]: this thread's channels are contiguous
+#pragma unroll
+        for (int e = 0; e < VW; e += 4) {
+            const float4 ww = *reinterpret_cast<const float4*>(w + k * C + c + e);
+            wr[k][e] = ww.x; wr[k][e + 1] = ww.y; wr[k][e + 2] = ww.z; wr[k][e + 3] = ww.w;
+        }
     T* orow = out + (static_cast<size_t>(b) * T1 + t) * F1 * C;
     const bool live = t < v1;
     for (int f = f0; f < F1; f += lanes_f) {
@@ -86,11 +93,17 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, i
     const int c = g * VW;
     float wr[9][VW], br[VW];
 #pragma unroll
-    for (int e = 0; e < VW; ++e) {
-        br[e] = bias[c + e];
-#pragma unroll
-        for (int k = 0; k < 9; ++k) wr[k][e] = w[(c + e) * 9 + k];
+    for (int e = 0; e < VW; e += 4) {
+        const float4 bb = *reinterpret_cast<const float4*>(bias + c + e);
+        br[e] = bb.x; br[e + 1] = bb.y; br[e + 2] = bb.z; br[e + 3] = bb.w;
     }
+#pragma unroll
+    for (int k = 0; k < 9; ++k)   // taps stored tap-major [9][C]: this thread's channels are contiguous
+#pragma unroll
+        for (int e = 0; e < VW; e += 4) {
+            const float4 ww = *reinterpret_cast<const float4*>(w + k * C + c + e);
+            wr[k][e] = ww.x; wr[k][e + 1] = ww.y; wr[k][e + 2] = ww.z; wr[k][e + 3] = ww.w;
+        }
     for (int f = f0; f < Fout; f += lanes_f) {
         float acc[VW];
 #pragma unroll

@@ -242,7 +242,7 @@ class Engine:
         arrs = [np.ascontiguousarray(m, dtype=np.float32) for m in mels]
         ptrs = (C.POINTER(C.c_float) * n)(*[_ptr(a) for a in arrs])
         tm, W = self.cfg.max_chunk_frames, self.out_width
-        out = np.zeros((n, tm, W), np.float32)
+        out = np.empty((n, tm, W), np.float32)
         frames = np.zeros(n, np.int32)
         ids_a, nr, vr, ka = _i32(ids), _i32(n_rows), _i32(valid_rows), _i32([int(k) for k in keep_all])
         toks = np.zeros((n, tm * self.cfg.max_symbols), np.int32) if decode else None
@@ -250,7 +250,7 @@ class Engine:
         check(lib().ud_step_batch(self.h, n, _ptr(ids_a, C.c_int32), ptrs, _ptr(nr, C.c_int), _ptr(vr, C.c_int),
                                   _ptr(ka, C.c_int), _ptr(out), _ptr(frames, C.c_int),
                                   _ptr(toks, C.c_int32) if decode else None, _ptr(ntok, C.c_int) if decode else None))
-        projs = [out[i, :frames[i]].copy() for i in range(n)]
+        projs = [out[i, :frames[i]] for i in range(n)]     # views into one result block
         tok_lists = [toks[i, :ntok[i]].tolist() for i in range(n)] if decode else None
         return projs, frames.tolist(), tok_lists
 
