@@ -237,13 +237,24 @@ def run_cache_bench(args, world, rank, local):
     rng = np.random.default_rng(rank)
     stream = torch.cuda.ExternalStream(eng.cuda_stream(), device=dev)
 
+    cache_len = np.zeros(B, np.int64)          # host mirror of each stream's cacheLen (bytes are counted from it)
+    row = D * 2
+
     def step():
+        """One step; returns its algorithmic HBM bytes: per stream and layer the k new K/V rows read and written,
+        the valid window rows read (cacheLen after the roll) and all L window rows written out, the conv rows
+        (k read, min(k, 8) written into the ring, 8 read and 8 written out); plus the conv-ring reset of each
+        evicted stream."""
         perm = [int(i) for i in rng.permutation(ids)]
         eng.cache_append(perm, k, kv_new.data_ptr(), cv_new.data_ptr())
         eng.cache_roll(perm, k)
         eng.cache_gather(perm, kv_out.data_ptr(), cv_out.data_ptr())
-        ev = [int(i) for i in rng.choice(ids, size=max(1, B // 20), replace=False)]
-        eng.cache_evict(ev)
+        np.minimum(cache_len + k, L, out=cache_len)
+        nbytes = NL * row * (B * (2 * (2 * k + L) + k + min(k, 8) + 16) + 2 * int(cache_len.sum()))
+        ev = rng.choice(ids, size=max(1, B // 20), replace=False)
+        eng.cache_evict([int(i) for i in ev])
+        cache_len[ev] = 0
+        return nbytes + len(ev) * NL * 8 * row
 
     for _ in range(args.warmup):
         step()
@@ -252,10 +263,11 @@ def run_cache_bench(args, world, rank, local):
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     l0 = eng.launch_count()
+    total_bytes = 0
     with ClockSampler(local) as clk:
         e0.record(stream)
         for _ in range(args.steps):
-            step()
+            total_bytes += step()
         e1.record(stream)
         e1.synchronize()
     launches = eng.launch_count() - l0
@@ -265,8 +277,8 @@ def run_cache_bench(args, world, rank, local):
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t = float(tt.item())
-    per_step = B * bytes_per_stream_step(NL, D, 2, k) + (B // 20) * NL * 8 * D * 2  # + conv-slot zeroing on refill
-    gbs = per_step * args.steps * world / (t / 1e3) / 1e9
+    per_step = total_bytes / args.steps
+    gbs = total_bytes * world / (t / 1e3) / 1e9
     hbm, _, _, src = peaks()
     if rank == 0:
         print(json.dumps({"metric": "cache-op HBM GB/s (append+roll+gather, 24 layers)", "value": gbs, "unit": "GB/s",
@@ -275,7 +287,8 @@ def run_cache_bench(args, world, rank, local):
                           "data": "synthetic",
                           "config": {"workload": f"C5: {B} streams/GPU, k={k} frames/step, 24 layers x 70 x 1024 K/V "
                                                  "rings + 8-row conv rings, random permutation, 5% evict+refill",
-                                     "bytes_per_step": per_step},
+                                     "bytes_per_step": per_step,
+                                     "full_window_bytes_per_stream_step": bytes_per_stream_step(NL, D, 2, k)},
                           "gpu_launches": launches,
                           "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
                                        "frac": gbs / hbm, "traffic": None, "note": f"peak = {src} HBM copy"},

@@ -17,7 +17,10 @@ pytestmark = pytest.mark.gpu
 
 REF_SHAPES = [(1, 1, 1), (1, 1024, 1024), (7, 33, 65), (64, 64, 64), (100, 257, 130), (129, 640, 1024), (3, 4096, 1024)]
 TC_SHAPES = [(17, 256, 256), (129, 640, 1024), (200, 3072, 1024), (333, 2048, 1024), (448, 1024, 4352),
-             (1024, 4096, 1024), (3584, 1024, 4096), (3584, 4096, 1024)]
+             (1024, 4096, 1024), (3584, 1024, 4096), (3584, 4096, 1024),
+             # shapes whose tile widths are not 256 (last tiles of 192, 128-wide tiles, 16-column remainders)
+             (3584, 1024, 1024), (3584, 640, 1024), (3584, 3072, 1024), (3584, 2048, 1024), (300, 1040, 512),
+             (2000, 1040, 256)]
 
 
 @pytest.fixture(scope="module", params=["bf16", "bf16-1cta", "f32"])

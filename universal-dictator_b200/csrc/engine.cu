@@ -243,7 +243,7 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
                     return fail(UD_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
                 it = e->amaps.emplace(key, t).first;
             }
-            if (e->tc2_on && M >= 256 && W.N % 256 == 0) {
+            if (e->tc2_on && M >= 256 && W.N % 16 == 0) {
                 gemm_tc2(it->second, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, e->stream);
             } else {
                 const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;

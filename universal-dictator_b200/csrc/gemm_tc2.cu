@@ -9,6 +9,11 @@
 // drain their TMEM rows and report back to the leader. Per CTA and stage that is 32 KB of shared memory for
 // 128 x BN x 64 multiply-adds: half the operand bytes per FLOP of the one-CTA kernel, so six stages cover the
 // TMA round trip. Every wait is bounded, as in gemm_tc.cu.
+//
+// Tile width: each launch uses one tile width tn (a multiple of 16, at most 256; the last tile of a row may be
+// narrower) chosen on the host so that (rounds of resident pairs) x tn is smallest. With 148 SMs and M = 3584
+// that turns the 256-wide tiling's partial last round (76% of SMs busy) into full rounds of 208-wide tiles. The
+// MMA's N, the W rows each CTA loads (tile width / 2) and the epilogue width are read from the tile.
 #include "common.cuh"
 #include "gemm_epi.cuh"
 #include "kernels.h"
@@ -25,7 +30,7 @@ template <int BN>
 struct Tc2Cfg {
     static constexpr int STAGES = 6;
     static constexpr int A_BYTES = 128 * BK * 2;        // this CTA's half of the A tile
-    static constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile
+    static constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile (a full 128-row box)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
@@ -79,7 +84,7 @@ __device__ __forceinline__ void tc2_commit_both(uint64_t* bar) {
 template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW, int M, int N,
-                    int K, const GemmEpilogue epi, int* err) {
+                    int K, int tn, const GemmEpilogue epi, int* err) {
     using C = Tc2Cfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -98,7 +103,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t rank = cluster_rank();
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
     const int num_m = (M + BM2 - 1) / BM2;
-    const int num_tiles = num_m * (N / BN);
+    const int tiles_per_row = (N + tn - 1) / tn;
+    const int num_tiles = num_m * tiles_per_row;
     const int num_kb = K / BK;
 
     if (threadIdx.x == 0) {
@@ -132,12 +138,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             for (int tile = pair; tile < num_tiles; tile += num_pairs) {
                 const int mb = tile % num_m, nb = tile / num_m;
+                const int c0 = nb * tn, w = min(tn, N - c0);
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, DEV_TIMEOUT_EMPTY, abort_v)) goto producer_done;
                     const uint32_t leader_full = peer_addr(smem_u32(&full[stage]), 0);
                     if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
                     tma_load_2d_pair(sA + stage * C::A_BYTES, &mapA, leader_full, kb * BK, mb * BM2 + rank * 128);
-                    tma_load_2d_pair(sB + stage * C::B_BYTES, &mapW, leader_full, kb * BK, nb * BN + rank * (BN / 2));
+                    tma_load_2d_pair(sB + stage * C::B_BYTES, &mapW, leader_full, kb * BK, c0 + static_cast<int>(rank) * (w / 2));
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
@@ -145,10 +152,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            const uint32_t idesc = idesc_bf16_f32(BM2, BN);
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
             for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+                const int nb = tile / num_m;
+                const uint32_t idesc = idesc_bf16_f32(BM2, min(tn, N - nb * tn));
                 if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1u, err, DEV_TIMEOUT_ACC_EMPTY, abort_v)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -172,12 +180,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else {
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
-        const int cbeg = half * (BN / 2), cend = cbeg + BN / 2;
+        const int half = (warp - 2) >> 2;   // the two warps of a lane quadrant take alternate 16-column blocks
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = pair; tile < num_tiles; tile += num_pairs) {
             const int mb = tile % num_m, nb = tile / num_m;
+            const int c0 = nb * tn, nblk = min(tn, N - c0) / 16;
             int ok = 1;
             if (lane == 0) ok = mbar_wait_bounded(&acc_full[acc], acc_phase, err, DEV_TIMEOUT_ACC_FULL, abort_v) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -187,16 +195,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const bool live = row < M;
             const bool res = epi.residual != nullptr && live;
             const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-            float rnext[32];
-            if (res) load_residual32(epi, row, nb * BN + cbeg, rnext);
+            float rnext[16];
+            if (res && half < nblk) load_residual16(epi, row, c0 + half * 16, rnext);
 #pragma unroll 1
-            for (int c0 = cbeg; c0 < cend; c0 += 32) {
-                float v[32], rcur[32];
+            for (int blk = half; blk < nblk; blk += 2) {
+                float v[16], rcur[16];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) rcur[j] = rnext[j];
-                if (res && c0 + 32 < cend) load_residual32(epi, row, nb * BN + c0 + 32, rnext);
-                tmem_ld32(t_row + static_cast<uint32_t>(c0), v);
-                if (live) epilogue_store32(epi, row, nb * BN + c0, v, rcur);
+                for (int j = 0; j < 16; ++j) rcur[j] = rnext[j];
+                if (res && blk + 2 < nblk) load_residual16(epi, row, c0 + (blk + 2) * 16, rnext);
+                tmem_ld16(t_row + static_cast<uint32_t>(blk * 16), v);
+                if (live) epilogue_store16(epi, row, c0 + blk * 16, v, rcur);
             }
             tc_fence_before();
             __syncwarp();
@@ -245,9 +253,20 @@ void launch2(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const 
         }
         max_pairs = n < num_sms / 2 ? n : num_sms / 2;
     }
-    const int tiles = ((M + BM2 - 1) / BM2) * (N / BN);
+    // Tile width: the multiple of 16 (<= BN) with the fewest (rounds x width), preferring wider tiles on ties.
+    const int num_m = (M + BM2 - 1) / BM2;
+    int tn = BN, best = 1 << 30, tiles = 0;
+    for (int wdt = BN; wdt >= 64; wdt -= 16) {
+        const int t = num_m * ((N + wdt - 1) / wdt);
+        const int rounds = (t + max_pairs - 1) / max_pairs;
+        if (rounds * wdt < best) {
+            best = rounds * wdt;
+            tn = wdt;
+            tiles = t;
+        }
+    }
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
-    gemm_tc2_kernel<BN><<<2 * pairs, kThreads, C::SMEM, s>>>(A.map, W.map, M, N, K, epi, err);
+    gemm_tc2_kernel<BN><<<2 * pairs, kThreads, C::SMEM, s>>>(A.map, W.map, M, N, K, tn, epi, err);
 }
 
 }  // namespace
