@@ -299,6 +299,68 @@ def run_cache_bench(args, world, rank, local):
         dist.destroy_process_group()
 
 
+GEMM_SHAPES = [  # (name, N, K, activation, residual, bf16 output): one encoder layer's projections
+    ("ff.up", 4096, 1024, 2, False, True), ("ff.down", 1024, 4096, 0, True, False),
+    ("attn.qkv", 3072, 1024, 0, False, True), ("attn.out", 1024, 1024, 0, True, False),
+    ("conv.pw1", 2048, 1024, 0, False, True), ("conv.pw2", 1024, 1024, 0, True, False)]
+
+
+def run_gemm_bench(args, local):
+    """The tcgen05 GEMM alone on one encoder layer's projection shapes, M = streams x (lookahead + 1) rows, with
+    each shape's epilogue (SiLU, residual, output type). Every call reads one of 24 weight copies in turn, as
+    the 24 layers do, so weights stream from HBM; device time per launch comes from the engine's per-launch
+    CUDA events. One JSON line: total FLOPs / total device time, with per-shape TFLOP/s."""
+    import ud
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(local)
+    M = args.streams * (args.lookahead + 1)
+    eng = ud.Engine(ud.default_config(n_layers=0, sub_channels=0, joint_dim=0, max_streams=1, max_batch=1),
+                    device=local)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    _, peak, _, src = peaks()   # kernels timed alone: the burst bf16 figure
+    per_shape, tot_flop, tot_ms, launches = {}, 0.0, 0.0, 0
+    for name, N, K, act, res, obf in GEMM_SHAPES:
+        A = (torch.randn(M, K, device=dev, generator=gen) * 0.5).bfloat16()
+        Ws = [(torch.randn(N, K, device=dev, generator=gen) * 0.03).bfloat16() for _ in range(24)]
+        R = torch.randn(M, N, device=dev, generator=gen) if res else None
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16 if obf else torch.float32)
+        torch.cuda.synchronize()
+
+        def call(i):
+            eng.debug_gemm(A.data_ptr(), Ws[i % 24].data_ptr(), M, N, K, out.data_ptr(), act=act,
+                           res_ptr=R.data_ptr() if res else None, out_bf16=obf)
+
+        for i in range(args.warmup):
+            call(i)
+        eng.profile(True)
+        for i in range(args.steps):
+            call(i)
+        prof = eng.profile_read()
+        eng.profile(False)
+        ms, n = prof["gemm_tc"]
+        if n != args.steps:
+            raise RuntimeError(f"{name}: {n} tensor-core GEMM launches for {args.steps} calls")
+        flop = 2.0 * M * N * K * args.steps
+        per_shape[f"{name} {M}x{N}x{K}"] = {"us": ms * 1e3 / n, "tflops": flop / (ms / 1e3) / 1e12}
+        tot_flop += flop
+        tot_ms += ms
+        launches += n
+        del A, Ws, R, out
+    achieved = tot_flop / (tot_ms / 1e3) / 1e12
+    print(json.dumps({"metric": "GEMM TFLOP/s (encoder layer shapes)", "value": achieved, "unit": "TFLOP/s",
+                      "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": tot_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": f"GEMM: one layer's six projections at M={M}, 24 weight copies each",
+                                 "engine": "2-CTA tcgen05" if os.environ.get("UD_TC2", "1") != "0" else "1-CTA tcgen05",
+                                 "l2": "weights larger than L2 across the 24 copies"},
+                      "gpu_launches": launches, "per_shape": per_shape,
+                      "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                                   "frac": achieved / peak, "traffic": None, "note": f"peak = {src} burst bf16"}}), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,8 +373,9 @@ def main():
                     help="also run greedy RNN-T decoding in each step (configs 2 and 4; C3 is the encoder step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c5"], default="c3",
-                    help="c3: the encoder step (default); c5: the cache-op microbenchmark")
+    ap.add_argument("--workload", choices=["c3", "c5", "gemm"], default="c3",
+                    help="c3: the encoder step (default); c5: the cache-op microbenchmark; gemm: the tensor-core "
+                         "GEMM on one layer's shapes")
     ap.add_argument("--cache-streams", type=int, default=1024, help="c5: streams per GPU")
     ap.add_argument("--cache-k", type=int, default=14, help="c5: frames appended per stream per step")
     args = ap.parse_args()
@@ -324,6 +387,10 @@ def main():
 
     if args.workload == "c5":
         run_cache_bench(args, world, rank, local)
+        return
+    if args.workload == "gemm":
+        if rank == 0:
+            run_gemm_bench(args, local)
         return
     if args.impl == "reference":
         res = run_reference(args, world, rank)

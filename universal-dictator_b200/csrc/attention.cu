@@ -67,6 +67,8 @@ __global__ void __launch_bounds__(256) relpos_attn_kernel(const T* __restrict__ 
                                                           const float* __restrict__ bias_v,
                                                           const BatchEntry* __restrict__ meta, const CacheGeom cg,
                                                           int layer, T* __restrict__ out, int ldo, int tb, int* err) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int CH = 16 / sizeof(T);  // elements per 16-byte chunk
     constexpr int CPR = DK / CH;        // chunks per head row
     const int b = blockIdx.x, h = blockIdx.y;
@@ -272,6 +274,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __res
                                                       const float* __restrict__ bias_v,
                                                       const BatchEntry* __restrict__ meta, const CacheGeom cg,
                                                       int layer, bf16* __restrict__ out, int ldo, int* err) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int DKk = 128;
     const int b = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -511,7 +515,7 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
                 tc_attr = lay.total;
             }
             dim3 grid(n, n_heads);
-            tc::attn_tc_kernel<<<grid, tc::kAttnThreads, lay.total, s>>>(qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer,
+            launch_pdl(tc::attn_tc_kernel, dim3(grid), dim3(tc::kAttnThreads), lay.total, s, qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer,
                                                             out, ldo, dev_err);
             return;
         }
@@ -524,7 +528,7 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
         attr_set = lay.total;
     }
     dim3 grid(n, n_heads);
-    relpos_attn_kernel<T><<<grid, 256, lay.total, s>>>(qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer, out,
+    launch_pdl(relpos_attn_kernel<T>, dim3(grid), dim3(256), lay.total, s, qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer, out,
                                                        ldo, tmax_batch, dev_err);
 }
 

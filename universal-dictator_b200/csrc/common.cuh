@@ -90,6 +90,13 @@ __device__ __forceinline__ void report_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel of the step lets the next kernel start launching at once (its CTAs then run their prologue while
+// this grid finishes) and waits for the previous grid to complete before touching its results. Both are
+// no-ops when the launch did not ask for programmatic serialization.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------ mbarrier (shared::cta)
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -35,6 +35,8 @@ __global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ 
                                                           const float* __restrict__ beta,
                                                           const BatchEntry* __restrict__ meta, const CacheGeom cg,
                                                           int layer, T* __restrict__ out, int ldo) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int R = KW - 1;
     extern __shared__ float ys[];  // [T][D] pre-norm conv output
     const int b = blockIdx.x;
@@ -127,7 +129,7 @@ void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, con
                              static_cast<int>(smem));
         attr_set = smem;
     }
-    conv_module_kernel<T, 9><<<n, 512, smem, s>>>(pw, ld_pw, dw, ln_g, ln_b, meta, cg, layer, out, ldo);
+    launch_pdl(conv_module_kernel<T, 9>, dim3(n), dim3(512), smem, s, pw, ld_pw, dw, ln_g, ln_b, meta, cg, layer, out, ldo);
 }
 
 template void conv_module<float>(const float*, int, const float*, const float*, const float*, const BatchEntry*, int,

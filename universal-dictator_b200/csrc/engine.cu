@@ -621,7 +621,7 @@ ud_status need(const WeightTable& t, const std::string& name, std::vector<int64_
 
 ud_status upload_f32(ud_engine* e, const float* host, size_t n, float** out) {
     UD_TRY(dalloc(e, out, n));
-    UD_CK(cudaMemcpy(*out, host, n * sizeof(float), cudaMemcpyHostToDevice));
+    UD_CK(cudaMemcpyAsync(*out, host, n * sizeof(float), cudaMemcpyHostToDevice, e->stream));
     return UD_OK;
 }
 
@@ -642,7 +642,8 @@ ud_status upload_gemm(ud_engine* e, Staging& stg, const std::vector<const float*
         if (n > stg.cap) return fail(UD_ERR_WEIGHTS, "staging buffer too small");
         size_t off = 0;
         for (size_t i = 0; i < parts.size(); ++i) {
-            UD_CK(cudaMemcpy(stg.p + off, parts[i], sizeof(float) * part_rows[i] * K, cudaMemcpyHostToDevice));
+            UD_CK(cudaMemcpyAsync(stg.p + off, parts[i], sizeof(float) * part_rows[i] * K, cudaMemcpyHostToDevice,
+                                  e->stream));
             off += static_cast<size_t>(part_rows[i]) * K;
         }
         void* p;
@@ -663,7 +664,7 @@ ud_status upload_gemm(ud_engine* e, Staging& stg, const std::vector<const float*
         UD_TRY(dalloc(e, &p, n));
         size_t off = 0;
         for (size_t i = 0; i < parts.size(); ++i) {
-            UD_CK(cudaMemcpy(p + off, parts[i], sizeof(float) * part_rows[i] * K, cudaMemcpyHostToDevice));
+            UD_CK(cudaMemcpyAsync(p + off, parts[i], sizeof(float) * part_rows[i] * K, cudaMemcpyHostToDevice, e->stream));
             off += static_cast<size_t>(part_rows[i]) * K;
         }
         W.p = p;
@@ -739,7 +740,7 @@ ud_status load_weights_impl(ud_engine* e, const ud_weight* table, int n) {
     float *pe_d = nullptr, *ptab_f = nullptr;
     UD_TRY(dalloc(e, &pe_d, pe.size()));
     UD_TRY(dalloc(e, &ptab_f, pe.size()));
-    UD_CK(cudaMemcpy(pe_d, pe.data(), pe.size() * sizeof(float), cudaMemcpyHostToDevice));
+    UD_CK(cudaMemcpyAsync(pe_d, pe.data(), pe.size() * sizeof(float), cudaMemcpyHostToDevice, e->stream));
     e->layers.assign(c.n_layers, LayerW{});
     for (int l = 0; l < c.n_layers; ++l) {
         LayerW& w = e->layers[l];
@@ -772,7 +773,7 @@ ud_status load_weights_impl(ud_engine* e, const ud_weight* table, int n) {
         UD_TRY(need(t, s + "self_attn.pos_bias_v", {H, DK}, &a)); UD_TRY(upload_f32(e, a, D, &w.pos_v));
         // Projected position table P = sinusoid(rel) . W_pos^T in fp32, stored in the engine dtype.
         UD_TRY(need(t, s + "self_attn.linear_pos.weight", {D, D}, &a));
-        UD_CK(cudaMemcpy(stg.p, a, sizeof(float) * D * D, cudaMemcpyHostToDevice));
+        UD_CK(cudaMemcpyAsync(stg.p, a, sizeof(float) * D * D, cudaMemcpyHostToDevice, e->stream));
         GemmEpilogue gp;
         gp.out = ptab_f;
         gp.ldo = D;
@@ -1385,7 +1386,8 @@ ud_status ud_rnnt_decode(ud_engine* e, ud_stream_id id, const float* f, int fram
     UD_CK(cudaMemcpyAsync(e->h_ntok, e->ntok_dev, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     UD_CK(cudaStreamSynchronize(e->stream));
     const int nt = e->h_ntok[0];
-    UD_CK(cudaMemcpy(tokens_out, e->tok_dev, sizeof(int32_t) * nt, cudaMemcpyDeviceToHost));
+    UD_CK(cudaMemcpyAsync(tokens_out, e->tok_dev, sizeof(int32_t) * nt, cudaMemcpyDeviceToHost, e->stream));
+    UD_CK(cudaStreamSynchronize(e->stream));
     *n_tokens_out = nt;
     return UD_OK;
 }
@@ -1511,11 +1513,12 @@ ud_status ud_cache_read(ud_engine* e, ud_stream_id id, int layer, int kind, void
     UD_TRY(check_device_error(e));
     const size_t row = static_cast<size_t>(e->D) * e->esz;
     if (kind < 2)
-        UD_CK(cudaMemcpy(host_out, g + (static_cast<size_t>(layer) * 2 + kind) * e->L * row, e->L * row,
-                         cudaMemcpyDeviceToHost));
+        UD_CK(cudaMemcpyAsync(host_out, g + (static_cast<size_t>(layer) * 2 + kind) * e->L * row, e->L * row,
+                              cudaMemcpyDeviceToHost, e->stream));
     else
-        UD_CK(cudaMemcpy(host_out, g + kv + static_cast<size_t>(layer) * e->cg.conv_ring * row, e->cg.conv_ring * row,
-                         cudaMemcpyDeviceToHost));
+        UD_CK(cudaMemcpyAsync(host_out, g + kv + static_cast<size_t>(layer) * e->cg.conv_ring * row,
+                              e->cg.conv_ring * row, cudaMemcpyDeviceToHost, e->stream));
+    UD_CK(cudaStreamSynchronize(e->stream));
     return UD_OK;
 }
 

@@ -27,6 +27,8 @@ __device__ __forceinline__ void store_scalar(const GemmEpilogue& epi, int m, int
 template <typename T, int MR, bool VEC>
 __global__ void __launch_bounds__(256) gemv_rows_kernel(const T* __restrict__ A, int lda, const T* __restrict__ W,
                                                         int M, int N, int K, const GemmEpilogue epi) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int VW = VEC ? Vec16<T>::N : 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = blockIdx.x * 8 + warp;
@@ -64,6 +66,8 @@ __global__ void __launch_bounds__(256) gemv_rows_kernel(const T* __restrict__ A,
 template <typename T>
 __global__ void __launch_bounds__(256) gemm_tiled_kernel(const T* __restrict__ A, int lda, const T* __restrict__ W,
                                                          int M, int N, int K, const GemmEpilogue epi) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ float As[16][64 + 4];
     __shared__ float Ws[16][64 + 4];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -109,15 +113,15 @@ void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const Gem
         const bool vec = K % VW == 0 && lda % VW == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(W) & 15) == 0;
         if (vec) {
-            if (M <= 2) gemv_rows_kernel<TA, 2, true><<<grid, 256, 0, s>>>(A, lda, W, M, N, K, epi);
-            else if (M <= 4) gemv_rows_kernel<TA, 4, true><<<grid, 256, 0, s>>>(A, lda, W, M, N, K, epi);
-            else gemv_rows_kernel<TA, 8, true><<<grid, 256, 0, s>>>(A, lda, W, M, N, K, epi);
+            if (M <= 2) launch_pdl(gemv_rows_kernel<TA, 2, true>, dim3(grid), dim3(256), 0, s, A, lda, W, M, N, K, epi);
+            else if (M <= 4) launch_pdl(gemv_rows_kernel<TA, 4, true>, dim3(grid), dim3(256), 0, s, A, lda, W, M, N, K, epi);
+            else launch_pdl(gemv_rows_kernel<TA, 8, true>, dim3(grid), dim3(256), 0, s, A, lda, W, M, N, K, epi);
         } else {
-            gemv_rows_kernel<TA, 8, false><<<grid, 256, 0, s>>>(A, lda, W, M, N, K, epi);
+            launch_pdl(gemv_rows_kernel<TA, 8, false>, dim3(grid), dim3(256), 0, s, A, lda, W, M, N, K, epi);
         }
     } else {
         dim3 grid((N + 63) / 64, (M + 63) / 64);
-        gemm_tiled_kernel<TA><<<grid, 256, 0, s>>>(A, lda, W, M, N, K, epi);
+        launch_pdl(gemm_tiled_kernel<TA>, dim3(grid), dim3(256), 0, s, A, lda, W, M, N, K, epi);
     }
 }
 

@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW, int M, int N,
                    int K, const GemmEpilogue epi, int* err) {
     using C = TcCfg<BN>;
+    pdl_launch_dependents();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -82,6 +83,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // the prologue above overlaps the previous kernel; its outputs are read only from here on
 
     if (warp == 0) {
         if (lane == 0) {
@@ -199,7 +201,7 @@ void launch(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const G
     }
     const int tiles = ((M + BM - 1) / BM) * (N / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_tc_kernel<BN><<<grid, kThreads, C::SMEM, s>>>(A.map, W.map, M, N, K, epi, err);
+    launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kThreads), C::SMEM, s, A.map, W.map, M, N, K, epi, err);
 }
 
 }  // namespace

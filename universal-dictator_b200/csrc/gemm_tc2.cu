@@ -10,10 +10,11 @@
 // 128 x BN x 64 multiply-adds: half the operand bytes per FLOP of the one-CTA kernel, so six stages cover the
 // TMA round trip. Every wait is bounded, as in gemm_tc.cu.
 //
-// Tile width: each launch uses one tile width tn (a multiple of 16, at most 256; the last tile of a row may be
-// narrower) chosen on the host so that (rounds of resident pairs) x tn is smallest. With 148 SMs and M = 3584
-// that turns the 256-wide tiling's partial last round (76% of SMs busy) into full rounds of 208-wide tiles. The
-// MMA's N, the W rows each CTA loads (tile width / 2) and the epilogue width are read from the tile.
+// Tile width: each launch uses one tile width tn, the fewest tiles per output row of at most BN columns with
+// their width balanced and rounded up to a multiple of 16 (N = 1024 -> 256; N = 1040 -> 5 tiles of 208; the
+// last tile of a row may be narrower). The MMA's N, the W rows each CTA loads (tile width / 2) and the epilogue
+// width are read from the tile. Narrower tiles that would fill a partial last round of pairs measured slower
+// than the wide tiles on the encoder's shapes, so the host does not trade width for rounds.
 #include "common.cuh"
 #include "gemm_epi.cuh"
 #include "kernels.h"
@@ -86,6 +87,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW, int M, int N,
                     int K, int tn, const GemmEpilogue epi, int* err) {
     using C = Tc2Cfg<BN>;
+    pdl_launch_dependents();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -131,6 +133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // the prologue above overlaps the previous kernel; its outputs are read only from here on
 
     if (warp == 0) {
         if (lane == 0) {
@@ -180,12 +183,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else {
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;   // the two warps of a lane quadrant take alternate 16-column blocks
+        const int half = (warp - 2) >> 2;   // the two warps of a lane quadrant split the tile's columns
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = pair; tile < num_tiles; tile += num_pairs) {
             const int mb = tile % num_m, nb = tile / num_m;
-            const int c0 = nb * tn, nblk = min(tn, N - c0) / 16;
+            const int c0 = nb * tn, nblk = min(tn, N - c0) / 16;   // 16-column blocks in this tile
+            const int hb = (nblk + 1) >> 1;
+            const int b0 = half ? hb : 0, b1 = half ? nblk : hb;    // this warp's blocks [b0, b1)
             int ok = 1;
             if (lane == 0) ok = mbar_wait_bounded(&acc_full[acc], acc_phase, err, DEV_TIMEOUT_ACC_FULL, abort_v) ? 1 : 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -195,16 +200,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const bool live = row < M;
             const bool res = epi.residual != nullptr && live;
             const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-            float rnext[16];
-            if (res && half < nblk) load_residual16(epi, row, c0 + half * 16, rnext);
+            float rnext[32];
+            if (res && b0 + 2 <= b1) load_residual32(epi, row, c0 + b0 * 16, rnext);
+            int blk = b0;
 #pragma unroll 1
-            for (int blk = half; blk < nblk; blk += 2) {
-                float v[16], rcur[16];
+            for (; blk + 2 <= b1; blk += 2) {   // 32-column chunks, the next chunk's residual in flight
+                float v[32], rcur[32];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) rcur[j] = rnext[j];
-                if (res && blk + 2 < nblk) load_residual16(epi, row, c0 + (blk + 2) * 16, rnext);
+                for (int j = 0; j < 32; ++j) rcur[j] = rnext[j];
+                if (res && blk + 4 <= b1) load_residual32(epi, row, c0 + (blk + 2) * 16, rnext);
+                tmem_ld32(t_row + static_cast<uint32_t>(blk * 16), v);
+                if (live) epilogue_store32(epi, row, c0 + blk * 16, v, rcur);
+            }
+            if (blk < b1) {   // a 16-column tail when this warp's share is an odd number of blocks
+                float v[16], r16[16];
+                if (res) load_residual16(epi, row, c0 + blk * 16, r16);
                 tmem_ld16(t_row + static_cast<uint32_t>(blk * 16), v);
-                if (live) epilogue_store16(epi, row, c0 + blk * 16, v, rcur);
+                if (live) epilogue_store16(epi, row, c0 + blk * 16, v, r16);
             }
             tc_fence_before();
             __syncwarp();
@@ -253,20 +265,13 @@ void launch2(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const 
         }
         max_pairs = n < num_sms / 2 ? n : num_sms / 2;
     }
-    // Tile width: the multiple of 16 (<= BN) with the fewest (rounds x width), preferring wider tiles on ties.
+    // Tile width: the fewest tiles per row, widths balanced and rounded up to a multiple of 16.
     const int num_m = (M + BM2 - 1) / BM2;
-    int tn = BN, best = 1 << 30, tiles = 0;
-    for (int wdt = BN; wdt >= 64; wdt -= 16) {
-        const int t = num_m * ((N + wdt - 1) / wdt);
-        const int rounds = (t + max_pairs - 1) / max_pairs;
-        if (rounds * wdt < best) {
-            best = rounds * wdt;
-            tn = wdt;
-            tiles = t;
-        }
-    }
+    const int per_row = (N + BN - 1) / BN;
+    const int tn = ((N + per_row - 1) / per_row + 15) / 16 * 16;
+    const int tiles = num_m * ((N + tn - 1) / tn);
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
-    gemm_tc2_kernel<BN><<<2 * pairs, kThreads, C::SMEM, s>>>(A.map, W.map, M, N, K, tn, epi, err);
+    launch_pdl(gemm_tc2_kernel<BN>, dim3(2 * pairs), dim3(kThreads), C::SMEM, s, A.map, W.map, M, N, K, tn, epi, err);
 }
 
 }  // namespace

@@ -12,6 +12,24 @@ using bf16 = __nv_bfloat16;
 
 enum Act : int { ACT_NONE = 0, ACT_RELU = 1, ACT_SILU = 2 };
 
+// Launches a kernel of the step with programmatic stream serialization (the kernel calls pdl_wait before reading
+// what earlier kernels wrote). Off when the environment sets UD_PDL=0.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // C = out_scale * act(A . W^T + bias) + res_scale * R   (the contract of the reference's Step.gemm,
 // Sources/DictatorEngine/Core/Kernels.swift:79-113, minus alpha which Nemotron never sets).
 struct GemmEpilogue {

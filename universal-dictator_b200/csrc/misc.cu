@@ -1,4 +1,6 @@
 // Small utility kernels: fills, dtype conversion, and the bounded-wait probe used by the failure-detection test.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -38,6 +40,15 @@ __global__ void wait_probe_kernel(int* err, uint64_t limit_ns) {
 }
 
 }  // namespace
+
+bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* v = std::getenv("UD_PDL");
+        on = (v && std::atoi(v) == 0) ? 0 : 1;
+    }
+    return on == 1;
+}
 
 void fill_f32(float* p, float v, size_t n, cudaStream_t s) {
     if (!n) return;

@@ -12,11 +12,11 @@ namespace {
 // D = 128 * NV: each lane holds NV float4 of its row (D <= 1024).
 #define UD_LN_DISPATCH(KERNEL, ...)                                                              \
     switch (D / 128) {                                                                           \
-        case 1: KERNEL<TO, 1><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
-        case 2: KERNEL<TO, 2><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
-        case 4: KERNEL<TO, 4><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
-        case 6: KERNEL<TO, 6><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                   \
-        default: KERNEL<TO, 8><<<(M + 7) / 8, 256, 0, s>>>(__VA_ARGS__); break;                  \
+        case 1: launch_pdl(KERNEL<TO, 1>, dim3((M + 7) / 8), dim3(256), 0, s, __VA_ARGS__); break;                   \
+        case 2: launch_pdl(KERNEL<TO, 2>, dim3((M + 7) / 8), dim3(256), 0, s, __VA_ARGS__); break;                   \
+        case 4: launch_pdl(KERNEL<TO, 4>, dim3((M + 7) / 8), dim3(256), 0, s, __VA_ARGS__); break;                   \
+        case 6: launch_pdl(KERNEL<TO, 6>, dim3((M + 7) / 8), dim3(256), 0, s, __VA_ARGS__); break;                   \
+        default: launch_pdl(KERNEL<TO, 8>, dim3((M + 7) / 8), dim3(256), 0, s, __VA_ARGS__); break;                  \
     }
 
 template <typename TO>
@@ -53,6 +53,8 @@ __device__ __forceinline__ void row_stats(const float (&v)[NV][4], int D, float&
 template <typename TO, int NV>
 __global__ void __launch_bounds__(256) ln_kernel(const float* x, const float* __restrict__ g,
                                                  const float* __restrict__ b, TO* y, int M, int D) {
+    pdl_launch_dependents();
+    pdl_wait();
     // x and y may alias (in-place): each warp reads its whole row before writing it.
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
@@ -80,6 +82,8 @@ template <typename TO, int NV>
 __global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const float* __restrict__ g1,
                                                   const float* __restrict__ b1, const float* __restrict__ g2,
                                                   const float* __restrict__ b2, TO* __restrict__ y, int M, int D) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= M) return;

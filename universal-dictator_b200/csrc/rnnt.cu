@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(kThreads) rnnt_kernel(const RnntWeights w, con
                                                         const BatchEntry* __restrict__ meta,
                                                         int32_t* __restrict__ tokens, int tok_stride,
                                                         int* __restrict__ n_tokens) {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ __align__(16) float sm[];
     const int Hp = w.Hp, J = w.J, V = w.V, NLp = w.layers;
     float* f = sm;                  // [J]
@@ -194,7 +196,7 @@ void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, i
         cudaFuncSetAttribute(rnnt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         attr_set = smem;
     }
-    rnnt_kernel<<<n, kThreads, smem, s>>>(w, st, proj, ld_proj, meta, tokens, tok_stride, n_tokens);
+    launch_pdl(rnnt_kernel, dim3(n), dim3(kThreads), smem, s, w, st, proj, ld_proj, meta, tokens, tok_stride, n_tokens);
 }
 
 void rnnt_reset(const RnntState& st, const int* slots, int n, const RnntWeights& w, cudaStream_t s) {

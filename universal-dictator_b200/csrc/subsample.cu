@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ me
                                                     const BatchEntry* __restrict__ meta, int Tin,
                                                     const float* __restrict__ w, const float* __restrict__ bias,
                                                     T* __restrict__ out, int T1, int F1, int C) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int VW = Vec16<T>::N;
     extern __shared__ float xs[];           // [3][mel_bins + 3], frequency index shifted by the left pad of 2
     const int W = mel_bins + 3;
@@ -82,6 +84,8 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, i
                                                      const BatchEntry* __restrict__ meta, const float* __restrict__ w,
                                                      const float* __restrict__ bias, T* __restrict__ out, int Tout,
                                                      int Fout, int C) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int VW = Vec16<T>::N;
     const int b = blockIdx.x, t = blockIdx.y;
     const int v1 = nxt(meta[b].valid_mel);
@@ -128,6 +132,8 @@ __global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, i
 
 __global__ void select_kernel(const float* __restrict__ sub_out, int T3, const float* __restrict__ out_bias,
                               const BatchEntry* __restrict__ meta, float* __restrict__ x, int D) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x, t = blockIdx.y;
     const BatchEntry& me = meta[b];
     if (t >= me.T) return;
@@ -141,6 +147,8 @@ __global__ void select_kernel(const float* __restrict__ sub_out, int T3, const f
 
 __global__ void pack_frames_kernel(const float* __restrict__ frames, int rows_stride,
                                    const BatchEntry* __restrict__ meta, float* __restrict__ x, int D) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x, t = blockIdx.y;
     const BatchEntry& me = meta[b];
     if (t >= me.T) return;
@@ -152,6 +160,8 @@ __global__ void pack_frames_kernel(const float* __restrict__ frames, int rows_st
 
 __global__ void scatter_rows_kernel(const float* __restrict__ src, const BatchEntry* __restrict__ meta,
                                     float* __restrict__ dst, int tmax, int W) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x, t = blockIdx.y;
     const BatchEntry& me = meta[b];
     if (t >= me.keep) return;
@@ -168,32 +178,32 @@ void sub_conv0(const float* mel, int rows_stride, int mel_bins, const BatchEntry
                const float* b, T* out, int T1, int F1, int C, cudaStream_t s) {
     dim3 grid(n, T1);
     const size_t smem = sizeof(float) * (3 * (mel_bins + 3));
-    conv0_kernel<T><<<grid, 256, smem, s>>>(mel, rows_stride, mel_bins, meta, Tin, w, b, out, T1, F1, C);
+    launch_pdl(conv0_kernel<T>, dim3(grid), dim3(256), smem, s, mel, rows_stride, mel_bins, meta, Tin, w, b, out, T1, F1, C);
 }
 
 template <typename T>
 void sub_dwconv(const T* in, int Tin, int Fin, const int*, int stage, const BatchEntry* meta, int n, const float* w,
                 const float* b, T* out, int Tout, int Fout, int C, cudaStream_t s) {
     dim3 grid(n, Tout);
-    dwconv_kernel<T><<<grid, 256, 0, s>>>(in, Tin, Fin, stage, meta, w, b, out, Tout, Fout, C);
+    launch_pdl(dwconv_kernel<T>, dim3(grid), dim3(256), 0, s, in, Tin, Fin, stage, meta, w, b, out, Tout, Fout, C);
 }
 
 template <typename T>
 void sub_select(const float* sub_out, int T3, const float* out_bias, const BatchEntry* meta, int n, float* x, int D,
                 cudaStream_t s) {
     dim3 grid(n, T3);
-    select_kernel<<<grid, 256, 0, s>>>(sub_out, T3, out_bias, meta, x, D);
+    launch_pdl(select_kernel, dim3(grid), dim3(256), 0, s, sub_out, T3, out_bias, meta, x, D);
 }
 
 void pack_frames(const float* frames, int rows_stride, const BatchEntry* meta, int n, int tmax, float* x, int D,
                  cudaStream_t s) {
     dim3 grid(n, tmax);
-    pack_frames_kernel<<<grid, 256, 0, s>>>(frames, rows_stride, meta, x, D);
+    launch_pdl(pack_frames_kernel, dim3(grid), dim3(256), 0, s, frames, rows_stride, meta, x, D);
 }
 
 void scatter_rows(const float* src, const BatchEntry* meta, int n, float* dst, int tmax, int W, cudaStream_t s) {
     dim3 grid(n, tmax);
-    scatter_rows_kernel<<<grid, 128, 0, s>>>(src, meta, dst, tmax, W);
+    launch_pdl(scatter_rows_kernel, dim3(grid), dim3(128), 0, s, src, meta, dst, tmax, W);
 }
 
 template void sub_conv0<float>(const float*, int, int, const BatchEntry*, int, int, const float*, const float*, float*,
