@@ -137,6 +137,22 @@ UD_API ud_status ud_step_batch_device(ud_engine* e, int n, const ud_stream_id* i
 UD_API ud_status ud_rnnt_decode(ud_engine* e, ud_stream_id id, const float* f, int frames, int32_t* tokens_out,
                          int* n_tokens_out);
 
+/* Allocation-free variant of ud_rnnt_decode (no reference counterpart: the reference's decoder allocates its
+ * tensors per call). Same arguments, results and carried decoder state, but the call's scratch (the frames, the
+ * batch entry, the token buffer and count) lives in one fixed 256 KiB block of the library's static device
+ * memory, and the call makes no cudaMalloc, cudaFree or host heap allocation. It is for callers that must not
+ * allocate: a real-time audio thread, where an allocation can take a lock or wait for the device to go idle and
+ * so miss the buffer deadline, and processes whose device memory is already fully reserved by another
+ * allocator, where a new cudaMalloc fails.
+ * Limit: 256 + 4*frames*max_symbols (rounded up to 256) + 4*frames*joint_dim <= 262144 bytes (100 frames at
+ * joint_dim 640 and max_symbols 10); larger calls return UD_ERR_INVALID_ARGUMENT.
+ * The block is shared by every engine and thread on a device: overlapping calls on one device race, and the
+ * caller must serialize them. The first call on each device resolves the block's address
+ * (cudaGetSymbolAddress) and must come before any stream capture on that device. Rejections return the status
+ * and clear the message that ud_last_error reports. */
+UD_API ud_status ud_rnnt_decode_static(ud_engine* e, ud_stream_id id, const float* f, int frames,
+                                       int32_t* tokens_out, int* n_tokens_out);
+
 /* Cache operations on the paged per-stream rings (the reference's cache roll, FastConformer.swift:464-477).
  * kind: 0 = K (projected keys), 1 = V (projected values), 2 = conv (depthwise-conv inputs).
  * Rows are in the engine dtype (bf16 or fp32), d_model wide, device pointers.

@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -952,6 +953,38 @@ float half_to_float(uint16_t h) {
 }  // namespace
 
 // ================================================================= C ABI
+// ---- Allocation-free RNN-T decode -------------------------------------------------------------------------
+// ud_rnnt_decode_static stages its per-call scratch (the batch entry, the token count, the token buffer and the
+// frames) in this fixed block of the module's static device memory instead of the engine workspace. One block
+// per device, shared by every engine and thread on that device.
+namespace {
+
+constexpr size_t kStaticScratchBytes = 256 * 1024;
+constexpr size_t kScrMeta = 0, kScrCount = 128, kScrTokens = 256;   // byte offsets; frames follow the tokens
+constexpr int kMaxScratchDevices = 64;
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_rnnt_scratch[kStaticScratchBytes];
+
+namespace {
+
+std::mutex g_scratch_mu;
+unsigned char* g_scratch_addr[kMaxScratchDevices];   // resolved once per device
+
+// Rejections record no message: building one could allocate.
+ud_status quiet(ud_status s) {
+    g_last_error.clear();
+    return s;
+}
+
+#define UD_CK_QUIET(call)                                  \
+    do {                                                   \
+        if ((call) != cudaSuccess) return quiet(UD_ERR_CUDA); \
+    } while (0)
+
+}  // namespace
+
 extern "C" {
 
 void ud_config_default(ud_config* c) {
@@ -1388,6 +1421,58 @@ ud_status ud_rnnt_decode(ud_engine* e, ud_stream_id id, const float* f, int fram
     const int nt = e->h_ntok[0];
     UD_CK(cudaMemcpyAsync(tokens_out, e->tok_dev, sizeof(int32_t) * nt, cudaMemcpyDeviceToHost, e->stream));
     UD_CK(cudaStreamSynchronize(e->stream));
+    *n_tokens_out = nt;
+    return UD_OK;
+}
+
+ud_status ud_rnnt_decode_static(ud_engine* e, ud_stream_id id, const float* f, int frames, int32_t* tokens_out,
+                                int* n_tokens_out) {
+    if (!e || !f || !tokens_out || !n_tokens_out) return quiet(UD_ERR_INVALID_ARGUMENT);
+    if (!e->loaded) return quiet(UD_ERR_NOT_READY);
+    if (!e->cfg.joint_dim) return quiet(UD_ERR_INVALID_ARGUMENT);
+    if (id < 0 || id >= e->cfg.max_streams || !e->slots[id].open) return quiet(UD_ERR_INVALID_ARGUMENT);
+    if (frames < 0 || e->device < 0 || e->device >= kMaxScratchDevices) return quiet(UD_ERR_INVALID_ARGUMENT);
+    const size_t tok_cap = static_cast<size_t>(frames) * e->cfg.max_symbols;
+    const size_t feat_off = (kScrTokens + sizeof(int32_t) * tok_cap + 255) & ~static_cast<size_t>(255);
+    const size_t feat_bytes = sizeof(float) * static_cast<size_t>(frames) * e->J;
+    if (feat_off + feat_bytes > kStaticScratchBytes) return quiet(UD_ERR_INVALID_ARGUMENT);   // beyond the block
+    *n_tokens_out = 0;
+    if (frames == 0) return UD_OK;
+    UD_CK_QUIET(cudaSetDevice(e->device));
+    unsigned char* scr = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_scratch_mu);
+        if (!g_scratch_addr[e->device]) {
+            void* p = nullptr;
+            UD_CK_QUIET(cudaGetSymbolAddress(&p, g_rnnt_scratch));
+            g_scratch_addr[e->device] = static_cast<unsigned char*>(p);
+        }
+        scr = g_scratch_addr[e->device];
+    }
+    BatchEntry* meta = reinterpret_cast<BatchEntry*>(scr + kScrMeta);
+    int* count = reinterpret_cast<int*>(scr + kScrCount);
+    int32_t* tokens = reinterpret_cast<int32_t*>(scr + kScrTokens);
+    float* feats = reinterpret_cast<float*>(scr + feat_off);
+    BatchEntry me;
+    std::memset(&me, 0, sizeof(me));
+    me.slot = id;
+    me.keep = frames;
+    me.T = frames;
+    // The count must read zero if the kernel never ran; the kernel overwrites it and fills tokens [0, count).
+    UD_CK_QUIET(cudaMemcpyAsync(meta, &me, sizeof(me), cudaMemcpyHostToDevice, e->stream));
+    UD_CK_QUIET(cudaMemsetAsync(count, 0, sizeof(int), e->stream));
+    UD_CK_QUIET(cudaMemcpyAsync(feats, f, feat_bytes, cudaMemcpyHostToDevice, e->stream));
+    rnnt_greedy(e->rw, e->rs, feats, e->J, meta, 1, tokens, static_cast<int>(tok_cap), count, e->stream);
+    e->launches++;
+    UD_CK_QUIET(cudaGetLastError());
+    int nt = 0;
+    UD_CK_QUIET(cudaMemcpyAsync(&nt, count, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    UD_CK_QUIET(cudaStreamSynchronize(e->stream));
+    if (nt < 0 || static_cast<size_t>(nt) > tok_cap) return quiet(UD_ERR_CUDA);
+    if (nt > 0) {
+        UD_CK_QUIET(cudaMemcpyAsync(tokens_out, tokens, sizeof(int32_t) * nt, cudaMemcpyDeviceToHost, e->stream));
+        UD_CK_QUIET(cudaStreamSynchronize(e->stream));
+    }
     *n_tokens_out = nt;
     return UD_OK;
 }

@@ -35,6 +35,7 @@ KINDS = ["gemm_tc", "gemm_simt", "attention", "conv", "norm", "subsample", "rnnt
 ABI_SYMBOLS = [
     "ud_config_default", "ud_init", "ud_shutdown", "ud_load_weights", "ud_load_safetensors", "ud_stream_open",
     "ud_stream_close", "ud_stream_step", "ud_step_batch", "ud_step_batch_device", "ud_rnnt_decode",
+    "ud_rnnt_decode_static",
     "ud_cache_append", "ud_cache_roll", "ud_cache_gather", "ud_cache_evict", "ud_cache_read", "ud_stream_info",
     "ud_get_cuda_stream", "ud_pool_info", "ud_synchronize", "ud_launch_count", "ud_debug_gemm",
     "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
@@ -84,6 +85,7 @@ def lib() -> C.CDLL:
             "ud_step_batch": (I, [eng, I, P(C.c_int32), P(P(F)), P(I), P(I), P(I), P(F), P(I), P(C.c_int32), P(I)]),
             "ud_step_batch_device": (I, [eng, I, P(C.c_int32), VP, I, P(I), P(I), P(I), VP, P(I), VP, VP]),
             "ud_rnnt_decode": (I, [eng, C.c_int32, P(F), I, P(C.c_int32), P(I)]),
+            "ud_rnnt_decode_static": (I, [eng, C.c_int32, P(F), I, P(C.c_int32), P(I)]),
             "ud_cache_append": (I, [eng, I, P(C.c_int32), I, VP, VP]),
             "ud_cache_roll": (I, [eng, I, P(C.c_int32), I]),
             "ud_cache_gather": (I, [eng, I, P(C.c_int32), VP, VP]),
@@ -272,6 +274,15 @@ class Engine:
         toks = np.zeros(max(1, f.shape[0] * self.cfg.max_symbols), np.int32)
         nt = C.c_int()
         check(lib().ud_rnnt_decode(self.h, sid, _ptr(f), f.shape[0], _ptr(toks, C.c_int32), C.byref(nt)))
+        return toks[:nt.value].tolist()
+
+    def rnnt_decode_static(self, sid: int, f: np.ndarray) -> list[int]:
+        """ud_rnnt_decode_static: the same decode with its scratch in the library's static device block (no
+        allocation in the call; overlapping calls on one device race)."""
+        f = np.ascontiguousarray(f, dtype=np.float32)
+        toks = np.zeros(max(1, f.shape[0] * self.cfg.max_symbols), np.int32)
+        nt = C.c_int()
+        check(lib().ud_rnnt_decode_static(self.h, sid, _ptr(f), f.shape[0], _ptr(toks, C.c_int32), C.byref(nt)))
         return toks[:nt.value].tolist()
 
     # ---------------------------------------------------------------- caches
