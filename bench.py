@@ -309,7 +309,8 @@ def run_gemm_bench(args, local):
     """The tcgen05 GEMM alone on one encoder layer's projection shapes, M = streams x (lookahead + 1) rows, with
     each shape's epilogue (SiLU, residual, output type). Every call reads one of 24 weight copies in turn, as
     the 24 layers do, so weights stream from HBM; device time per launch comes from the engine's per-launch
-    CUDA events. One JSON line: total FLOPs / total device time, with per-shape TFLOP/s."""
+    CUDA events. One JSON line: total FLOPs / total device time, with per-shape TFLOP/s and, for context,
+    cuBLAS's time for the same product (torch.matmul back to back, no epilogue)."""
     import ud
 
     dev = torch.device("cuda", local)
@@ -342,7 +343,21 @@ def run_gemm_bench(args, local):
         if n != args.steps:
             raise RuntimeError(f"{name}: {n} tensor-core GEMM launches for {args.steps} calls")
         flop = 2.0 * M * N * K * args.steps
-        per_shape[f"{name} {M}x{N}x{K}"] = {"us": ms * 1e3 / n, "tflops": flop / (ms / 1e3) / 1e12}
+        # For context only: cuBLAS (torch.matmul, bf16 output, no epilogue) on the same operands.
+        ref_out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        for i in range(args.warmup):
+            torch.matmul(A, Ws[i % 24].t(), out=ref_out)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record()
+        for i in range(args.steps):
+            torch.matmul(A, Ws[i % 24].t(), out=ref_out)
+        c1.record()
+        c1.synchronize()
+        cublas_ms = c0.elapsed_time(c1)
+        per_shape[f"{name} {M}x{N}x{K}"] = {"us": ms * 1e3 / n, "tflops": flop / (ms / 1e3) / 1e12,
+                                            "cublas_us": cublas_ms * 1e3 / args.steps,
+                                            "cublas_tflops": flop / (cublas_ms / 1e3) / 1e12}
+        del ref_out
         tot_flop += flop
         tot_ms += ms
         launches += n

@@ -103,7 +103,7 @@ struct ud_engine {
     float* x = nullptr;
     void *h = nullptr, *hid = nullptr, *qkv = nullptr, *att = nullptr, *pw = nullptr, *y = nullptr;
     float* proj = nullptr;
-    void *a1 = nullptr, *a2 = nullptr, *a3 = nullptr, *a4 = nullptr, *a5 = nullptr;
+    void *a2 = nullptr, *a3 = nullptr, *a4 = nullptr, *a5 = nullptr;
     float* subout = nullptr;
     float* in_stage = nullptr;
     float* out_stage = nullptr;
@@ -371,16 +371,11 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         {
             Launch L_(e, UD_KIND_SUBSAMPLE);
             if (e->bf)
-                sub_conv0<bf16>(in_dev, rows_stride, e->cfg.mel_bins, md, n, Tin, e->c0_w, e->c0_b, (bf16*)e->a1, T1, e->F1, C, st);
+                sub_conv01<bf16>(in_dev, rows_stride, e->cfg.mel_bins, md, n, Tin, e->c0_w, e->c0_b, T1, e->F1, e->c2_w,
+                                 e->c2_b, (bf16*)e->a2, T2, e->F2, C, e->num_sms, st);
             else
-                sub_conv0<float>(in_dev, rows_stride, e->cfg.mel_bins, md, n, Tin, e->c0_w, e->c0_b, (float*)e->a1, T1, e->F1, C, st);
-        }
-        {
-            Launch L_(e, UD_KIND_SUBSAMPLE);
-            if (e->bf)
-                sub_dwconv<bf16>((bf16*)e->a1, T1, e->F1, nullptr, 1, md, n, e->c2_w, e->c2_b, (bf16*)e->a2, T2, e->F2, C, st);
-            else
-                sub_dwconv<float>((float*)e->a1, T1, e->F1, nullptr, 1, md, n, e->c2_w, e->c2_b, (float*)e->a2, T2, e->F2, C, st);
+                sub_conv01<float>(in_dev, rows_stride, e->cfg.mel_bins, md, n, Tin, e->c0_w, e->c0_b, T1, e->F1, e->c2_w,
+                                  e->c2_b, (float*)e->a2, T2, e->F2, C, e->num_sms, st);
         }
         GemmEpilogue g3 = epi_out(e->a3, C, true, e);
         g3.bias = e->c3_b;
@@ -389,9 +384,9 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         {
         Launch L_(e, UD_KIND_SUBSAMPLE);
         if (e->bf)
-            sub_dwconv<bf16>((bf16*)e->a3, T2, e->F2, nullptr, 2, md, n, e->c5_w, e->c5_b, (bf16*)e->a4, T3, e->F3, C, st);
+            sub_dwconv2<bf16>((bf16*)e->a3, T2, e->F2, md, n, e->c5_w, e->c5_b, (bf16*)e->a4, T3, e->F3, C, st);
         else
-            sub_dwconv<float>((float*)e->a3, T2, e->F2, nullptr, 2, md, n, e->c5_w, e->c5_b, (float*)e->a4, T3, e->F3, C, st);
+            sub_dwconv2<float>((float*)e->a3, T2, e->F2, md, n, e->c5_w, e->c5_b, (float*)e->a4, T3, e->F3, C, st);
         }
         GemmEpilogue g6 = epi_out(e->a5, C, true, e);
         g6.bias = e->c6_b;
@@ -1141,8 +1136,7 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
     if ((s = dalloc_bytes(e, &e->y, Mc * D * es)) != UD_OK) return cleanup(s);
     if (c.joint_dim && (s = dalloc(e, &e->proj, Mc * c.joint_dim)) != UD_OK) return cleanup(s);
     if (sub) {
-        const size_t T1 = nxt(e->max_rows_in), T2 = nxt(T1), T3 = nxt(T2), C = e->C;
-        if ((s = dalloc_bytes(e, &e->a1, B * T1 * e->F1 * C * es)) != UD_OK) return cleanup(s);
+        const size_t T2 = nxt(nxt(e->max_rows_in)), T3 = nxt(T2), C = e->C;   // conv0's output is never stored
         if ((s = dalloc_bytes(e, &e->a2, B * T2 * e->F2 * C * es)) != UD_OK) return cleanup(s);
         if ((s = dalloc_bytes(e, &e->a3, B * T2 * e->F2 * C * es)) != UD_OK) return cleanup(s);
         if ((s = dalloc_bytes(e, &e->a4, B * T3 * e->F3 * C * es)) != UD_OK) return cleanup(s);

@@ -34,7 +34,8 @@ struct TcCfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 256;   // epilogue staging after the barriers
+    static constexpr int SMEM = EPI_OFF + 8 * kEpiStageBytes + 1024;
 };
 
 template <int BN>
@@ -55,6 +56,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     volatile int* abort_v = abort_flag;
+    float* epi_stage = reinterpret_cast<float*>(smem + C::EPI_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_m = (M + BM - 1) / BM;
@@ -131,7 +133,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int q = warp & 3;                       // TMEM lane quadrant accessible to this warp
         const int half = (warp - 2) >> 2;             // which half of the tile's columns
-        const int cbeg = half * (BN / 2), cend = cbeg + BN / 2;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -141,21 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const int row = mb * BM + q * 32 + lane;
-            const bool live = row < M;
-            const bool res = epi.residual != nullptr && live;
             const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-            float rnext[32];
-            if (res) load_residual32(epi, row, nb * BN + cbeg, rnext);
-#pragma unroll 1
-            for (int c0 = cbeg; c0 < cend; c0 += 32) {
-                float v[32], rcur[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) rcur[j] = rnext[j];
-                if (res && c0 + 32 < cend) load_residual32(epi, row, nb * BN + c0 + 32, rnext);
-                tmem_ld32(t_row + static_cast<uint32_t>(c0), v);
-                if (live) epilogue_store32(epi, row, nb * BN + c0, v, rcur);
-            }
+            // the two warps of a lane quadrant take the two halves of the tile's 16-column blocks
+            epi_drain(epi, epi_stage + (warp - 2) * kEpiStageFloats, t_row, mb * BM + q * 32, M, nb * BN,
+                      half * (BN / 32), (half + 1) * (BN / 32), lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);

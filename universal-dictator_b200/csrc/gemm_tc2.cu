@@ -34,7 +34,8 @@ struct Tc2Cfg {
     static constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile (a full 128-row box)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 256;   // epilogue staging after the barriers
+    static constexpr int SMEM = EPI_OFF + kEpiWarps * kEpiStageBytes + 1024;
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -100,6 +101,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     volatile int* abort_v = abort_flag;
+    float* epi_stage = reinterpret_cast<float*>(smem + C::EPI_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_rank();
@@ -196,28 +198,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             tc_fence_after();
-            const int row = mb * BM2 + static_cast<int>(rank) * 128 + q * 32 + lane;
-            const bool live = row < M;
-            const bool res = epi.residual != nullptr && live;
+            const int row0 = mb * BM2 + static_cast<int>(rank) * 128 + q * 32;
             const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-            float rnext[32];
-            if (res && b0 + 2 <= b1) load_residual32(epi, row, c0 + b0 * 16, rnext);
-            int blk = b0;
-#pragma unroll 1
-            for (; blk + 2 <= b1; blk += 2) {   // 32-column chunks, the next chunk's residual in flight
-                float v[32], rcur[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) rcur[j] = rnext[j];
-                if (res && blk + 4 <= b1) load_residual32(epi, row, c0 + (blk + 2) * 16, rnext);
-                tmem_ld32(t_row + static_cast<uint32_t>(blk * 16), v);
-                if (live) epilogue_store32(epi, row, c0 + blk * 16, v, rcur);
-            }
-            if (blk < b1) {   // a 16-column tail when this warp's share is an odd number of blocks
-                float v[16], r16[16];
-                if (res) load_residual16(epi, row, c0 + blk * 16, r16);
-                tmem_ld16(t_row + static_cast<uint32_t>(blk * 16), v);
-                if (live) epilogue_store16(epi, row, c0 + blk * 16, v, r16);
-            }
+            epi_drain(epi, epi_stage + (warp - 2) * kEpiStageFloats, t_row, row0, M, c0, b0, b1, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(peer_addr(smem_u32(&acc_empty[acc]), 0));

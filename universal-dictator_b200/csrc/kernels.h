@@ -111,12 +111,15 @@ void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, con
                  int ldo, cudaStream_t s);
 
 // ---- Subsampling (causal dw-striding x8, channel-last activations [b][t][f][c]).
+// conv0 + ReLU fused with the stage-1 depthwise conv: mel [n][rows_stride][mel_bins] -> out [n][T2][F2][C].
 template <typename T>
-void sub_conv0(const float* mel, int rows_stride, int mel_bins, const BatchEntry* meta, int n, int Tin,
-               const float* w, const float* b, T* out, int T1, int F1, int C, cudaStream_t s);
+void sub_conv01(const float* mel, int rows_stride, int mel_bins, const BatchEntry* meta, int n, int Tin, const float* w0,
+                const float* b0, int T1, int F1, const float* w1, const float* b1, T* out, int T2, int F2, int C,
+                int num_sms, cudaStream_t s);
+// Stage-2 depthwise conv: in [n][Tin][Fin][C] -> out [n][Tout][Fout][C].
 template <typename T>
-void sub_dwconv(const T* in, int Tin, int Fin, const int* in_valid_by_stage, int stage, const BatchEntry* meta,
-                int n, const float* w, const float* b, T* out, int Tout, int Fout, int C, cudaStream_t s);
+void sub_dwconv2(const T* in, int Tin, int Fin, const BatchEntry* meta, int n, const float* w, const float* b, T* out,
+                 int Tout, int Fout, int C, cudaStream_t s);
 template <typename T>
 void sub_select(const float* sub_out, int T3, const float* out_bias, const BatchEntry* meta, int n, float* x,
                 int D, cudaStream_t s);

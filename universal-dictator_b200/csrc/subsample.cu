@@ -17,32 +17,181 @@ namespace {
 __device__ __forceinline__ int nxt(int t) { return t / 2 + 1; }
 
 // Taps are stored tap-major, w[k * C + c] (transposed from the checkpoint's [C][1][3][3] at load).
-// One CTA per (stream, output row). Each thread owns one 8-channel group (its 72 taps in registers) and steps
-// over output frequencies; the three input mel rows sit in shared memory and are read as broadcasts.
+//
+// conv0 (1 -> C channels, 3x3 stride 2, ReLU, rows >= v1 zero) fused with the stage-1 depthwise conv (3x3
+// stride 2 over conv0's output, input rows >= v1 zero): conv0's output is never stored. Persistent: each CTA
+// walks stage-1 output rows (stream b, row t2) with a stride of the grid; a row needs conv0 rows 2 t2 - 2 .. 2 t2,
+// i.e. mel rows 4 t2 - 6 .. 4 t2 (7 rows), staged in shared memory by zero-filling cp.async, the next row's
+// while the current one is computed. Each thread owns one channel group (conv0 taps in registers, loaded once)
+// and a contiguous run of output columns, carrying the conv0 column shared by neighbouring outputs
+// (f1 = 2 f2). Sums keep the order of the two separate convolutions (bias, then taps kh-major, kw-minor), in
+// fp32 throughout.
+__device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, bool ok) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(ok ? 4 : 0)
+                 : "memory");
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
-                                                    const BatchEntry* __restrict__ meta, int Tin,
-                                                    const float* __restrict__ w, const float* __restrict__ bias,
-                                                    T* __restrict__ out, int T1, int F1, int C) {
+__global__ void __launch_bounds__(256, 1) conv01_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
+                                                        const BatchEntry* __restrict__ meta, int Tin,
+                                                        const float* __restrict__ w0, const float* __restrict__ b0,
+                                                        int T1, int F1, const float* __restrict__ w1,
+                                                        const float* __restrict__ b1, T* __restrict__ out, int T2,
+                                                        int F2, int C, int rows_total) {
     pdl_launch_dependents();
     pdl_wait();
     constexpr int VW = Vec16<T>::N;
-    extern __shared__ float xs[];           // [3][mel_bins + 3], frequency index shifted by the left pad of 2
-    const int W = mel_bins + 3;
+    extern __shared__ __align__(16) float sm[];
+    const int W = mel_bins + 3;                           // mel columns shifted by the left pad of 2
+    float* w1s = sm;                                      // [9][C]
+    float* b1s = w1s + 9 * C;                             // [C]
+    float* xs = b1s + C;                                  // [2][7][W]
+    // mel rows 4 t2 - 6 .. 4 t2 of row r into dst (zeros outside the stream's valid rows and the frequency pad)
+    auto prefetch = [&](int r, float* dst) {
+        const int b = r / T2, t2 = r % T2;
+        const int vm = meta[b].valid_mel;
+        const int mel0 = 4 * t2 - 6;
+        for (int i = threadIdx.x; i < 7 * W; i += blockDim.x) {
+            const int rr = i / W, q = i % W - 2;
+            const int row = mel0 + rr;
+            const bool ok = row >= 0 && row < vm && row < Tin && q >= 0 && q < mel_bins;
+            cp_async4_zfill(dst + i, ok ? mel + (static_cast<size_t>(b) * rows_stride + row) * mel_bins + q : mel, ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (blockIdx.x < rows_total) prefetch(blockIdx.x, xs);
+    for (int i = threadIdx.x; i < 9 * C; i += blockDim.x) w1s[i] = w1[i];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) b1s[i] = b1[i];
+
+    const int groups = C / VW;
+    const int lanes_f = blockDim.x / groups;
+    const int g = threadIdx.x % groups, fl = threadIdx.x / groups;
+    const int per = (F2 + lanes_f - 1) / lanes_f;
+    const int fa = fl * per, fb = fl < lanes_f ? min(F2, fa + per) : fa;
+    const int c = fl < lanes_f ? g * VW : 0;
+    float wr[9][VW], br[VW];
+#pragma unroll
+    for (int e = 0; e < VW; e += 4) {
+        const float4 bb = *reinterpret_cast<const float4*>(b0 + c + e);
+        br[e] = bb.x; br[e + 1] = bb.y; br[e + 2] = bb.z; br[e + 3] = bb.w;
+    }
+#pragma unroll
+    for (int k = 0; k < 9; ++k)
+#pragma unroll
+        for (int e = 0; e < VW; e += 4) {
+            const float4 ww = *reinterpret_cast<const float4*>(w0 + k * C + c + e);
+            wr[k][e] = ww.x; wr[k][e + 1] = ww.y; wr[k][e + 2] = ww.z; wr[k][e + 3] = ww.w;
+        }
+
+    int buf = 0;
+    for (int r = blockIdx.x; r < rows_total; r += gridDim.x) {
+        const int rn = r + gridDim.x;
+        if (rn < rows_total) prefetch(rn, xs + (buf ^ 1) * 7 * W);
+        else asm volatile("cp.async.commit_group;" ::: "memory");    // keeps one group per iteration
+        asm volatile("cp.async.wait_group 1;" ::: "memory");           // row r's group has landed
+        __syncthreads();
+        const float* x = xs + buf * 7 * W;
+        const int b = r / T2, t2 = r % T2;
+        const int v1 = nxt(meta[b].valid_mel);
+        bool row_ok[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int t1 = 2 * t2 - 2 + k;
+            row_ok[k] = t1 >= 0 && t1 < T1 && t1 < v1;
+        }
+        // conv0 output at (row 2 t2 - 2 + k, column f1) for this thread's channels; zero where masked or padded.
+        auto conv0 = [&](int k, int f1, float (&dst)[VW]) {
+            if (!row_ok[k] || f1 < 0 || f1 >= F1) {
+#pragma unroll
+                for (int e = 0; e < VW; ++e) dst[e] = 0.f;
+                return;
+            }
+#pragma unroll
+            for (int e = 0; e < VW; ++e) dst[e] = br[e];
+#pragma unroll
+            for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+                for (int kw = 0; kw < 3; ++kw) {
+                    const float xv = x[(2 * k + kh) * W + 2 * f1 + kw];
+#pragma unroll
+                    for (int e = 0; e < VW; ++e) dst[e] = fmaf(wr[kh * 3 + kw][e], xv, dst[e]);
+                }
+#pragma unroll
+            for (int e = 0; e < VW; ++e) dst[e] = fmaxf(dst[e], 0.f);
+        };
+        if (fa < fb) {
+            float left[3][VW];   // conv0 column 2 f2 - 2, carried from the previous output
+#pragma unroll
+            for (int k = 0; k < 3; ++k) conv0(k, 2 * fa - 2, left[k]);
+            for (int f2 = fa; f2 < fb; ++f2) {
+                float acc[VW];
+#pragma unroll
+                for (int e = 0; e < VW; e += 4) {
+                    const float4 bb = *reinterpret_cast<const float4*>(b1s + c + e);
+                    acc[e] = bb.x; acc[e + 1] = bb.y; acc[e + 2] = bb.z; acc[e + 3] = bb.w;
+                }
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    float mid[VW], right[VW];
+                    conv0(k, 2 * f2 - 1, mid);
+                    conv0(k, 2 * f2, right);
+#pragma unroll
+                    for (int e = 0; e < VW; e += 4) {
+                        const float4 wa = *reinterpret_cast<const float4*>(w1s + (k * 3 + 0) * C + c + e);
+                        const float4 wb = *reinterpret_cast<const float4*>(w1s + (k * 3 + 1) * C + c + e);
+                        const float4 wc = *reinterpret_cast<const float4*>(w1s + (k * 3 + 2) * C + c + e);
+                        const float a4[4] = {wa.x, wa.y, wa.z, wa.w}, b4[4] = {wb.x, wb.y, wb.z, wb.w};
+                        const float c4[4] = {wc.x, wc.y, wc.z, wc.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            acc[e + i] = fmaf(a4[i], left[k][e + i], acc[e + i]);
+                            acc[e + i] = fmaf(b4[i], mid[e + i], acc[e + i]);
+                            acc[e + i] = fmaf(c4[i], right[e + i], acc[e + i]);
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < VW; ++e) left[k][e] = right[e];
+                }
+                store16<T>(out + ((static_cast<size_t>(b) * T2 + t2) * F2 + f2) * C + c, acc);
+            }
+        }
+        __syncthreads();   // xs[buf] is refilled by the next iteration's prefetch
+        buf ^= 1;
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// Stage-2 depthwise conv (3x3 stride 2; input rows >= v2 = nxt(nxt(valid_mel)) read as zero). One CTA per
+// (stream, output row t): the three input rows 2t-2 .. 2t are staged in shared memory with 16-byte coalesced
+// loads (masked rows as zeros); each thread owns one channel group (taps in registers) and a run of output
+// columns.
+template <typename T>
+__global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, int Tin, int Fin,
+                                                      const BatchEntry* __restrict__ meta, const float* __restrict__ w,
+                                                      const float* __restrict__ bias, T* __restrict__ out, int Tout,
+                                                      int Fout, int C) {
+    pdl_launch_dependents();
+    pdl_wait();
+    constexpr int VW = Vec16<T>::N;
+    extern __shared__ __align__(16) unsigned char smraw[];
+    T* xs = reinterpret_cast<T*>(smraw);   // [3][Fin][C]
     const int b = blockIdx.x, t = blockIdx.y;
-    const int vm = meta[b].valid_mel;
-    const int v1 = nxt(vm);
-    for (int i = threadIdx.x; i < 3 * W; i += blockDim.x) {
-        const int r = i / W, q = i % W - 2;
-        const int row = 2 * t - 2 + r;
-        const bool ok = row >= 0 && row < vm && row < Tin && q >= 0 && q < mel_bins;
-        xs[i] = ok ? mel[(static_cast<size_t>(b) * rows_stride + row) * mel_bins + q] : 0.f;
+    const int vin = nxt(nxt(meta[b].valid_mel));
+    const int row_elems = Fin * C;
+    for (int k = 0; k < 3; ++k) {
+        const int r = 2 * t - 2 + k;
+        const bool ok = r >= 0 && r < Tin && r < vin;
+        const uint4* src = reinterpret_cast<const uint4*>(in + (static_cast<size_t>(b) * Tin + (ok ? r : 0)) * row_elems);
+        uint4* dst = reinterpret_cast<uint4*>(xs + k * row_elems);
+        for (int i = threadIdx.x; i < row_elems / VW; i += blockDim.x) dst[i] = ok ? src[i] : make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
     const int groups = C / VW;
-    const int lanes_f = blockDim.x / groups;  // threads sharing a channel group, each taking every lanes_f-th f
-    const int g = threadIdx.x % groups, f0 = threadIdx.x / groups;
-    if (f0 >= lanes_f) return;
+    const int lanes_f = blockDim.x / groups;
+    const int g = threadIdx.x % groups, fl = threadIdx.x / groups;
+    if (fl >= lanes_f) return;
+    const int per = (Fout + lanes_f - 1) / lanes_f;
+    const int fa = fl * per, fb = min(Fout, fa + per);
     const int c = g * VW;
     float wr[9][VW], br[VW];
 #pragma unroll
@@ -51,15 +200,13 @@ __global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ me
         br[e] = bb.x; br[e + 1] = bb.y; br[e + 2] = bb.z; br[e + 3] = bb.w;
     }
 #pragma unroll
-    for (int k = 0; k < 9; ++k)   // taps stored tap-major [9][C]: this thread's channels are contiguous
+    for (int k = 0; k < 9; ++k)
 #pragma unroll
         for (int e = 0; e < VW; e += 4) {
             const float4 ww = *reinterpret_cast<const float4*>(w + k * C + c + e);
             wr[k][e] = ww.x; wr[k][e + 1] = ww.y; wr[k][e + 2] = ww.z; wr[k][e + 3] = ww.w;
         }
-    T* orow = out + (static_cast<size_t>(b) * T1 + t) * F1 * C;
-    const bool live = t < v1;
-    for (int f = f0; f < F1; f += lanes_f) {
+    for (int f = fa; f < fb; ++f) {
         float acc[VW];
 #pragma unroll
         for (int e = 0; e < VW; ++e) acc[e] = br[e];
@@ -67,65 +214,13 @@ __global__ void __launch_bounds__(256) conv0_kernel(const float* __restrict__ me
         for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
             for (int kw = 0; kw < 3; ++kw) {
-                const float xv = xs[kh * W + 2 * f + kw];
-#pragma unroll
-                for (int e = 0; e < VW; ++e) acc[e] = fmaf(wr[kh * 3 + kw][e], xv, acc[e]);
-            }
-#pragma unroll
-        for (int e = 0; e < VW; ++e) acc[e] = live ? fmaxf(acc[e], 0.f) : 0.f;
-        store16<T>(orow + static_cast<size_t>(f) * C + c, acc);
-    }
-}
-
-// One CTA per (stream, output row); each thread owns one 8-channel group (taps in registers), steps over output
-// frequencies, and reads its inputs with 16-byte loads.
-template <typename T>
-__global__ void __launch_bounds__(256) dwconv_kernel(const T* __restrict__ in, int Tin, int Fin, int stage,
-                                                     const BatchEntry* __restrict__ meta, const float* __restrict__ w,
-                                                     const float* __restrict__ bias, T* __restrict__ out, int Tout,
-                                                     int Fout, int C) {
-    pdl_launch_dependents();
-    pdl_wait();
-    constexpr int VW = Vec16<T>::N;
-    const int b = blockIdx.x, t = blockIdx.y;
-    const int v1 = nxt(meta[b].valid_mel);
-    const int vin = stage == 1 ? v1 : nxt(v1);
-    const int groups = C / VW;
-    const int lanes_f = blockDim.x / groups;
-    const int g = threadIdx.x % groups, f0 = threadIdx.x / groups;
-    if (f0 >= lanes_f) return;
-    const int c = g * VW;
-    float wr[9][VW], br[VW];
-#pragma unroll
-    for (int e = 0; e < VW; e += 4) {
-        const float4 bb = *reinterpret_cast<const float4*>(bias + c + e);
-        br[e] = bb.x; br[e + 1] = bb.y; br[e + 2] = bb.z; br[e + 3] = bb.w;
-    }
-#pragma unroll
-    for (int k = 0; k < 9; ++k)   // taps stored tap-major [9][C]: this thread's channels are contiguous
-#pragma unroll
-        for (int e = 0; e < VW; e += 4) {
-            const float4 ww = *reinterpret_cast<const float4*>(w + k * C + c + e);
-            wr[k][e] = ww.x; wr[k][e + 1] = ww.y; wr[k][e + 2] = ww.z; wr[k][e + 3] = ww.w;
-        }
-    for (int f = f0; f < Fout; f += lanes_f) {
-        float acc[VW];
-#pragma unroll
-        for (int e = 0; e < VW; ++e) acc[e] = br[e];
-#pragma unroll
-        for (int kh = 0; kh < 3; ++kh) {
-            const int r = 2 * t + kh - 2;
-            if (r < 0 || r >= Tin || r >= vin) continue;
-#pragma unroll
-            for (int kw = 0; kw < 3; ++kw) {
                 const int q = 2 * f + kw - 2;
                 if (q < 0 || q >= Fin) continue;
                 float x[VW];
-                load16<T>(in + ((static_cast<size_t>(b) * Tin + r) * Fin + q) * C + c, x);
+                load16<T>(xs + (kh * Fin + q) * C + c, x);
 #pragma unroll
                 for (int e = 0; e < VW; ++e) acc[e] = fmaf(wr[kh * 3 + kw][e], x[e], acc[e]);
             }
-        }
         store16<T>(out + ((static_cast<size_t>(b) * Tout + t) * Fout + f) * C + c, acc);
     }
 }
@@ -174,18 +269,28 @@ __global__ void scatter_rows_kernel(const float* __restrict__ src, const BatchEn
 }  // namespace
 
 template <typename T>
-void sub_conv0(const float* mel, int rows_stride, int mel_bins, const BatchEntry* meta, int n, int Tin, const float* w,
-               const float* b, T* out, int T1, int F1, int C, cudaStream_t s) {
-    dim3 grid(n, T1);
-    const size_t smem = sizeof(float) * (3 * (mel_bins + 3));
-    launch_pdl(conv0_kernel<T>, dim3(grid), dim3(256), smem, s, mel, rows_stride, mel_bins, meta, Tin, w, b, out, T1, F1, C);
+void sub_conv01(const float* mel, int rows_stride, int mel_bins, const BatchEntry* meta, int n, int Tin, const float* w0,
+                const float* b0, int T1, int F1, const float* w1, const float* b1, T* out, int T2, int F2, int C,
+                int num_sms, cudaStream_t s) {
+    const int rows = n * T2;
+    if (rows <= 0) return;
+    const size_t smem = sizeof(float) * (9 * C + C + 2 * 7 * (mel_bins + 3));
+    const int grid = rows < num_sms ? rows : num_sms;
+    launch_pdl(conv01_kernel<T>, dim3(grid), dim3(256), smem, s, mel, rows_stride, mel_bins, meta, Tin, w0, b0, T1, F1,
+               w1, b1, out, T2, F2, C, rows);
 }
 
 template <typename T>
-void sub_dwconv(const T* in, int Tin, int Fin, const int*, int stage, const BatchEntry* meta, int n, const float* w,
-                const float* b, T* out, int Tout, int Fout, int C, cudaStream_t s) {
-    dim3 grid(n, Tout);
-    launch_pdl(dwconv_kernel<T>, dim3(grid), dim3(256), 0, s, in, Tin, Fin, stage, meta, w, b, out, Tout, Fout, C);
+void sub_dwconv2(const T* in, int Tin, int Fin, const BatchEntry* meta, int n, const float* w, const float* b, T* out,
+                 int Tout, int Fout, int C, cudaStream_t s) {
+    const size_t smem = sizeof(T) * 3 * static_cast<size_t>(Fin) * C;
+    static size_t attr_set[2] = {0, 0};
+    size_t& cur = attr_set[sizeof(T) == 4 ? 1 : 0];
+    if (smem > 48 * 1024 && smem > cur) {
+        cudaFuncSetAttribute(dwconv2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        cur = smem;
+    }
+    launch_pdl(dwconv2_kernel<T>, dim3(n, Tout), dim3(256), smem, s, in, Tin, Fin, meta, w, b, out, Tout, Fout, C);
 }
 
 template <typename T>
@@ -206,14 +311,14 @@ void scatter_rows(const float* src, const BatchEntry* meta, int n, float* dst, i
     launch_pdl(scatter_rows_kernel, dim3(grid), dim3(128), 0, s, src, meta, dst, tmax, W);
 }
 
-template void sub_conv0<float>(const float*, int, int, const BatchEntry*, int, int, const float*, const float*, float*,
-                               int, int, int, cudaStream_t);
-template void sub_conv0<bf16>(const float*, int, int, const BatchEntry*, int, int, const float*, const float*, bf16*, int,
-                              int, int, cudaStream_t);
-template void sub_dwconv<float>(const float*, int, int, const int*, int, const BatchEntry*, int, const float*,
-                                const float*, float*, int, int, int, cudaStream_t);
-template void sub_dwconv<bf16>(const bf16*, int, int, const int*, int, const BatchEntry*, int, const float*, const float*,
-                               bf16*, int, int, int, cudaStream_t);
+template void sub_conv01<float>(const float*, int, int, const BatchEntry*, int, int, const float*, const float*, int, int,
+                                const float*, const float*, float*, int, int, int, int, cudaStream_t);
+template void sub_conv01<bf16>(const float*, int, int, const BatchEntry*, int, int, const float*, const float*, int, int,
+                               const float*, const float*, bf16*, int, int, int, int, cudaStream_t);
+template void sub_dwconv2<float>(const float*, int, int, const BatchEntry*, int, const float*, const float*, float*, int,
+                                 int, int, cudaStream_t);
+template void sub_dwconv2<bf16>(const bf16*, int, int, const BatchEntry*, int, const float*, const float*, bf16*, int,
+                                int, int, cudaStream_t);
 template void sub_select<float>(const float*, int, const float*, const BatchEntry*, int, float*, int, cudaStream_t);
 
 }  // namespace ud
