@@ -37,9 +37,11 @@ template <int NV>
 __device__ __forceinline__ void row_stats(const float (&v)[NV][4], int D, float& mean, float& rstd) {
     constexpr int nv = NV;
     float s = 0.f;
+#pragma unroll
     for (int i = 0; i < nv; ++i) s += v[i][0] + v[i][1] + v[i][2] + v[i][3];
     mean = warp_sum(s) / static_cast<float>(D);
     float q = 0.f;
+#pragma unroll
     for (int i = 0; i < nv; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -48,6 +50,23 @@ __device__ __forceinline__ void row_stats(const float (&v)[NV][4], int D, float&
         }
     const float var = warp_sum(q) / static_cast<float>(D);
     rstd = rsqrtf(var + 1e-5f);
+}
+
+// gamma/beta for one float4 of this lane's columns (4 KB vectors shared by every row: L1-resident).
+__device__ __forceinline__ void load_affine4(const float* __restrict__ g, const float* __restrict__ b, int c, float (&gg)[4],
+                                             float (&bb)[4]) {
+    const float4 g4 = *reinterpret_cast<const float4*>(g + c), b4 = *reinterpret_cast<const float4*>(b + c);
+    gg[0] = g4.x; gg[1] = g4.y; gg[2] = g4.z; gg[3] = g4.w;
+    bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
+}
+
+template <int NV>
+__device__ __forceinline__ void load_row(const float* xr, int lane, float (&v)[NV][4]) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float4 t = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
+        v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
+    }
 }
 
 template <typename TO, int NV>
@@ -59,22 +78,18 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* x, const float* __
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= M) return;
-    constexpr int nv = NV;
-    const float* xr = x + static_cast<size_t>(row) * D;
     float v[NV][4];
-    for (int i = 0; i < nv; ++i) {
-        float4 t = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
-        v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
-    }
+    load_row<NV>(x + static_cast<size_t>(row) * D, lane, v);
     float mean, rstd;
     row_stats<NV>(v, D, mean, rstd);
     TO* yr = y + static_cast<size_t>(row) * D;
-    for (int i = 0; i < nv; ++i) {
-        const int c = (i * 32 + lane) * 4;
-        float o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * g[c + j] + b[c + j];
-        store4<TO>(yr + c, o);
+    for (int i = 0; i < NV; ++i) {
+        float gg[4], bb[4], o[4];
+        load_affine4(g, b, (i * 32 + lane) * 4, gg, bb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
+        store4<TO>(yr + (i * 32 + lane) * 4, o);
     }
 }
 
@@ -87,29 +102,28 @@ __global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const f
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= M) return;
-    constexpr int nv = NV;
     float* xr = x + static_cast<size_t>(row) * D;
     float v[NV][4];
-    for (int i = 0; i < nv; ++i) {
-        float4 t = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
-        v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
-    }
+    load_row<NV>(xr, lane, v);
     float mean, rstd;
     row_stats<NV>(v, D, mean, rstd);
-    for (int i = 0; i < nv; ++i) {
-        const int c = (i * 32 + lane) * 4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[i][j] = (v[i][j] - mean) * rstd * g1[c + j] + b1[c + j];
-        *reinterpret_cast<float4*>(xr + c) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+    for (int i = 0; i < NV; ++i) {
+        float gg[4], bb[4];
+        load_affine4(g1, b1, (i * 32 + lane) * 4, gg, bb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
+        *reinterpret_cast<float4*>(xr + (i * 32 + lane) * 4) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
     }
     row_stats<NV>(v, D, mean, rstd);
     TO* yr = y + static_cast<size_t>(row) * D;
-    for (int i = 0; i < nv; ++i) {
-        const int c = (i * 32 + lane) * 4;
-        float o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * g2[c + j] + b2[c + j];
-        store4<TO>(yr + c, o);
+    for (int i = 0; i < NV; ++i) {
+        float gg[4], bb[4], o[4];
+        load_affine4(g2, b2, (i * 32 + lane) * 4, gg, bb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
+        store4<TO>(yr + (i * 32 + lane) * 4, o);
     }
 }
 
