@@ -490,12 +490,14 @@ def main():
     tc_launches = prof["gemm_tc"][1] / 2
     flops = gemm_flops_per_step(n, T, R, cfg)
     achieved = flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else None
-    traffic = None
+    traffic, traffic_of = None, None
     tfile = ROOT / "profiles" / "gemm_tc_c3_traffic.txt"
     if tfile.exists():
         for line in tfile.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
                 traffic = float(line.split(":")[1])
+            elif line.startswith("kernel:"):
+                traffic_of = line.split(":", 1)[1].strip()
 
     # End to end through the host-buffer API (pinned host mel in, projections + tokens out), wall clock.
     e2e = None
@@ -547,6 +549,8 @@ def main():
                "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
                             "frac": (achieved / bf16_sus) if achieved else None, "traffic": traffic,
                             "kernel": "gemm_tc (tcgen05)",
+                            "traffic_of": (f"{traffic_of}: dram__bytes_read.sum + dram__bytes_write.sum from one ncu "
+                                           "capture (profiles/gemm_tc_c3_traffic.txt)") if traffic_of else None,
                             "note": f"algorithmic GEMM FLOPs per step / summed tcgen05 GEMM time per step "
                                     f"({tc_launches:.0f} launches), CUDA events on the engine stream; peak = "
                                     f"{src} sustained bf16"},

@@ -213,8 +213,11 @@ __global__ void __launch_bounds__(256) relpos_attn_kernel(const T* __restrict__ 
 //   BDraw = (Q + v) [16 x dk] . P^T [dk x np]           position term for every rel in the window
 //   S[i, j] = (AC[i, j] + BDraw[i, (L + i - j) - rel_min]) / sqrt(dk), softmax over visible keys (fp32)
 //   O     = softmax [16 x nk] (bf16) . V [nk x dk]
-// One CTA (4 warps) per (stream, head); K, V and the needed P rows are staged in shared memory with
-// cp.async; fragments come from ldmatrix (row stride 136 elements: conflict-free, 16-byte aligned rows).
+// One CTA (16 warps, two CTAs per SM) per (stream, head). A first pass writes each key's source row (cache
+// page or this chunk's QKV row) to a small table, so the copies of K, V and the needed P rows into shared
+// memory (cp.async) need no per-chunk page arithmetic; fragments come from ldmatrix (row stride 136 elements:
+// conflict-free, 16-byte aligned rows). The 13 AC/BD jobs of 16 columns run in one round over the warps, each
+// warp then normalises one query row, and each warp computes 8 output columns of O.
 namespace tc {
 
 constexpr int TM = 16;
@@ -236,6 +239,11 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t* r, const void* p) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(smem_u32(p)));
 }
+__device__ __forceinline__ void ldsm_x2_t(uint32_t* r, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(smem_u32(p)));
+}
 __device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -245,7 +253,7 @@ __device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b
 
 struct Lay {
     int nkp, npp, psw, acw, bdw;  // padded key rows (x16), padded position rows (x16), row strides
-    size_t qu, qv, k, v, p, ac, bd, pb, total;
+    size_t qu, qv, k, v, p, ac, bd, pb, kp, vp, total;
     __host__ __device__ Lay(int L) {
         nkp = (L + TM + 15) / 16 * 16;
         npp = (TM + L + TM - 1 + 15) / 16 * 16;
@@ -261,19 +269,22 @@ struct Lay {
         ac = o; o += sizeof(float) * TM * acw;
         bd = o; o += sizeof(float) * TM * bdw;
         pb = o; o += sizeof(bf16) * TM * psw;
+        o = (o + 15) / 16 * 16;
+        kp = o; o += sizeof(void*) * nkp;   // per-key source rows of K and V
+        vp = o; o += sizeof(void*) * nkp;
         total = (o + 127) / 128 * 128;
     }
 };
 
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 512;
 constexpr int kAttnWarps = kAttnThreads / 32;
 
-__global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __restrict__ qkv, int ld_qkv,
-                                                      const bf16* __restrict__ ptab, int tmax,
-                                                      const float* __restrict__ bias_u,
-                                                      const float* __restrict__ bias_v,
-                                                      const BatchEntry* __restrict__ meta, const CacheGeom cg,
-                                                      int layer, bf16* __restrict__ out, int ldo, int* err) {
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __restrict__ qkv, int ld_qkv,
+                                                         const bf16* __restrict__ ptab, int tmax,
+                                                         const float* __restrict__ bias_u,
+                                                         const float* __restrict__ bias_v,
+                                                         const BatchEntry* __restrict__ meta, const CacheGeom cg,
+                                                         int layer, bf16* __restrict__ out, int ldo, int* err) {
     pdl_launch_dependents();
     pdl_wait();
     constexpr int DKk = 128;
@@ -298,36 +309,43 @@ __global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __res
     float* AC = reinterpret_cast<float*>(sm + lay.ac);
     float* BD = reinterpret_cast<float*>(sm + lay.bd);
     bf16* Pb = reinterpret_cast<bf16*>(sm + lay.pb);
+    const bf16** KP = reinterpret_cast<const bf16**>(sm + lay.kp);
+    const bf16** VP = reinterpret_cast<const bf16**>(sm + lay.vp);
 
-    // ---- stage K and P (group 0) and V (group 1) with cp.async; zero the padding rows.
+    // ---- per-key source rows: cached frame f = head - L + j in its page, or this chunk's row j - L (null when
+    //      the page is not mapped, which is reported and read as zeros)
     const bf16* kpool = reinterpret_cast<const bf16*>(cg.kpool);
     const bf16* vpool = reinterpret_cast<const bf16*>(cg.vpool);
-    auto key_src = [&](int r, int c, const bf16*& ks, const bf16*& vs) -> bool {
+    for (int r = tid; r < nk; r += kAttnThreads) {
         const int j = lo + r;
+        const bf16 *ks = nullptr, *vs = nullptr;
         if (j < L) {
             const int f = head - L + j;
             const int page = me.pages[(f / PF) % kPageSlots];
-            if (page < 0 || page >= cg.n_pages) return false;
-            const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
-            ks = kpool + off;
-            vs = vpool + off;
+            if (page >= 0 && page < cg.n_pages) {
+                const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff;
+                ks = kpool + off;
+                vs = vpool + off;
+            } else {
+                report_error(err, DEV_BAD_PAGE);
+            }
         } else {
-            const bf16* src = qkv + static_cast<size_t>(row_off + (j - L)) * ld_qkv + hoff + c;
+            const bf16* src = qkv + static_cast<size_t>(row_off + (j - L)) * ld_qkv + hoff;
             ks = src + D;
             vs = src + 2 * D;
         }
-        return true;
-    };
+        KP[r] = ks;
+        VP[r] = vs;
+    }
+    __syncthreads();
+
+    // ---- stage K and P (group 0) and V (group 1) with cp.async; zero the padding rows.
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
     for (int idx = tid; idx < nk * 16; idx += kAttnThreads) {
         const int r = idx >> 4, c = (idx & 15) * 8;
-        const bf16 *ks, *vs;
-        if (!key_src(r, c, ks, vs)) {
-            report_error(err, DEV_BAD_PAGE);
-            *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
-            continue;
-        }
-        cp_async16(Ks + r * RSB + c, ks);
+        const bf16* ks = KP[r];
+        if (ks) cp_async16(Ks + r * RSB + c, ks + c);
+        else *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
     }
     for (int idx = tid; idx < np * 16; idx += kAttnThreads) {
         const int r = idx >> 4, c = (idx & 15) * 8;
@@ -336,12 +354,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __res
     asm volatile("cp.async.commit_group;" ::: "memory");
     for (int idx = tid; idx < nk * 16; idx += kAttnThreads) {
         const int r = idx >> 4, c = (idx & 15) * 8;
-        const bf16 *ks, *vs;
-        if (!key_src(r, c, ks, vs)) {
-            *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
-            continue;
-        }
-        cp_async16(Vs + r * RSB + c, vs);
+        const bf16* vs = VP[r];
+        if (vs) cp_async16(Vs + r * RSB + c, vs + c);
+        else *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     for (int idx = tid; idx < (lay.nkp - nk) * 16; idx += kAttnThreads) {
@@ -375,15 +390,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __res
     asm volatile("cp.async.wait_group 1;" ::: "memory");   // K and P have landed; V may still be in flight
     __syncthreads();
 
-    // ---- AC and BDraw: jobs of two n-tiles (16 columns), round-robin over the 4 warps.
+    // ---- AC and BDraw: jobs of two n-tiles (16 columns), one round over the warps.
     {
-        uint32_t aq[8][4], av[8][4];
         const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-            ldsm_x4(aq[ks], QU + arow * RSB + ks * 16 + acol);
-            ldsm_x4(av[ks], QV + arow * RSB + ks * 16 + acol);
-        }
         const int n_ac = (nk + 15) / 16, n_bd = (np + 15) / 16;
         const int g = lane >> 2, t4 = lane & 3;
         const int brow = (lane & 7) + ((lane >> 4) << 3), bcol = ((lane >> 3) & 1) * 8;
@@ -391,12 +400,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __res
             const bool is_ac = job < n_ac;
             const int n0 = (is_ac ? job : job - n_ac) * 16;
             const bf16* Bs = is_ac ? Ks : Ps;
+            const bf16* As = is_ac ? QU : QV;
             float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
-                uint32_t bfr[4];
+                uint32_t a[4], bfr[4];
+                ldsm_x4(a, As + arow * RSB + ks * 16 + acol);
                 ldsm_x4(bfr, Bs + (n0 + brow) * RSB + ks * 16 + bcol);
-                const uint32_t* a = is_ac ? aq[ks] : av[ks];
                 mma16816(c0, a, bfr[0], bfr[1]);
                 mma16816(c1, a, bfr[2], bfr[3]);
             }
@@ -410,7 +420,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __res
     }
     __syncthreads();
 
-    // ---- softmax rows (fp32), probabilities to bf16
+    // ---- softmax rows (fp32), probabilities to bf16: one query row per warp
     const float scale = rsqrtf(static_cast<float>(DKk));
     for (int i = warp; i < TM; i += kAttnWarps) {
         bf16* prow = Pb + i * lay.psw;
@@ -448,34 +458,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_tc_kernel(const bf16* __res
     asm volatile("cp.async.wait_group 0;" ::: "memory");   // V
     __syncthreads();
 
-    // ---- O = P . V: warp w owns output columns [16w, 16w + 16)
+    // ---- O = P . V: warp w owns output columns [8w, 8w + 8)
     {
-        float acc[2][4] = {};
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
-        const int vrow = (lane & 7) + ((lane >> 3) & 1) * 8, vcol = (lane >> 4) * 8;
+        const int n0 = warp * 8;
         const int ksteps = (nk + 15) / 16;
         for (int ks = 0; ks < ksteps; ++ks) {
-            uint32_t a[4];
+            uint32_t a[4], bfr[2];
             ldsm_x4(a, Pb + arow * lay.psw + ks * 16 + acol);
-            {
-                const int n0 = warp * 16;
-                uint32_t bfr[4];
-                ldsm_x4_t(bfr, Vs + (ks * 16 + vrow) * RSB + n0 + vcol);
-                mma16816(acc[0], a, bfr[0], bfr[1]);
-                mma16816(acc[1], a, bfr[2], bfr[3]);
-            }
+            ldsm_x2_t(bfr, Vs + (ks * 16 + (lane & 15)) * RSB + n0);
+            mma16816(acc, a, bfr[0], bfr[1]);
         }
         const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            const int col = hoff + warp * 16 + nt * 8 + 2 * t4;
-            if (g < T_)
-                *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g) * ldo + col) =
-                    __floats2bfloat162_rn(acc[nt][0], acc[nt][1]);
-            if (g + 8 < T_)
-                *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g + 8) * ldo + col) =
-                    __floats2bfloat162_rn(acc[nt][2], acc[nt][3]);
-        }
+        const int col = hoff + n0 + 2 * t4;
+        if (g < T_)
+            *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g) * ldo + col) =
+                __floats2bfloat162_rn(acc[0], acc[1]);
+        if (g + 8 < T_)
+            *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g + 8) * ldo + col) =
+                __floats2bfloat162_rn(acc[2], acc[3]);
     }
 
     // ---- append this chunk's K/V rows at frames head + t
