@@ -125,6 +125,7 @@ struct ud_engine {
     int* err_h = nullptr;
     int64_t launches = 0;
     std::map<std::tuple<const void*, int, int, int>, TmaMatrix> amaps;
+    std::map<std::tuple<const void*, int, int, int, int>, TmaMatrix> emaps;   // bf16 GEMM output blocks
     // CUDA graphs of the steady step, keyed by batch shape; metadata lives in a fixed device buffer for them
     struct GraphEntry {
         cudaGraphExec_t exec;
@@ -245,7 +246,19 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
                 it = e->amaps.emplace(key, t).first;
             }
             if (e->tc2_on && M >= 256 && W.N % 16 == 0) {
-                gemm_tc2(it->second, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, e->stream);
+                // tensor map of a bf16 output for the TMA epilogue (null when a map cannot describe it)
+                auto emap = [&](const void* p, int ld, bool bf) -> const TmaMatrix* {
+                    const auto k = std::make_tuple(p, M, W.N, ld, bf ? 1 : 0);
+                    auto jt = e->emaps.find(k);
+                    if (jt == e->emaps.end()) {
+                        TmaMatrix t;
+                        if (!make_tma_epi(t, p, M, W.N, ld, bf)) return nullptr;
+                        jt = e->emaps.emplace(k, t).first;
+                    }
+                    return &jt->second;
+                };
+                const TmaMatrix* om = (epi.out_bf16 && !epi.residual) ? emap(epi.out, epi.ldo, true) : nullptr;
+                gemm_tc2(it->second, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, om, e->stream);
             } else {
                 const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;
                 gemm_tc(it->second, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms,

@@ -216,6 +216,29 @@ bool make_tma_bf16(TmaMatrix& t, const void* base, int rows, int cols, int ld, i
     return true;
 }
 
+bool make_tma_epi(TmaMatrix& t, const void* base, int rows, int cols, int ld, bool bf16) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    const int esz = bf16 ? 2 : 4;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (static_cast<long long>(ld) * esz) % 16 != 0 ||
+        (cols * esz) % 128 != 0)
+        return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esz};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), 32u};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = enc(&t.map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+    t.base = base;
+    t.rows = rows;
+    t.cols = cols;
+    t.ld = ld;
+    t.box_rows = 32;
+    return true;
+}
+
 int gemm_tc_pick_bn(int M, int N, int num_sms) {
     const int num_m = (M + BM - 1) / BM;
     if (N % 256 == 0 && num_m * (N / 256) >= num_sms) return 256;

@@ -52,14 +52,19 @@ struct TmaMatrix {
     int rows = 0, cols = 0, ld = 0, box_rows = 0;
 };
 bool make_tma_bf16(TmaMatrix& t, const void* base, int rows, int cols, int ld, int box_rows);
+// Epilogue blocks: 32 rows x 128 bytes (32 fp32 or 64 bf16 columns), 128-byte swizzle, for TMA stores of GEMM
+// outputs.
+bool make_tma_epi(TmaMatrix& t, const void* base, int rows, int cols, int ld, bool bf16);
 int gemm_tc_pick_bn(int M, int N, int num_sms);
 void gemm_tc(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, int bn, const GemmEpilogue& epi,
              int* dev_err, int num_sms, cudaStream_t s);
 
 // 2-CTA variant (cluster of 2, cta_group::2), 256 x bn tiles per CTA pair; bn must be 256 and W's tensor map
 // must have 128-row boxes (each CTA loads half of the W tile). M >= 256 recommended.
+// out_map (may be null): the epilogue tensor map of epi.out (make_tma_epi); bf16 outputs without a residual are
+// then stored through TMA when every tile is 256 wide.
 void gemm_tc2(const TmaMatrix& A, const TmaMatrix& W_half, int M, int N, int K, int bn, const GemmEpilogue& epi,
-              int* dev_err, int num_sms, cudaStream_t s);
+              int* dev_err, int num_sms, const TmaMatrix* out_map, cudaStream_t s);
 
 // ---- SIMT GEMM for few rows (M small) and for the fp32 engine. TA/TW in {float, bf16}.
 template <typename TA, typename TW>
