@@ -50,6 +50,26 @@ def peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+def rank_streams(n: int, rank: int) -> list[int]:
+    """Global ids of the n streams rank `rank` owns: disjoint across ranks (streams are sharded, nothing is
+    shared), so each rank's synthetic input differs."""
+    return [rank * n + s for s in range(n)]
+
+
+def max_over_ranks(value: float, dist, device) -> float:
+    """The slowest rank's time: every rank contributes its own device time, all receive the maximum."""
+    if dist is None:
+        return value
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(units_per_rank: int, steps: int, world: int, t_max_ms: float) -> float:
+    """Units processed by all ranks per second of the slowest rank's time."""
+    return units_per_rank * steps * world / (t_max_ms / 1e3)
+
+
 def chunk_schedule(R: int, total_rows: int):
     """The live chunk walk (NemotronStreamer.swift:109-154) over a whole utterance: (start, rows) per step,
     first chunk 1+8R rows, then 9 pre-encode rows + 8+8R new rows; only full chunks."""
@@ -272,11 +292,7 @@ def run_cache_bench(args, world, rank, local):
         e1.synchronize()
     launches = eng.launch_count() - l0
     ms = e0.elapsed_time(e1)
-    t = ms
-    if dist:
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t = float(tt.item())
+    t = max_over_ranks(ms, dist, dev)
     per_step = total_bytes / args.steps
     gbs = total_bytes * world / (t / 1e3) / 1e9
     hbm, _, _, src = peaks()
@@ -433,8 +449,8 @@ def main():
 
     dev = torch.device("cuda", local)
     mel = torch.empty(n, TOTAL_ROWS, MEL, device=dev)
-    for s in range(n):
-        mel[s].normal_(generator=torch.Generator(device=dev).manual_seed(s))
+    for s, gid in enumerate(rank_streams(n, rank)):
+        mel[s].normal_(generator=torch.Generator(device=dev).manual_seed(gid))
     tm, J, ms = cfg.max_chunk_frames, cfg.joint_dim, cfg.max_symbols
     proj = torch.empty(n, tm, J, device=dev)
     toks = torch.empty(n, tm * ms, device=dev, dtype=torch.int32)
@@ -471,13 +487,10 @@ def main():
     eng.synchronize()
     launches = eng.launch_count() - l0
     ms_dev = ev0.elapsed_time(ev1)
-    t_max = ms_dev
+    t_max = max_over_ranks(ms_dev, dist, dev)
     if dist:
-        t = torch.tensor([ms_dev], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max = float(t.item())
         dist.barrier()
-    value = n * args.steps * world / (t_max / 1e3)
+    value = whole_job_rate(n, args.steps, world, t_max)
 
     # Kernel attribution (outside the timed region): per-class device time over two more steps.
     eng.profile(True)
@@ -526,14 +539,10 @@ def main():
         rows_sum = 0
         for _ in range(args.steps):
             rows_sum += step_host()
-        dt = time.perf_counter() - t0
-        if dist:
-            t = torch.tensor([dt], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            dt = float(t.item())
+        dt = max_over_ranks(time.perf_counter() - t0, dist, dev)
         h2d = rows_sum / args.steps * MEL * 4 * n
         d2h = n * tm * J * 4 + ((n * tm * ms * 4 + n * 4) if decode else 0)
-        e2e = {"value": n * args.steps * world / dt, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+        e2e = {"value": whole_job_rate(n, args.steps, world, dt * 1e3), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "timing": "host wall clock, synchronous ud_step_batch calls"}
 
     cpu = None

@@ -28,9 +28,11 @@ template <> struct Pair<bf16> {
 };
 
 // Each thread owns a channel pair; the time loop reads only the GLU input and this thread's ring rows, so
-// loads of different frames are independent (restrict pointers) and stay in flight together.
+// loads of different frames are independent (restrict pointers) and stay in flight together. Taps are stored
+// tap-major, w[k * D + c], so a warp reads each tap of its 64 channels with one coalesced 256-byte load. Two
+// CTAs fit on an SM (64 registers), so the 256 streams of a C3 batch run in one wave.
 template <typename T, int KW>
-__global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ pw, int ld_pw,
+__global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict__ pw, int ld_pw,
                                                           const float* __restrict__ dw, const float* __restrict__ g,
                                                           const float* __restrict__ beta,
                                                           const BatchEntry* __restrict__ meta, const CacheGeom cg,
@@ -48,8 +50,9 @@ __global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ 
         float w0[KW], w1[KW], a[KW], bq[KW];
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
-            w0[k] = dw[c * KW + k];
-            w1[k] = dw[(c + 1) * KW + k];
+            const float2 wk = *reinterpret_cast<const float2*>(dw + k * D + c);
+            w0[k] = wk.x;
+            w1[k] = wk.y;
         }
 #pragma unroll
         for (int i = 0; i < R; ++i) {  // frame head - R + i, read before any ring row is rewritten
@@ -109,8 +112,9 @@ __global__ void __launch_bounds__(512) conv_module_kernel(const T* __restrict__ 
         T* orow = out + static_cast<size_t>(row_off + t) * ldo;
         for (int c = lane * 2; c < D; c += 64) {
             const float2 v = *reinterpret_cast<const float2*>(yr + c);
-            const float z0 = (v.x - mean) * rstd * g[c] + beta[c];
-            const float z1 = (v.y - mean) * rstd * g[c + 1] + beta[c + 1];
+            const float2 gg = *reinterpret_cast<const float2*>(g + c), bb = *reinterpret_cast<const float2*>(beta + c);
+            const float z0 = (v.x - mean) * rstd * gg.x + bb.x;
+            const float z1 = (v.y - mean) * rstd * gg.y + bb.y;
             Pair<T>::st(orow + c, z0 / (1.f + expf(-z0)), z1 / (1.f + expf(-z1)));
         }
     }

@@ -777,7 +777,14 @@ ud_status load_weights_impl(ud_engine* e, const ud_weight* table, int n) {
         UD_TRY(need(t, s + "self_attn.linear_out.weight", {D, D}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {D}, D, w.wo));
         UD_TRY(need(t, s + "conv.pointwise_conv1.weight", {2 * D, D, 1}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {2 * D}, D, w.pw1));
         UD_TRY(need(t, s + "conv.pointwise_conv2.weight", {D, D, 1}, &a)); UD_TRY(upload_gemm(e, stg, {a}, {D}, D, w.pw2));
-        UD_TRY(need(t, s + "conv.depthwise_conv.weight", {D, 1, e->KC}, &a)); UD_TRY(upload_f32(e, a, D * e->KC, &w.dw));
+        UD_TRY(need(t, s + "conv.depthwise_conv.weight", {D, 1, e->KC}, &a));
+        {   // tap-major [KC][D] so a thread's channel pair reads each tap with one 8-byte load
+            std::vector<float> tm(static_cast<size_t>(D) * e->KC);
+            for (int c = 0; c < D; ++c)
+                for (int k = 0; k < e->KC; ++k) tm[static_cast<size_t>(k) * D + c] = a[static_cast<size_t>(c) * e->KC + k];
+            UD_TRY(upload_f32(e, tm.data(), tm.size(), &w.dw));
+            UD_CK(cudaStreamSynchronize(e->stream));   // tm is a temporary
+        }
         UD_TRY(need(t, s + "self_attn.pos_bias_u", {H, DK}, &a)); UD_TRY(upload_f32(e, a, D, &w.pos_u));
         UD_TRY(need(t, s + "self_attn.pos_bias_v", {H, DK}, &a)); UD_TRY(upload_f32(e, a, D, &w.pos_v));
         // Projected position table P = sinusoid(rel) . W_pos^T in fp32, stored in the engine dtype.
