@@ -22,17 +22,32 @@ __device__ __forceinline__ int nxt(int t) { return t / 2 + 1; }
 // stride 2 over conv0's output, input rows >= v1 zero): conv0's output is never stored. Persistent: each CTA
 // walks stage-1 output rows (stream b, row t2) with a stride of the grid; a row needs conv0 rows 2 t2 - 2 .. 2 t2,
 // i.e. mel rows 4 t2 - 6 .. 4 t2 (7 rows), staged in shared memory by zero-filling cp.async, the next row's
-// while the current one is computed. Each thread owns one channel group (conv0 taps in registers, loaded once)
+// while the current one is computed. Each thread owns four channels (conv0 taps in registers, loaded once)
 // and a contiguous run of output columns, carrying the conv0 column shared by neighbouring outputs
-// (f1 = 2 f2). Sums keep the order of the two separate convolutions (bias, then taps kh-major, kw-minor), in
-// fp32 throughout.
+// (f1 = 2 f2); 64 channel groups x 4 column lanes (9, 9, 9, 6 of the 33 columns), two CTAs per SM. Sums keep
+// the order of the two separate convolutions (bias, then taps kh-major, kw-minor), in fp32 throughout.
+
+// Four consecutive channels: 16 bytes (fp32) or 8 bytes (bf16).
+template <typename T>
+__device__ __forceinline__ void store4v(T* p, const float* v) {
+    if constexpr (sizeof(T) == 4) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&lo);
+        u.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(p) = u;
+    }
+}
+
 __device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, bool ok) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(ok ? 4 : 0)
                  : "memory");
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256, 1) conv01_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
+__global__ void __launch_bounds__(256, 2) conv01_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
                                                         const BatchEntry* __restrict__ meta, int Tin,
                                                         const float* __restrict__ w0, const float* __restrict__ b0,
                                                         int T1, int F1, const float* __restrict__ w1,
@@ -40,7 +55,7 @@ __global__ void __launch_bounds__(256, 1) conv01_kernel(const float* __restrict_
                                                         int F2, int C, int rows_total) {
     pdl_launch_dependents();
     pdl_wait();
-    constexpr int VW = Vec16<T>::N;
+    constexpr int VW = 4;   // channels per thread: 64 channel groups x 4 column lanes, two CTAs per SM
     extern __shared__ __align__(16) float sm[];
     const int W = mel_bins + 3;                           // mel columns shifted by the left pad of 2
     float* w1s = sm;                                      // [9][C]
@@ -152,7 +167,7 @@ __global__ void __launch_bounds__(256, 1) conv01_kernel(const float* __restrict_
 #pragma unroll
                     for (int e = 0; e < VW; ++e) left[k][e] = right[e];
                 }
-                store16<T>(out + ((static_cast<size_t>(b) * T2 + t2) * F2 + f2) * C + c, acc);
+                store4v<T>(out + ((static_cast<size_t>(b) * T2 + t2) * F2 + f2) * C + c, acc);
             }
         }
         __syncthreads();   // xs[buf] is refilled by the next iteration's prefetch
@@ -275,7 +290,7 @@ void sub_conv01(const float* mel, int rows_stride, int mel_bins, const BatchEntr
     const int rows = n * T2;
     if (rows <= 0) return;
     const size_t smem = sizeof(float) * (9 * C + C + 2 * 7 * (mel_bins + 3));
-    const int grid = rows < num_sms ? rows : num_sms;
+    const int grid = rows < 2 * num_sms ? rows : 2 * num_sms;
     launch_pdl(conv01_kernel<T>, dim3(grid), dim3(256), smem, s, mel, rows_stride, mel_bins, meta, Tin, w0, b0, T1, F1,
                w1, b1, out, T2, F2, C, rows);
 }
