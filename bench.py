@@ -315,6 +315,97 @@ def run_cache_bench(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_streamer_bench(args, world, rank, local):
+    """Config 4: concurrent streams through the host-side streamer (ud_streamer_*, NemotronStreamer's chunk walk)
+    at [70,6], `--c4-streams` slots per GPU (512 = 4096 over 8 GPUs). Streams arrive as a Poisson process of
+    200/s per GPU in audio time (a step advances every stream by one 0.56 s chunk), last U[2 s, 60 s], wait in a
+    queue for a free slot, and leave when their final chunk (keepAll) has run; greedy RNN-T decoding runs on
+    every kept frame with each stream's carried decoder state. Each stream's mel is a window of a seeded N(0,1)
+    host pool, all of it available at admission. Timing is the host wall clock around synchronous streamer steps
+    (host rows in, tokens out), max over ranks; value = stream-steps of all ranks per second."""
+    import ud
+    from oracle.weights import NEMOTRON, make_weights
+
+    R, slots, fps = 6, args.c4_streams, 100
+    chunk_s = (8 + 8 * R) / fps
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    cfg = ud.default_config(max_streams=slots, max_batch=slots, max_chunk_frames=16)
+    eng = ud.Engine(cfg, device=local)
+    sd = make_weights(NEMOTRON, seed=0)
+    sd["joint.joint_net.2.bias"][NEMOTRON.blank] += args.blank_offset
+    eng.load_weights(sd)
+    st = ud.Streamer(eng, R, decode=True)
+    rng = np.random.default_rng(1000 + rank)
+    pool = np.random.default_rng(rank).standard_normal((64 * 60 * fps, MEL), dtype=np.float32)
+    queue: list[int] = []          # lengths in rows of waiting streams
+    active: dict[int, int] = {}    # streamer id -> rows
+    stats = {"steps": 0, "admitted": 0, "finished": 0, "tokens": 0}
+
+    def step():
+        queue.extend(int(rng.uniform(2, 60) * fps) for _ in range(rng.poisson(200 * chunk_s)))
+        while queue and len(active) < slots:
+            n = queue.pop(0)
+            off = int(rng.integers(0, pool.shape[0] - n))
+            sid = st.open(pool[off:off + n])
+            st.push(sid, n, last=True)
+            active[sid] = n
+            stats["admitted"] += 1
+        n_stepped, n_done = st.step()
+        if n_done:
+            for sid in list(active):
+                toks, fin = st.tokens(sid)
+                if fin:
+                    stats["tokens"] += len(toks)
+                    st.release(sid)
+                    del active[sid]
+                    stats["finished"] += 1
+        return n_stepped
+
+    for _ in range(args.warmup):
+        step()
+    eng.synchronize()
+    if dist:
+        dist.barrier()
+    total = 0
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            total += step()
+        dt = time.perf_counter() - t0
+    t_max = max_over_ranks(dt * 1e3, dist, dev)
+    all_steps = total
+    if dist:
+        tt = torch.tensor([float(total)], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt)
+        all_steps = int(tt.item())
+    value = all_steps / (t_max / 1e3)
+    if rank == 0:
+        print(json.dumps({"metric": METRIC + " [C4 streamer]", "value": value, "unit": UNIT, "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max / args.steps,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                          "data": "synthetic",
+                          "config": {"workload": f"C4: {slots} stream slots/GPU, [70,6] (T=7, 65-row chunks), Poisson "
+                                                 "arrivals 200/s/GPU, lengths U[2 s, 60 s], greedy RNN-T per stream",
+                                     "blank_offset": args.blank_offset,
+                                     "stream_steps_per_step": all_steps / max(1, args.steps) / world,
+                                     "admitted": stats["admitted"], "finished": stats["finished"],
+                                     "tokens": stats["tokens"], "queue": len(queue),
+                                     "timing": "host wall clock, synchronous streamer steps (host mel in, tokens out)",
+                                     "parallelism": f"stream-sharded x{world}, no collectives"},
+                          "gpu_launches": None, "clocks": clk.summary()}), flush=True)
+    st.close()
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 GEMM_SHAPES = [  # (name, N, K, activation, residual, bf16 output): one encoder layer's projections
     ("ff.up", 4096, 1024, 2, False, True), ("ff.down", 1024, 4096, 0, True, False),
     ("attn.qkv", 3072, 1024, 0, False, True), ("attn.out", 1024, 1024, 0, True, False),
@@ -404,9 +495,14 @@ def main():
                     help="also run greedy RNN-T decoding in each step (configs 2 and 4; C3 is the encoder step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c5", "gemm"], default="c3",
-                    help="c3: the encoder step (default); c5: the cache-op microbenchmark; gemm: the tensor-core "
-                         "GEMM on one layer's shapes")
+    ap.add_argument("--workload", choices=["c3", "c4", "c5", "gemm"], default="c3",
+                    help="c3: the encoder step (default); c4: concurrent streams through the host-side streamer; "
+                         "c5: the cache-op microbenchmark; gemm: the tensor-core GEMM on one layer's shapes")
+    ap.add_argument("--c4-streams", type=int, default=512, help="c4: stream slots per GPU")
+    ap.add_argument("--blank-offset", type=float, default=1.0,
+                    help="c4: added to the joint's blank bias. With N(0,0.02) weights greedy decoding emits the "
+                         "10-symbol maximum on every frame below about 0.5 and no symbol from 1.0 up; 1.0 (the "
+                         "default) costs one joint evaluation per frame, 0 is the worst case")
     ap.add_argument("--cache-streams", type=int, default=1024, help="c5: streams per GPU")
     ap.add_argument("--cache-k", type=int, default=14, help="c5: frames appended per stream per step")
     args = ap.parse_args()
@@ -418,6 +514,9 @@ def main():
 
     if args.workload == "c5":
         run_cache_bench(args, world, rank, local)
+        return
+    if args.workload == "c4":
+        run_streamer_bench(args, world, rank, local)
         return
     if args.workload == "gemm":
         if rank == 0:

@@ -115,7 +115,8 @@ UD_API ud_status ud_stream_step(ud_engine* e, ud_stream_id id, const float* mel,
 
 /* Batched protocol calls over n distinct streams (one encoder pass for all of them), host buffers.
  * mel[i] points at stream i's rows. proj_out: n * max_chunk_frames * joint_dim floats, stream i at
- * proj_out + i*max_chunk_frames*joint_dim. If tokens_out is not NULL the RNN-T greedy decoder
+ * proj_out + i*max_chunk_frames*joint_dim (may be NULL when tokens are requested: the projections are then
+ * not copied out). If tokens_out is not NULL the RNN-T greedy decoder
  * (RNNT.swift:127-151) also runs on the kept frames with each stream's carried state:
  * tokens_out holds n * max_chunk_frames * max_symbols ids, stream i at offset
  * i*max_chunk_frames*max_symbols, and n_tokens_out[i] their count. Synchronous. */
@@ -208,6 +209,42 @@ UD_API ud_status ud_debug_gemm(ud_engine* e, const void* A, const void* W, int M
  * wait the pipelined kernels use; it gives up after limit_ns, and the call returns UD_ERR_DEVICE_TIMEOUT
  * with the engine still usable. */
 UD_API ud_status ud_debug_wait_probe(ud_engine* e, uint64_t limit_ns);
+
+/* The configuration the engine was created with. */
+UD_API ud_status ud_get_config(ud_engine* e, ud_config* out);
+
+/* ---- Host-side batched streamer (NemotronStreamer, Sources/DictatorCore/Nemotron/NemotronStreamer.swift:16-163)
+ *
+ * The chunk walk of one stream (runBuffered, NemotronStreamer.swift:70-91, and the live drainChunks, :109-154):
+ * the stream has consumed `idx` of the `avail` mel rows it has so far; `last` says no more rows will come.
+ * Returns 1 when a chunk is ready and fills rows [*start, *start + *n_rows) (the first chunk 1+8R rows with no
+ * pre-encode cache, later chunks 9 cached rows + 8+8R new rows, the final chunk shorter), *keep_all (the final
+ * chunk) and *next_idx; 0 when the stream must wait for rows (a full chunk is run only once more rows, or the
+ * end, have arrived, so the final chunk is known); -1 when it has ended (what remains is too short to encode). */
+UD_API int ud_chunk_next(int lookahead, int idx, int avail, int last, int* start, int* n_rows, int* keep_all,
+                         int* next_idx);
+
+/* A streamer drives many streams of one engine: each step runs every stream with a ready chunk in one batched
+ * encoder pass (ud_step_batch, with greedy RNN-T decoding when decode != 0) and appends the tokens to the
+ * stream. Streams read their mel from a caller-owned host buffer [capacity_rows, mel_bins] that stays valid
+ * until the stream is released; rows become available through ud_streamer_push. A stream's engine slot is
+ * taken at open (UD_ERR_POOL_EXHAUSTED when the engine has none free) and freed when its final chunk has run.
+ * Calls on one streamer are serialised by the caller. */
+typedef struct ud_streamer ud_streamer;
+typedef int32_t ud_streamer_id;
+UD_API ud_status ud_streamer_create(ud_engine* e, int lookahead, int decode, ud_streamer** out);
+UD_API ud_status ud_streamer_destroy(ud_streamer* s);
+UD_API ud_status ud_streamer_open(ud_streamer* s, const float* mel, int capacity_rows, ud_streamer_id* out);
+/* n_rows more rows are valid at the end of the stream's buffer; last != 0: the stream ends there. */
+UD_API ud_status ud_streamer_push(ud_streamer* s, ud_streamer_id id, int n_rows, int last);
+/* One batched step (at most max_batch streams, in order of id); *n_stepped streams advanced one chunk,
+ * *n_finished of them ran their final chunk (or ended with a remainder too short to encode). */
+UD_API ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished);
+/* Tokens so far (up to cap copied), the total count, and whether the stream has finished. */
+UD_API ud_status ud_streamer_tokens(ud_streamer* s, ud_streamer_id id, int32_t* out, int cap, int* n_tokens,
+                                    int* finished);
+/* Forgets a stream (closing its engine slot if it has not finished); its id may be reused. */
+UD_API ud_status ud_streamer_release(ud_streamer* s, ud_streamer_id id);
 
 /* Text of the last error on this thread ("" if none). Returns the full length. */
 UD_API size_t ud_last_error(char* buf, size_t len);

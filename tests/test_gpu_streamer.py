@@ -1,0 +1,117 @@
+"""The host-side batched streamer (ud_streamer_*, NemotronStreamer.swift:16-163) on the GPU.
+
+  * buffered streams of different lengths: each stream's tokens equal the oracle run stream by stream
+    (runBuffered's chunk walk, Encoder.stream_step, then RNNT.greedy with carried state);
+  * the same streams fed row by row in random increments (live input) give the same tokens;
+  * admission: opening more streams than the engine has slots is refused as a status, and a slot freed by a
+    finished stream is reused.
+The model is 2 layers with subsampling and a 1-layer prediction net (fp32 engine, 1e-4 tolerance class); the
+joint is sharpened so that token choices are decided by clear logit margins."""
+
+import random
+
+import numpy as np
+import pytest
+import torch
+
+import ud
+from oracle.rnnt import RNNT, DecoderState
+from oracle.stream_step import Encoder, StreamState, chunk_plan
+from oracle.weights import ModelDims, make_weights, sharpen_joint
+
+pytestmark = pytest.mark.gpu
+
+R = 6
+LENGTHS = [500, 57, 230, 131, 9]   # includes a stream whose only chunk is its first, and a 1-chunk remainder
+
+
+@pytest.fixture(scope="module")
+def model():
+    dims = ModelDims(n_layers=2)
+    sd = sharpen_joint(make_weights(dims, seed=2), dims, 11)
+    eng = ud.Engine(ud.default_config(n_layers=2, dtype=ud.DTYPE_F32, max_streams=4, max_batch=4))
+    eng.load_weights(sd)
+    yield eng, sd, dims
+    eng.close()
+
+
+def _mels():
+    return [torch.randn(n, 128, generator=torch.Generator().manual_seed(100 + i)).numpy()
+            for i, n in enumerate(LENGTHS)]
+
+
+def _oracle_tokens(sd, dims, mel: np.ndarray) -> list[int]:
+    enc, dec = Encoder(sd, dims), RNNT(sd, dims)
+    st, ds = StreamState(dims), DecoderState(dims)
+    toks: list[int] = []
+    m = torch.from_numpy(mel)
+    for start, n, valid, keep_all in chunk_plan(mel.shape[0], R):
+        proj, keep, *_ = enc.stream_step(st, m[start:start + n], n, valid, keep_all, R)
+        if keep:
+            toks += dec.greedy(proj, ds)
+    return toks
+
+
+def _run(eng, mels, live: bool, seed: int = 0) -> list[list[int]]:
+    """Admits streams as slots allow (4 of them), feeds them buffered or in random increments, steps until all
+    are done; returns tokens per stream in input order."""
+    s = ud.Streamer(eng, R, decode=True)
+    rng = random.Random(seed)
+    try:
+        pending = list(range(len(mels)))
+        active: dict[int, int] = {}        # streamer id -> input index
+        fed = [0] * len(mels)
+        out: dict[int, list[int]] = {}
+        while pending or active:
+            while pending and len(active) < 4:
+                i = pending.pop(0)
+                active[s.open(mels[i])] = i
+            for sid, i in active.items():
+                if fed[i] < len(mels[i]):
+                    n = len(mels[i]) - fed[i] if not live else min(len(mels[i]) - fed[i], rng.randint(1, 80))
+                    fed[i] += n
+                    s.push(sid, n, last=fed[i] == len(mels[i]))
+            s.step()
+            for sid in list(active):
+                toks, fin = s.tokens(sid)
+                if fin:
+                    out[active.pop(sid)] = toks
+                    s.release(sid)
+        return [out[i] for i in range(len(mels))]
+    finally:
+        s.close()
+
+
+def test_buffered_streams_match_the_oracle(model):
+    eng, sd, dims = model
+    mels = _mels()
+    got = _run(eng, mels, live=False)
+    for i, mel in enumerate(mels):
+        assert got[i] == _oracle_tokens(sd, dims, mel), i
+    assert any(len(t) > 0 for t in got)
+
+
+def test_live_increments_equal_buffered(model):
+    eng, _, _ = model
+    mels = _mels()
+    assert _run(eng, mels, live=True, seed=3) == _run(eng, mels, live=False)
+
+
+def test_admission_is_a_status_and_slots_are_reused(model):
+    eng, _, _ = model
+    s = ud.Streamer(eng, R, decode=True)
+    try:
+        mel = np.zeros((60, 128), np.float32)
+        ids = [s.open(mel) for _ in range(4)]
+        with pytest.raises(ud.EngineError) as ei:
+            s.open(mel)
+        assert ei.value.status == 5   # pool exhausted
+        s.push(ids[0], 60, last=True)
+        while not s.tokens(ids[0])[1]:
+            s.step()
+        s.release(ids[0])
+        ids[0] = s.open(mel)          # the finished stream's slot is free again
+        with pytest.raises(ud.EngineError):
+            s.push(ids[1], 61)        # beyond the stream's buffer
+    finally:
+        s.close()

@@ -1000,6 +1000,11 @@ ud_status quiet(ud_status s) {
 
 }  // namespace
 
+namespace ud {
+// Lets other host translation units (the streamer) record an error message for ud_last_error.
+ud_status host_fail(ud_status s, const char* msg) { return fail(s, msg); }
+}  // namespace ud
+
 extern "C" {
 
 void ud_config_default(ud_config* c) {
@@ -1345,7 +1350,7 @@ ud_status ud_step_batch_device(ud_engine* e, int n, const ud_stream_id* ids, con
 ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* const* mel, const int* n_rows,
                         const int* valid_rows, const int* keep_all, float* proj_out, int* frames_out,
                         int32_t* tokens_out, int* n_tokens_out) {
-    if (!e || !mel || !n_rows || !proj_out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (!e || !mel || !n_rows || (!proj_out && !tokens_out)) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
     if (n < 1 || n > e->cfg.max_batch) return fail(UD_ERR_INVALID_ARGUMENT, "batch size out of range");
     if (tokens_out && !n_tokens_out) return fail(UD_ERR_INVALID_ARGUMENT, "n_tokens_out is NULL");
     UD_CK(cudaSetDevice(e->device));
@@ -1379,7 +1384,8 @@ ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const floa
     UD_TRY(run_batch(e, n, ids, e->in_stage, stride, n_rows, valid_rows, keep_all, e->out_stage, frames.data(),
                      tokens_out ? e->tok_dev : nullptr, e->ntok_dev, true));
     const size_t out_n = static_cast<size_t>(n) * e->tmax * e->out_width;
-    UD_CK(cudaMemcpyAsync(proj_out, e->out_stage, sizeof(float) * out_n, cudaMemcpyDeviceToHost, e->stream));
+    if (proj_out)
+        UD_CK(cudaMemcpyAsync(proj_out, e->out_stage, sizeof(float) * out_n, cudaMemcpyDeviceToHost, e->stream));
     if (tokens_out) {
         UD_CK(cudaMemcpyAsync(tokens_out, e->tok_dev, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols,
                               cudaMemcpyDeviceToHost, e->stream));
@@ -1642,6 +1648,12 @@ ud_status ud_pool_info(ud_engine* e, int* free_pages, int* total_pages, int* ele
     if (free_pages) *free_pages = static_cast<int>(e->free_pages.size());
     if (total_pages) *total_pages = e->cg.n_pages;
     if (elem_bytes) *elem_bytes = e->esz;
+    return UD_OK;
+}
+
+ud_status ud_get_config(ud_engine* e, ud_config* out) {
+    if (!e || !out) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = e->cfg;
     return UD_OK;
 }
 

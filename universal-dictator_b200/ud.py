@@ -39,7 +39,8 @@ ABI_SYMBOLS = [
     "ud_cache_append", "ud_cache_roll", "ud_cache_gather", "ud_cache_evict", "ud_cache_read", "ud_stream_info",
     "ud_get_cuda_stream", "ud_pool_info", "ud_synchronize", "ud_launch_count", "ud_debug_gemm",
     "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
-    "ud_status_string",
+    "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
+    "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_tokens", "ud_streamer_release",
 ]
 
 
@@ -102,6 +103,15 @@ def lib() -> C.CDLL:
             "ud_profile_read": (I, [eng, I, P(C.c_double), P(C.c_int64)]),
             "ud_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
             "ud_status_string": (C.c_char_p, [I]),
+            "ud_get_config": (I, [eng, P(Config)]),
+            "ud_chunk_next": (I, [I, I, I, I, P(I), P(I), P(I), P(I)]),
+            "ud_streamer_create": (I, [eng, I, I, P(VP)]),
+            "ud_streamer_destroy": (I, [VP]),
+            "ud_streamer_open": (I, [VP, P(F), I, P(C.c_int32)]),
+            "ud_streamer_push": (I, [VP, C.c_int32, I, I]),
+            "ud_streamer_step": (I, [VP, P(I), P(I)]),
+            "ud_streamer_tokens": (I, [VP, C.c_int32, P(C.c_int32), I, P(I), P(I)]),
+            "ud_streamer_release": (I, [VP, C.c_int32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -351,6 +361,60 @@ class Engine:
                                   C.c_void_p(bias_ptr) if bias_ptr else None, act, out_scale,
                                   C.c_void_p(res_ptr) if res_ptr else None, res_scale, C.c_void_p(C_ptr),
                                   int(out_bf16)))
+
+
+def chunk_next(lookahead: int, idx: int, avail: int, last: bool):
+    """ud_chunk_next: (1, start, n_rows, keep_all, next_idx) for a ready chunk, (0, ...) to wait, (-1, ...) when the
+    stream has ended."""
+    st, rows, keep, nxt = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+    r = lib().ud_chunk_next(lookahead, idx, avail, int(last), C.byref(st), C.byref(rows), C.byref(keep), C.byref(nxt))
+    return r, st.value, rows.value, bool(keep.value), nxt.value
+
+
+class Streamer:
+    """Host-side batched streamer (NemotronStreamer.swift:16-163) over one engine: streams read mel from their own
+    host buffers, rows arrive with push(), and step() runs every stream with a ready chunk in one batched pass,
+    appending each stream's greedy RNN-T tokens."""
+
+    def __init__(self, engine: "Engine", lookahead: int, decode: bool = True):
+        self.engine = engine
+        self.h = C.c_void_p()
+        check(lib().ud_streamer_create(engine.h, lookahead, int(decode), C.byref(self.h)))
+        self._bufs: dict[int, np.ndarray] = {}
+
+    def open(self, mel: np.ndarray) -> int:
+        """Registers a stream over `mel` [rows, mel_bins] (kept alive here); no rows are available until pushed."""
+        mel = np.ascontiguousarray(mel, dtype=np.float32)
+        sid = C.c_int32()
+        check(lib().ud_streamer_open(self.h, _ptr(mel), mel.shape[0], C.byref(sid)))
+        self._bufs[sid.value] = mel
+        return sid.value
+
+    def push(self, sid: int, n_rows: int, last: bool = False):
+        check(lib().ud_streamer_push(self.h, sid, n_rows, int(last)))
+
+    def step(self) -> tuple[int, int]:
+        """One batched step: (streams advanced, streams finished)."""
+        n, d = C.c_int(), C.c_int()
+        check(lib().ud_streamer_step(self.h, C.byref(n), C.byref(d)))
+        return n.value, d.value
+
+    def tokens(self, sid: int) -> tuple[list[int], bool]:
+        n, fin = C.c_int(), C.c_int()
+        check(lib().ud_streamer_tokens(self.h, sid, None, 0, C.byref(n), C.byref(fin)))
+        out = np.zeros(max(1, n.value), np.int32)
+        check(lib().ud_streamer_tokens(self.h, sid, _ptr(out, C.c_int32), n.value, C.byref(n), C.byref(fin)))
+        return out[:n.value].tolist(), bool(fin.value)
+
+    def release(self, sid: int):
+        check(lib().ud_streamer_release(self.h, sid))
+        self._bufs.pop(sid, None)
+
+    def close(self):
+        if self.h:
+            check(lib().ud_streamer_destroy(self.h))
+            self.h = C.c_void_p()
+            self._bufs.clear()
 
 
 def wait_probe(engine: "Engine", limit_ns: int):
