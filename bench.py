@@ -148,6 +148,15 @@ def gemm_flops_per_step(n: int, T: int, R: int, cfg) -> float:
     return float(layers + sub + joint)
 
 
+def weight_bytes(cfg) -> float:
+    """bf16 bytes of every GEMM operand a step reads: 24 layers x 24.12 M, the subsampling pointwise and output
+    projections, and joint.enc."""
+    D, F, C, J, NL = cfg.d_model, cfg.ff_dim, cfg.sub_channels, cfg.joint_dim, cfg.n_layers
+    F3 = ((MEL // 2 + 1) // 2 + 1) // 2 + 1
+    layer = 2 * F * D * 2 + 3 * D * D + D * D + 2 * D * D + D * D
+    return 2.0 * (NL * layer + 2 * C * C + C * F3 * D + D * J)
+
+
 def cpu_baseline(sd, R: int, budget_s: float = 12.0, max_steps: int = 40):
     """The CPU restatement of the reference's step (fp32, batch 1, all host threads) on a bounded sample of
     the same workload: one stream's consecutive chunks. Returns (stream-steps/s, threads, sample text)."""
@@ -218,6 +227,14 @@ def run_reference(args, world, rank):
 
 
 def workload_config(args):
+    if args.workload == "c2":
+        return {"workload": f"C2: one stream, [70,{args.lookahead}] (T={args.lookahead + 1}, "
+                            f"{9 + 8 + 8 * args.lookahead}-row mel chunks), subsampling + 24-layer FastConformer + "
+                            "joint.enc + RNN-T greedy (1-layer LSTM 640), 10 s of mel",
+                "streams_per_gpu": 1, "lookahead": args.lookahead, "n_layers": 24, "d_model": 1024, "decode": True,
+                "blank_offset": args.blank_offset,
+                "l2": "weights (1.16 GB) larger than L2, read by every step",
+                "parallelism": f"stream-sharded x{args.gpus}, no collectives"}
     return {"workload": f"C3: {args.streams} synchronous streams/GPU, [70,{args.lookahead}] (T={args.lookahead + 1}, "
                         f"{9 + 8 + 8 * args.lookahead}-row mel chunks), subsampling + 24-layer FastConformer + joint.enc"
                         + (" + RNN-T greedy" if args.decode else ""),
@@ -358,13 +375,11 @@ def run_streamer_bench(args, world, rank, local):
             stats["admitted"] += 1
         n_stepped, n_done = st.step()
         if n_done:
-            for sid in list(active):
-                toks, fin = st.tokens(sid)
-                if fin:
-                    stats["tokens"] += len(toks)
-                    st.release(sid)
-                    del active[sid]
-                    stats["finished"] += 1
+            for sid in st.finished():
+                stats["tokens"] += len(st.tokens(sid)[0])
+                st.release(sid)
+                del active[sid]
+                stats["finished"] += 1
         return n_stepped
 
     for _ in range(args.warmup):
@@ -495,18 +510,21 @@ def main():
                     help="also run greedy RNN-T decoding in each step (configs 2 and 4; C3 is the encoder step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c4", "c5", "gemm"], default="c3",
-                    help="c3: the encoder step (default); c4: concurrent streams through the host-side streamer; "
-                         "c5: the cache-op microbenchmark; gemm: the tensor-core GEMM on one layer's shapes")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "gemm"], default="c3",
+                    help="c3: the encoder step (default); c2: one stream at [70,1] with RNN-T decoding (latency); "
+                         "c4: concurrent streams through the host-side streamer; c5: the cache-op microbenchmark; "
+                         "gemm: the tensor-core GEMM on one layer's shapes")
     ap.add_argument("--c4-streams", type=int, default=512, help="c4: stream slots per GPU")
     ap.add_argument("--blank-offset", type=float, default=1.0,
-                    help="c4: added to the joint's blank bias. With N(0,0.02) weights greedy decoding emits the "
+                    help="c2/c4: added to the joint's blank bias. With N(0,0.02) weights greedy decoding emits the "
                          "10-symbol maximum on every frame below about 0.5 and no symbol from 1.0 up; 1.0 (the "
                          "default) costs one joint evaluation per frame, 0 is the worst case")
     ap.add_argument("--cache-streams", type=int, default=1024, help="c5: streams per GPU")
     ap.add_argument("--cache-k", type=int, default=14, help="c5: frames appended per stream per step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "c2":
+        args.streams, args.lookahead, args.decode = 1, 1, True
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -543,11 +561,14 @@ def main():
     cfg = ud.default_config(max_streams=n, max_batch=n, max_chunk_frames=max(16, T))
     eng = ud.Engine(cfg, device=local)
     sd = make_weights(NEMOTRON, seed=0)
+    if args.workload == "c2":
+        sd["joint.joint_net.2.bias"][NEMOTRON.blank] += args.blank_offset
     eng.load_weights(sd)
     ids = [eng.open(R) for _ in range(n)]
 
     dev = torch.device("cuda", local)
-    mel = torch.empty(n, TOTAL_ROWS, MEL, device=dev)
+    total_rows = 1000 if args.workload == "c2" else TOTAL_ROWS
+    mel = torch.empty(n, total_rows, MEL, device=dev)
     for s, gid in enumerate(rank_streams(n, rank)):
         mel[s].normal_(generator=torch.Generator(device=dev).manual_seed(gid))
     tm, J, ms = cfg.max_chunk_frames, cfg.joint_dim, cfg.max_symbols
@@ -555,7 +576,7 @@ def main():
     toks = torch.empty(n, tm * ms, device=dev, dtype=torch.int32)
     ntok = torch.empty(n, device=dev, dtype=torch.int32)
     torch.cuda.synchronize()
-    sched = chunk_schedule(R, TOTAL_ROWS)
+    sched = chunk_schedule(R, total_rows)
     decode = args.decode
     state = {"i": 0}
 
@@ -564,7 +585,7 @@ def main():
         if c == 0 and state["i"] > 0:
             eng.cache_evict(ids)           # the utterance ended: fresh caches and decoder state, same slots
         start, rows = sched[c]
-        eng.step_batch_device(ids, mel.data_ptr() + start * MEL * 4, TOTAL_ROWS, [rows] * n, [rows] * n, [False] * n,
+        eng.step_batch_device(ids, mel.data_ptr() + start * MEL * 4, total_rows, [rows] * n, [rows] * n, [False] * n,
                               proj.data_ptr(), toks.data_ptr() if decode else None, ntok.data_ptr() if decode else None)
         state["i"] += 1
 
@@ -614,7 +635,7 @@ def main():
     # End to end through the host-buffer API (pinned host mel in, projections + tokens out), wall clock.
     e2e = None
     if not args.no_e2e:
-        hmel = torch.empty(n, TOTAL_ROWS, MEL, pin_memory=True)
+        hmel = torch.empty(n, total_rows, MEL, pin_memory=True)
         hmel.copy_(mel.cpu())
         hnp = hmel.numpy()
         eng.cache_evict(ids)
@@ -649,12 +670,21 @@ def main():
         v, cores, sample = cpu_baseline(sd, R)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
+    roof_gemv = None
+    if n * T <= 16:   # few rows: the projections run as GEMVs over the whole weight set (HBM-bound)
+        simt_ms = prof["gemm_simt"][0] / 2
+        wbytes = weight_bytes(cfg)
+        gbs = wbytes / (simt_ms / 1e3) / 1e9 if simt_ms > 0 else None
+        roof_gemv = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": (gbs / hbm) if gbs else None, "traffic": None, "kernel": "gemm_simt (GEMV)",
+                     "note": f"weight bytes per step ({wbytes / 1e9:.3f} GB bf16) / summed GEMV time per step, CUDA "
+                             f"events on the engine stream; peak = {src} HBM copy"}
     if rank == 0:
         res = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
                "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": workload_config(args),
                "e2e": e2e, "gpu_launches": launches,
-               "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
+               "roofline": roof_gemv or {"bound": "tensor", "achieved": achieved, "peak": bf16_sus, "unit": "TFLOP/s",
                             "frac": (achieved / bf16_sus) if achieved else None, "traffic": traffic,
                             "kernel": "gemm_tc (tcgen05)",
                             "traffic_of": (f"{traffic_of}: dram__bytes_read.sum + dram__bytes_write.sum from one ncu "

@@ -240,6 +240,8 @@ UD_API ud_status ud_streamer_push(ud_streamer* s, ud_streamer_id id, int n_rows,
 /* One batched step (at most max_batch streams, in order of id); *n_stepped streams advanced one chunk,
  * *n_finished of them ran their final chunk (or ended with a remainder too short to encode). */
 UD_API ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished);
+/* The ids of the streams that finished in the last ud_streamer_step (up to cap copied) and their count. */
+UD_API ud_status ud_streamer_finished(ud_streamer* s, ud_streamer_id* out, int cap, int* n);
 /* Tokens so far (up to cap copied), the total count, and whether the stream has finished. */
 UD_API ud_status ud_streamer_tokens(ud_streamer* s, ud_streamer_id id, int32_t* out, int cap, int* n_tokens,
                                     int* finished);

@@ -72,8 +72,10 @@ def _run(eng, mels, live: bool, seed: int = 0) -> list[list[int]]:
                     fed[i] += n
                     s.push(sid, n, last=fed[i] == len(mels[i]))
             s.step()
+            done = s.finished()
             for sid in list(active):
                 toks, fin = s.tokens(sid)
+                assert fin == (sid in done)
                 if fin:
                     out[active.pop(sid)] = toks
                     s.release(sid)

@@ -46,6 +46,7 @@ struct ud_streamer {
     std::vector<int> rows, keep, frames, ntok, who, next;
     std::vector<float> proj;
     std::vector<int32_t> toks;
+    std::vector<ud_streamer_id> just_finished;   // ids that finished in the last step
 };
 
 extern "C" {
@@ -156,6 +157,7 @@ ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
     if (!s) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL streamer");
     int n = 0, done = 0;
     const int mel_bins = s->cfg.mel_bins;
+    s->just_finished.clear();
     for (int id = 0; id < static_cast<int>(s->recs.size()) && n < s->cfg.max_batch; ++id) {
         StreamRec& r = s->recs[id];
         if (!r.used || r.finished) continue;
@@ -165,6 +167,7 @@ ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
         if (c < 0) {   // what remains is too short to encode: the stream ends here
             ud_stream_close(s->e, r.slot);
             r.finished = true;
+            s->just_finished.push_back(id);
             ++done;
             continue;
         }
@@ -192,12 +195,21 @@ ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
             if (s->keep[i]) {   // the final chunk: free the engine slot
                 ud_stream_close(s->e, r.slot);
                 r.finished = true;
+                s->just_finished.push_back(s->who[i]);
                 ++done;
             }
         }
     }
     if (n_stepped) *n_stepped = n;
     if (n_finished) *n_finished = done;
+    return UD_OK;
+}
+
+ud_status ud_streamer_finished(ud_streamer* s, ud_streamer_id* out, int cap, int* n) {
+    if (!s || !n) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    const int k = static_cast<int>(s->just_finished.size());
+    if (out && cap > 0) std::memcpy(out, s->just_finished.data(), sizeof(ud_streamer_id) * static_cast<size_t>(k < cap ? k : cap));
+    *n = k;
     return UD_OK;
 }
 

@@ -40,7 +40,8 @@ ABI_SYMBOLS = [
     "ud_get_cuda_stream", "ud_pool_info", "ud_synchronize", "ud_launch_count", "ud_debug_gemm",
     "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
-    "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_tokens", "ud_streamer_release",
+    "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
+    "ud_streamer_release",
 ]
 
 
@@ -110,6 +111,7 @@ def lib() -> C.CDLL:
             "ud_streamer_open": (I, [VP, P(F), I, P(C.c_int32)]),
             "ud_streamer_push": (I, [VP, C.c_int32, I, I]),
             "ud_streamer_step": (I, [VP, P(I), P(I)]),
+            "ud_streamer_finished": (I, [VP, P(C.c_int32), I, P(I)]),
             "ud_streamer_tokens": (I, [VP, C.c_int32, P(C.c_int32), I, P(I), P(I)]),
             "ud_streamer_release": (I, [VP, C.c_int32]),
         }
@@ -398,6 +400,14 @@ class Streamer:
         n, d = C.c_int(), C.c_int()
         check(lib().ud_streamer_step(self.h, C.byref(n), C.byref(d)))
         return n.value, d.value
+
+    def finished(self) -> list[int]:
+        """Ids of the streams that finished in the last step."""
+        n = C.c_int()
+        check(lib().ud_streamer_finished(self.h, None, 0, C.byref(n)))
+        out = np.zeros(max(1, n.value), np.int32)
+        check(lib().ud_streamer_finished(self.h, _ptr(out, C.c_int32), n.value, C.byref(n)))
+        return out[:n.value].tolist()
 
     def tokens(self, sid: int) -> tuple[list[int], bool]:
         n, fin = C.c_int(), C.c_int()
