@@ -388,12 +388,21 @@ def run_streamer_bench(args, world, rank, local):
     if dist:
         dist.barrier()
     total = 0
+    l0 = eng.launch_count()
     with ClockSampler(local) as clk:
         t0 = time.perf_counter()
         for _ in range(args.steps):
             total += step()
         dt = time.perf_counter() - t0
+    launches = eng.launch_count() - l0
     t_max = max_over_ranks(dt * 1e3, dist, dev)
+    # Where the device time goes: 3 more steps with per-kind CUDA-event timing (eager launches, no graphs).
+    eng.profile(True)
+    for _ in range(3):
+        step()
+    eng.synchronize()
+    prof = eng.profile_read()
+    eng.profile(False)
     all_steps = total
     if dist:
         tt = torch.tensor([float(total)], device=dev, dtype=torch.float64)
@@ -413,7 +422,9 @@ def run_streamer_bench(args, world, rank, local):
                                      "tokens": stats["tokens"], "queue": len(queue),
                                      "timing": "host wall clock, synchronous streamer steps (host mel in, tokens out)",
                                      "parallelism": f"stream-sharded x{world}, no collectives"},
-                          "gpu_launches": None, "clocks": clk.summary()}), flush=True)
+                          "gpu_launches": launches,
+                          "kernel_ms_per_step": {k: round(v[0] / 3, 4) for k, v in prof.items() if v[1]},
+                          "clocks": clk.summary()}), flush=True)
     st.close()
     eng.close()
     if dist:

@@ -20,6 +20,7 @@ enum DeviceError : int {
     DEV_TIMEOUT_ACC_EMPTY = 4,  // GEMM: waiting for the epilogue to drain TMEM
     DEV_BAD_PAGE = 5,           // cache: a page slot needed by a kernel is unmapped
     DEV_TIMEOUT_TEST = 6,       // the failure-detection test wait
+    DEV_TIMEOUT_GRID = 7,       // RNN-T: waiting at a grid barrier of the lock-step decoder
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T v);

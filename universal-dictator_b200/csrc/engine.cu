@@ -94,6 +94,8 @@ struct ud_engine {
     float* jenc_b = nullptr;
     RnntWeights rw{};
     RnntState rs{};
+    RnntScratch rscr{};          // lock-step decoder scratch
+    bool rnnt_lockstep = true;   // UD_RNNT_LOCKSTEP=0: one CTA per stream instead
 
     CacheGeom cg{};
     std::vector<int> free_pages;
@@ -288,8 +290,9 @@ ud_status check_device_error(ud_engine* e) {
         UD_CK(cudaMemsetAsync(e->err_d, 0, sizeof(int), e->stream));
         UD_CK(cudaStreamSynchronize(e->stream));
         static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
-                                      "GEMM TMEM drain wait", "unmapped cache page", "test wait"};
-        const char* nm = (code >= 0 && code <= 6) ? names[code] : "unknown";
+                                      "GEMM TMEM drain wait", "unmapped cache page", "test wait",
+                                      "RNN-T grid barrier wait"};
+        const char* nm = (code >= 0 && code <= 7) ? names[code] : "unknown";
         if (code == DEV_BAD_PAGE) return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
         return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
     }
@@ -431,6 +434,23 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         g.out_scale = scale;
         return g;
     };
+    // LayerNorm of x feeding one GEMM: fused into the few-row GEMV as its prologue, else normalised into h first.
+    const bool ln_fused = M <= 16 && gemv_ln_fits(M, D, e->bf);
+    auto ln_gemm = [&](const float* g, const float* b, const WeightMat& W, const GemmEpilogue& epi) -> ud_status {
+        if (!ln_fused) {
+            ln(g, b);
+            return gemm(e, e->h, D, M, W, epi);
+        }
+        Launch L_(e, UD_KIND_GEMM_SIMT);
+        LnPrologue p;
+        p.x = e->x;
+        p.ldx = D;
+        p.g = g;
+        p.b = b;
+        if (e->bf) gemm_simt<bf16, bf16>(nullptr, D, static_cast<const bf16*>(W.p), M, W.N, W.K, epi, st, &p);
+        else gemm_simt<float, float>(nullptr, D, static_cast<const float*>(W.p), M, W.N, W.K, epi, st, &p);
+        return UD_OK;
+    };
     if (NL > 0) ln(e->layers[0].ln_ff1_g, e->layers[0].ln_ff1_b);
     for (int l = 0; l < NL; ++l) {
         LayerW& w = e->layers[l];
@@ -438,8 +458,7 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         gs.act = ACT_SILU;
         UD_TRY(gemm(e, e->h, D, M, w.ff1_w1, gs));
         UD_TRY(gemm(e, e->hid, e->F, M, w.ff1_w2, resid(0.5f)));
-        ln(w.ln_att_g, w.ln_att_b);
-        UD_TRY(gemm(e, e->h, D, M, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
+        UD_TRY(ln_gemm(w.ln_att_g, w.ln_att_b, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
         {
         Launch L_(e, UD_KIND_ATTENTION);
         if (e->bf)
@@ -450,8 +469,7 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
                                     l, (float*)e->att, D, e->H, e->err_d, st);
         }
         UD_TRY(gemm(e, e->att, D, M, w.wo, resid(1.0f)));
-        ln(w.ln_conv_g, w.ln_conv_b);
-        UD_TRY(gemm(e, e->h, D, M, w.pw1, epi_out(e->pw, 2 * D, true, e)));
+        UD_TRY(ln_gemm(w.ln_conv_g, w.ln_conv_b, w.pw1, epi_out(e->pw, 2 * D, true, e)));
         {
         Launch L_(e, UD_KIND_CONV);
         if (e->bf)
@@ -462,8 +480,7 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
                                (float*)e->y, D, st);
         }
         UD_TRY(gemm(e, e->y, D, M, w.pw2, resid(1.0f)));
-        ln(w.ln_ff2_g, w.ln_ff2_b);
-        UD_TRY(gemm(e, e->h, D, M, w.ff2_w1, gs));
+        UD_TRY(ln_gemm(w.ln_ff2_g, w.ln_ff2_b, w.ff2_w1, gs));
         UD_TRY(gemm(e, e->hid, e->F, M, w.ff2_w2, resid(0.5f)));
         if (l + 1 < NL) {
             LayerW& nx = e->layers[l + 1];
@@ -489,7 +506,8 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         }
         if (tokens_dev) {
             Launch L_(e, UD_KIND_RNNT);
-            rnnt_greedy(e->rw, e->rs, e->proj, e->J, md, n, tokens_dev, e->tmax * e->cfg.max_symbols, ntok_dev, st);
+            rnnt_greedy(e->rw, e->rs, e->proj, e->J, md, n, tokens_dev, e->tmax * e->cfg.max_symbols, ntok_dev,
+                        e->rnnt_lockstep ? &e->rscr : nullptr, e->num_sms, e->err_d, st);
         }
     } else {
         Launch L_(e, UD_KIND_OTHER);
@@ -1202,6 +1220,17 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
         if ((s = dalloc(e, &r.pend_g, S * c.joint_dim)) != UD_OK) return cleanup(s);
         if ((s = dalloc(e, &r.last_tok, S)) != UD_OK) return cleanup(s);
         if ((s = dalloc(e, &r.pend_valid, S)) != UD_OK) return cleanup(s);
+        if (const char* g = std::getenv("UD_RNNT_LOCKSTEP")) e->rnnt_lockstep = std::atoi(g) != 0;
+        RnntScratch& q = e->rscr;
+        q.max_n = c.max_batch;
+        q.max_grid = e->num_sms;
+        if (const char* g = std::getenv("UD_RNNT_LOCKSTEP_MAX")) q.lockstep_max_n = std::atoi(g);
+        const size_t parts = static_cast<size_t>(q.max_n) * q.max_grid;
+        if ((s = dalloc(e, &q.barrier, 1)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &q.done_frame, q.max_n)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &q.emitted, q.max_n)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &q.part_val, parts)) != UD_OK) return cleanup(s);
+        if ((s = dalloc(e, &q.part_idx, parts)) != UD_OK) return cleanup(s);
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(UD_ERR_CUDA, "device synchronize failed"));
     *out = e;
@@ -1433,11 +1462,13 @@ ud_status ud_rnnt_decode(ud_engine* e, ud_stream_id id, const float* f, int fram
     if (frames * e->cfg.max_symbols > cap) return fail(UD_ERR_INVALID_ARGUMENT, "too many frames for one call");
     {
         Launch L_(e, UD_KIND_RNNT);
-        rnnt_greedy(e->rw, e->rs, e->proj, e->J, e->meta_d[mi], 1, e->tok_dev, cap, e->ntok_dev, e->stream);
+        rnnt_greedy(e->rw, e->rs, e->proj, e->J, e->meta_d[mi], 1, e->tok_dev, cap, e->ntok_dev,
+                    e->rnnt_lockstep ? &e->rscr : nullptr, e->num_sms, e->err_d, e->stream);
     }
     UD_CK(cudaGetLastError());
     UD_CK(cudaMemcpyAsync(e->h_ntok, e->ntok_dev, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     UD_CK(cudaStreamSynchronize(e->stream));
+    UD_TRY(check_device_error(e));
     const int nt = e->h_ntok[0];
     UD_CK(cudaMemcpyAsync(tokens_out, e->tok_dev, sizeof(int32_t) * nt, cudaMemcpyDeviceToHost, e->stream));
     UD_CK(cudaStreamSynchronize(e->stream));
@@ -1482,7 +1513,8 @@ ud_status ud_rnnt_decode_static(ud_engine* e, ud_stream_id id, const float* f, i
     UD_CK_QUIET(cudaMemcpyAsync(meta, &me, sizeof(me), cudaMemcpyHostToDevice, e->stream));
     UD_CK_QUIET(cudaMemsetAsync(count, 0, sizeof(int), e->stream));
     UD_CK_QUIET(cudaMemcpyAsync(feats, f, feat_bytes, cudaMemcpyHostToDevice, e->stream));
-    rnnt_greedy(e->rw, e->rs, feats, e->J, meta, 1, tokens, static_cast<int>(tok_cap), count, e->stream);
+    rnnt_greedy(e->rw, e->rs, feats, e->J, meta, 1, tokens, static_cast<int>(tok_cap), count,
+                e->rnnt_lockstep ? &e->rscr : nullptr, e->num_sms, e->err_d, e->stream);
     e->launches++;
     UD_CK_QUIET(cudaGetLastError());
     int nt = 0;

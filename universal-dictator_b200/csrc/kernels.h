@@ -67,8 +67,18 @@ void gemm_tc2(const TmaMatrix& A, const TmaMatrix& W_half, int M, int N, int K, 
               int* dev_err, int num_sms, const TmaMatrix* out_map, cudaStream_t s);
 
 // ---- SIMT GEMM for few rows (M small) and for the fp32 engine. TA/TW in {float, bf16}.
+// LayerNorm prologue of the few-row GEMV: A = LN(x) (eps 1e-5), x fp32 [M, ldx] with K columns; A is then unused.
+// Only for M <= 16 when gemv_ln_fits(M, K, TA is bf16); epi.out must not alias x.
+struct LnPrologue {
+    const float* x = nullptr;
+    int ldx = 0;
+    const float* g = nullptr;
+    const float* b = nullptr;
+};
+bool gemv_ln_fits(int M, int K, bool bf16_rows);
 template <typename TA, typename TW>
-void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s);
+void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s,
+               const LnPrologue* ln = nullptr);
 
 // ---- LayerNorm over rows of width D (eps 1e-5). x fp32 [M, D] -> y (TO) [M, D].
 template <typename TO>
@@ -160,8 +170,22 @@ struct RnntState {         // per slot
     int* last_tok;         // [slots]
     int* pend_valid;       // [slots]
 };
+// Scratch of the lock-step decoder (all streams of a batch advance frame by frame together, every SM holding a
+// slice of the LSTM, prediction and joint rows in shared memory; grid barriers between the stages).
+struct RnntScratch {
+    unsigned long long* barrier = nullptr;  // grid-barrier arrival counter, zeroed before each launch
+    int* done_frame = nullptr;              // [max_n] frames a stream has finished in this launch
+    int* emitted = nullptr;                 // [max_n] symbols emitted in the current frame
+    float* part_val = nullptr;              // [max_n * max_grid] per-CTA joint maxima
+    int* part_idx = nullptr;                // [max_n * max_grid] their vocabulary ids
+    int max_n = 0, max_grid = 0;
+    int lockstep_max_n = 64;   // larger batches decode faster with one CTA per stream (grid full, weights in L2)
+};
+// Greedy decoding of n streams. With scr, n <= scr->lockstep_max_n and weights whose slices fit in shared
+// memory the lock-step kernel runs on min(num_sms, scr->max_grid) CTAs; otherwise one CTA per stream.
 void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, int ld_proj, const BatchEntry* meta,
-                 int n, int32_t* tokens, int tok_stride, int* n_tokens, cudaStream_t s);
+                 int n, int32_t* tokens, int tok_stride, int* n_tokens, const RnntScratch* scr, int num_sms,
+                 int* dev_err, cudaStream_t s);
 void rnnt_reset(const RnntState& st, const int* slots, int n, const RnntWeights& w, cudaStream_t s);
 
 void pack_frames(const float* frames, int rows_stride, const BatchEntry* meta, int n, int tmax, float* x, int D,

@@ -8,6 +8,8 @@
 //                     token is computed lazily and committed (h, c, lastToken) only when a token is emitted
 // The decoder state (committed h/c, last token, pending prediction) lives per stream slot in device memory and
 // carries across calls. argmax keeps the first maximum (RNNT.swift:138-140).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -181,6 +183,338 @@ __global__ void rnnt_reset_kernel(const RnntState st, const int* __restrict__ sl
     }
 }
 
+// ---------------------------------------------------------------- lock-step decoder
+// The same greedy semantics with the streams of a batch advanced together: per frame t, every stream that has
+// not finished the frame takes one symbol iteration at a time,
+//   [LSTM layers + prediction for the streams without a pending prediction]  ->  joint + argmax  ->  decide,
+// and the frame ends when every stream has emitted blank or the symbol limit. Each CTA owns a slice of the
+// hidden units (all four gates of each, so it can apply the cell update itself), of the prediction rows and of
+// the vocabulary rows; those weight slices stay in shared memory for the whole launch, so each iteration reads
+// only the streams' vectors (from L2). A grid barrier (bounded wait) separates the stages; the owner CTA of a
+// stream (b mod grid) combines the per-CTA maxima in vocabulary order (first maximum, RNNT.swift:138-140),
+// emits, commits the LSTM state and marks the stream's progress. Data written by other CTAs during the launch is
+// read through L2 (ld.global.cg).
+
+constexpr int kLsThreads = 512;
+constexpr int kLsWarps = kLsThreads / 32;
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier: all CTAs of the launch are resident (one per SM at most, grid <= SM count). Returns false (and
+// records DEV_TIMEOUT_GRID) when the wait exceeds kWaitLimitNs; the caller then leaves the kernel.
+__device__ bool grid_sync(unsigned long long* ctr, unsigned long long& target, int* err, volatile int* s_fail) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        target += gridDim.x;
+        __threadfence();
+        atomicAdd(ctr, 1ull);
+        const uint64_t t0 = global_timer_ns();
+        while (ld_acquire_u64(ctr) < target) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                report_error(err, DEV_TIMEOUT_GRID);
+                *s_fail = 1;
+                break;
+            }
+            __nanosleep(32);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return *s_fail == 0;
+}
+
+// Dot product of one weight row [a ; b] (len each) with [x ; y], lanes over float4 chunks; full sum in every lane.
+__device__ __forceinline__ float dot2(const float* a, const float* x, const float* b, const float* y, int len,
+                                      int lane) {
+    float acc = 0.f;
+    for (int i = lane * 4; i < len; i += 128) {
+        const float4 w = *reinterpret_cast<const float4*>(a + i), v = *reinterpret_cast<const float4*>(x + i);
+        acc = fmaf(w.x, v.x, fmaf(w.y, v.y, fmaf(w.z, v.z, fmaf(w.w, v.w, acc))));
+    }
+    if (b) {
+        for (int i = lane * 4; i < len; i += 128) {
+            const float4 w = *reinterpret_cast<const float4*>(b + i), v = *reinterpret_cast<const float4*>(y + i);
+            acc = fmaf(w.x, v.x, fmaf(w.y, v.y, fmaf(w.z, v.z, fmaf(w.w, v.w, acc))));
+        }
+    }
+    return warp_sum(acc);
+}
+
+struct LsGeom {
+    int nu, nj, nv;     // hidden units, prediction rows and vocabulary rows per CTA
+    int sb;             // streams per staged tile
+    int wl_smem;        // LSTM slices in shared memory (else read from global)
+};
+
+// Appends the streams b (in order) that are still in frame t, and those of them without a pending prediction.
+__device__ void ls_lists(const BatchEntry* meta, int n, int t, const RnntState& st, const RnntScratch& scr, int* act,
+                         int* need, int* s_cnt, int* s_wa, int* s_wn) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int na = 0, nn = 0;
+    for (int b0 = 0; b0 < n; b0 += kLsThreads) {
+        const int b = b0 + tid;
+        bool fa = false, fn = false;
+        if (b < n && t < meta[b].keep && __ldcg(scr.done_frame + b) <= t) {
+            fa = true;
+            fn = __ldcg(st.pend_valid + meta[b].slot) == 0;
+        }
+        const unsigned ba = __ballot_sync(0xffffffffu, fa), bn = __ballot_sync(0xffffffffu, fn);
+        if (lane == 0) { s_wa[warp] = __popc(ba); s_wn[warp] = __popc(bn); }
+        __syncthreads();
+        int pa = na, pn = nn, ta = 0, tn = 0;
+        for (int w = 0; w < kLsWarps; ++w) {
+            if (w < warp) { pa += s_wa[w]; pn += s_wn[w]; }
+            ta += s_wa[w];
+            tn += s_wn[w];
+        }
+        const unsigned lt = (1u << lane) - 1u;
+        if (fa) act[pa + __popc(ba & lt)] = b;
+        if (fn) need[pn + __popc(bn & lt)] = b;
+        na += ta;
+        nn += tn;
+        __syncthreads();
+    }
+    if (tid == 0) { s_cnt[0] = na; s_cnt[1] = nn; }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kLsThreads, 1) rnnt_lockstep_kernel(
+    const RnntWeights w, const RnntState st, const float* __restrict__ proj, int ld_proj,
+    const BatchEntry* __restrict__ meta, int n, int32_t* __restrict__ tokens, int tok_stride, int* __restrict__ n_tokens,
+    const RnntScratch scr, const LsGeom gm, int* err) {
+    pdl_wait();
+    extern __shared__ __align__(16) float lsm[];
+    const int Hp = w.Hp, J = w.J, V = w.V, NLp = w.layers, G = gridDim.x, k = blockIdx.x;
+    const int H2 = 2 * Hp, XW = max(H2, J), YW = max(4 * gm.nu, gm.nv), SB = gm.sb;
+    float* Wl = lsm;                                                            // [NLp][4][nu][2Hp] (if wl_smem)
+    float* Wp = Wl + (gm.wl_smem ? static_cast<size_t>(NLp) * 4 * gm.nu * H2 : 0);  // [nj][Hp]
+    float* Wo = Wp + static_cast<size_t>(gm.nj) * Hp;                           // [nv][J]
+    float* X = Wo + static_cast<size_t>(gm.nv) * J;                             // [SB][XW]
+    float* Y = X + static_cast<size_t>(SB) * XW;                                // [SB][YW]
+    int* act = reinterpret_cast<int*>(Y + static_cast<size_t>(SB) * YW);        // [n]
+    int* need = act + n;                                                        // [n]
+    __shared__ int s_fail, s_cnt[2], s_wa[kLsWarps], s_wn[kLsWarps];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int u0 = k * gm.nu, nuk = max(0, min(Hp, u0 + gm.nu) - u0);
+    const int j0 = k * gm.nj, njk = max(0, min(J, j0 + gm.nj) - j0);
+    const int v0 = k * gm.nv, nvk = max(0, min(V, v0 + gm.nv) - v0);
+    const int blank = V - 1;
+    if (tid == 0) s_fail = 0;
+
+    // This CTA's weight slices into shared memory (float4 rows; Hp and J are multiples of 4).
+    if (gm.wl_smem) {
+        const int h4 = Hp / 4;
+        const int total = NLp * 4 * nuk * 2 * h4;
+        for (int i = tid; i < total; i += kLsThreads) {
+            int r = i;
+            const int c = r % h4; r /= h4;
+            const int half = r % 2; r /= 2;
+            const int uu = r % nuk; r /= nuk;
+            const int q = r % 4, l = r / 4;
+            const float* src = (half ? w.w_hh[l] : w.w_ih[l]) + static_cast<size_t>(q * Hp + u0 + uu) * Hp;
+            reinterpret_cast<float4*>(Wl + (static_cast<size_t>(l * 4 + q) * gm.nu + uu) * H2 + half * Hp)[c] =
+                reinterpret_cast<const float4*>(src)[c];
+        }
+    }
+    for (int i = tid; i < njk * (Hp / 4); i += kLsThreads) {
+        const int jj = i / (Hp / 4), c = i % (Hp / 4);
+        reinterpret_cast<float4*>(Wp + static_cast<size_t>(jj) * Hp)[c] =
+            reinterpret_cast<const float4*>(w.pred_w + static_cast<size_t>(j0 + jj) * Hp)[c];
+    }
+    for (int i = tid; i < nvk * (J / 4); i += kLsThreads) {
+        const int vv = i / (J / 4), c = i % (J / 4);
+        reinterpret_cast<float4*>(Wo + static_cast<size_t>(vv) * J)[c] =
+            reinterpret_cast<const float4*>(w.out_w + static_cast<size_t>(v0 + vv) * J)[c];
+    }
+    if (tid == 0)
+        for (int b = k; b < n; b += G) {
+            scr.done_frame[b] = 0;
+            scr.emitted[b] = 0;
+            n_tokens[b] = 0;
+        }
+    int tmax = 0;
+    for (int b = 0; b < n; ++b) tmax = max(tmax, meta[b].keep);
+    unsigned long long target = 0;
+    if (!grid_sync(scr.barrier, target, err, &s_fail)) return;
+
+    for (int t = 0; t < tmax; ++t) {
+        for (;;) {
+            ls_lists(meta, n, t, st, scr, act, need, s_cnt, s_wa, s_wn);
+            const int na = s_cnt[0], nn = s_cnt[1];
+            if (na == 0) break;
+            if (nn > 0) {
+                // ---- LSTM layers for the streams that need a new prediction: gates for this CTA's units
+                for (int l = 0; l < NLp; ++l) {
+                    for (int s0 = 0; s0 < nn; s0 += SB) {
+                        const int sb = min(SB, nn - s0);
+                        for (int s = warp; s < sb; s += kLsWarps) {   // one warp per stream: [x ; h]
+                            const int slot = meta[need[s0 + s]].slot;
+                            const float4* xs = nullptr;
+                            if (l == 0) {
+                                const int tok = __ldcg(st.last_tok + slot);
+                                if (tok != blank) xs = reinterpret_cast<const float4*>(w.embed + static_cast<size_t>(tok) * Hp);
+                            } else {
+                                xs = reinterpret_cast<const float4*>(st.pend_h + (static_cast<size_t>(slot) * NLp + l - 1) * Hp);
+                            }
+                            const float4* hs4 = reinterpret_cast<const float4*>(st.h + (static_cast<size_t>(slot) * NLp + l) * Hp);
+                            float4* xr = reinterpret_cast<float4*>(X + s * XW);
+#pragma unroll 4
+                            for (int c = lane; c < Hp / 4; c += 32) {
+                                xr[c] = xs ? (l == 0 ? xs[c] : __ldcg(xs + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                xr[Hp / 4 + c] = __ldcg(hs4 + c);
+                            }
+                        }
+                        __syncthreads();
+                        const int rows = 4 * nuk;
+                        for (int it = warp; it < rows * sb; it += kLsWarps) {
+                            const int lr = it / sb, s = it - lr * sb;
+                            const int q = lr / nuk, uu = lr - q * nuk;
+                            const float *ra, *rb;
+                            if (gm.wl_smem) {
+                                ra = Wl + (static_cast<size_t>(l * 4 + q) * gm.nu + uu) * H2;
+                                rb = ra + Hp;
+                            } else {
+                                ra = w.w_ih[l] + static_cast<size_t>(q * Hp + u0 + uu) * Hp;
+                                rb = w.w_hh[l] + static_cast<size_t>(q * Hp + u0 + uu) * Hp;
+                            }
+                            const float v = dot2(ra, X + s * XW, rb, X + s * XW + Hp, Hp, lane);
+                            if (lane == 0) Y[s * YW + lr] = v + w.bias[l][q * Hp + u0 + uu];
+                        }
+                        __syncthreads();
+                        for (int i = tid; i < sb * nuk; i += kLsThreads) {
+                            const int s = i / nuk, uu = i - s * nuk;
+                            const int slot = meta[need[s0 + s]].slot;
+                            const float* gy = Y + s * YW;
+                            const float ig = sigm(gy[uu]), fg = sigm(gy[nuk + uu]);
+                            const float gg = tanhf(gy[2 * nuk + uu]), og = sigm(gy[3 * nuk + uu]);
+                            const size_t o = (static_cast<size_t>(slot) * NLp + l) * Hp + u0 + uu;
+                            const float cn = fg * __ldcg(st.c + o) + ig * gg;
+                            st.pend_c[o] = cn;
+                            st.pend_h[o] = og * tanhf(cn);
+                        }
+                        __syncthreads();
+                    }
+                    if (!grid_sync(scr.barrier, target, err, &s_fail)) return;
+                }
+                // ---- prediction output g = joint.pred(h_top) for this CTA's rows
+                for (int s0 = 0; s0 < nn; s0 += SB) {
+                    const int sb = min(SB, nn - s0);
+                    for (int s = warp; s < sb; s += kLsWarps) {
+                        const int slot = meta[need[s0 + s]].slot;
+                        const float4* src = reinterpret_cast<const float4*>(st.pend_h + (static_cast<size_t>(slot) * NLp + NLp - 1) * Hp);
+                        float4* xr = reinterpret_cast<float4*>(X + s * XW);
+#pragma unroll 4
+                        for (int c = lane; c < Hp / 4; c += 32) xr[c] = __ldcg(src + c);
+                    }
+                    __syncthreads();
+                    for (int it = warp; it < njk * sb; it += kLsWarps) {
+                        const int jj = it / sb, s = it - jj * sb;
+                        const float v = dot2(Wp + static_cast<size_t>(jj) * Hp, X + s * XW, nullptr, nullptr, Hp, lane);
+                        if (lane == 0) st.pend_g[static_cast<size_t>(meta[need[s0 + s]].slot) * J + j0 + jj] = v + w.pred_b[j0 + jj];
+                    }
+                    __syncthreads();
+                }
+                if (!grid_sync(scr.barrier, target, err, &s_fail)) return;
+            }
+            // ---- joint logits for this CTA's vocabulary rows and their first maximum, per active stream
+            for (int s0 = 0; s0 < na; s0 += SB) {
+                const int sb = min(SB, na - s0);
+                for (int s = warp; s < sb; s += kLsWarps) {   // one warp per stream: relu(f_t + g)
+                    const BatchEntry& me = meta[act[s0 + s]];
+                    const float4* fp = reinterpret_cast<const float4*>(proj + static_cast<size_t>(me.row_off + t) * ld_proj);
+                    const float4* gp = reinterpret_cast<const float4*>(st.pend_g + static_cast<size_t>(me.slot) * J);
+                    float4* xr = reinterpret_cast<float4*>(X + s * XW);
+#pragma unroll 4
+                    for (int c = lane; c < J / 4; c += 32) {
+                        const float4 a = fp[c], g = __ldcg(gp + c);
+                        xr[c] = make_float4(fmaxf(a.x + g.x, 0.f), fmaxf(a.y + g.y, 0.f), fmaxf(a.z + g.z, 0.f),
+                                            fmaxf(a.w + g.w, 0.f));
+                    }
+                }
+                __syncthreads();
+                for (int it = warp; it < nvk * sb; it += kLsWarps) {
+                    const int vv = it / sb, s = it - vv * sb;
+                    const float v = dot2(Wo + static_cast<size_t>(vv) * J, X + s * XW, nullptr, nullptr, J, lane);
+                    if (lane == 0) Y[s * YW + vv] = v + w.out_b[v0 + vv];
+                }
+                __syncthreads();
+                for (int s = warp; s < sb; s += kLsWarps) {
+                    float bv = -INFINITY;
+                    int bi = 0x7fffffff;
+                    for (int vv = lane; vv < nvk; vv += 32) {
+                        const float v = Y[s * YW + vv];
+                        if (v > bv) { bv = v; bi = v0 + vv; }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                    }
+                    if (lane == 0) {
+                        const size_t pi = static_cast<size_t>(act[s0 + s]) * G + k;
+                        scr.part_val[pi] = bv;
+                        scr.part_idx[pi] = bi;
+                    }
+                }
+                __syncthreads();
+            }
+            if (!grid_sync(scr.barrier, target, err, &s_fail)) return;
+            // ---- decide, by the owner CTA of each active stream
+            for (int i = warp; i < na; i += kLsWarps) {
+                const int b = act[i];
+                if (b % G != k) continue;
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+                for (int kk = lane; kk < G; kk += 32) {
+                    const float v = __ldcg(scr.part_val + static_cast<size_t>(b) * G + kk);
+                    const int ix = __ldcg(scr.part_idx + static_cast<size_t>(b) * G + kk);
+                    if (v > bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                }
+                const int slot = meta[b].slot;
+                if (bi == blank) {
+                    if (lane == 0) {
+                        st.pend_valid[slot] = 1;
+                        scr.done_frame[b] = t + 1;
+                        scr.emitted[b] = 0;
+                    }
+                } else {
+                    for (int x = lane; x < NLp * Hp; x += 32) {
+                        const size_t o = static_cast<size_t>(slot) * NLp * Hp + x;
+                        st.h[o] = __ldcg(st.pend_h + o);
+                        st.c[o] = __ldcg(st.pend_c + o);
+                    }
+                    if (lane == 0) {
+                        const int nt = __ldcg(n_tokens + b);
+                        tokens[static_cast<size_t>(b) * tok_stride + nt] = bi;
+                        n_tokens[b] = nt + 1;
+                        st.last_tok[slot] = bi;
+                        st.pend_valid[slot] = 0;
+                        const int em = __ldcg(scr.emitted + b) + 1;
+                        if (em >= w.max_symbols) {
+                            scr.done_frame[b] = t + 1;
+                            scr.emitted[b] = 0;
+                        } else {
+                            scr.emitted[b] = em;
+                        }
+                    }
+                }
+            }
+            if (!grid_sync(scr.barrier, target, err, &s_fail)) return;
+        }
+    }
+}
+
 }  // namespace
 
 size_t rnnt_smem_bytes(const RnntWeights& w) {
@@ -188,8 +522,39 @@ size_t rnnt_smem_bytes(const RnntWeights& w) {
 }
 
 void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, int ld_proj, const BatchEntry* meta,
-                 int n, int32_t* tokens, int tok_stride, int* n_tokens, cudaStream_t s) {
+                 int n, int32_t* tokens, int tok_stride, int* n_tokens, const RnntScratch* scr, int num_sms,
+                 int* dev_err, cudaStream_t s) {
     if (n <= 0) return;
+    if (scr && scr->barrier && n <= scr->max_n && n <= scr->lockstep_max_n && w.Hp % 4 == 0 && w.J % 4 == 0 &&
+        ld_proj % 4 == 0 && (reinterpret_cast<uintptr_t>(proj) & 15) == 0 && w.max_symbols > 0) {
+        const int G = std::min(num_sms, scr->max_grid);
+        LsGeom gm;
+        gm.nu = (w.Hp + G - 1) / G;
+        gm.nj = (w.J + G - 1) / G;
+        gm.nv = (w.V + G - 1) / G;
+        const size_t XW = std::max(2 * w.Hp, w.J), YW = std::max(4 * gm.nu, gm.nv);
+        const size_t wl = sizeof(float) * static_cast<size_t>(w.layers) * 4 * gm.nu * 2 * w.Hp;
+        const size_t fixed = sizeof(float) * (static_cast<size_t>(gm.nj) * w.Hp + static_cast<size_t>(gm.nv) * w.J) +
+                             sizeof(int) * 2 * static_cast<size_t>(n);
+        const size_t per_stream = sizeof(float) * (XW + YW);
+        constexpr size_t kSmemMax = 227 * 1024 - 1024;   // static shared memory of the kernel stays below 1 KB
+        gm.wl_smem = wl + fixed + 4 * per_stream <= kSmemMax ? 1 : 0;
+        const size_t base = fixed + (gm.wl_smem ? wl : 0);
+        if (base + per_stream <= kSmemMax) {
+            gm.sb = static_cast<int>(std::min<size_t>(16, (kSmemMax - base) / per_stream));
+            const size_t smem = base + per_stream * gm.sb;
+            static size_t attr_set = 0;
+            if (smem > attr_set) {
+                cudaFuncSetAttribute(rnnt_lockstep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kSmemMax));
+                attr_set = kSmemMax;
+            }
+            cudaMemsetAsync(scr->barrier, 0, sizeof(unsigned long long), s);
+            rnnt_lockstep_kernel<<<G, kLsThreads, smem, s>>>(w, st, proj, ld_proj, meta, n, tokens, tok_stride, n_tokens,
+                                                             *scr, gm, dev_err);
+            return;
+        }
+    }
     const size_t smem = rnnt_smem_bytes(w);
     static size_t attr_set = 0;
     if (smem > 48 * 1024 && smem > attr_set) {
