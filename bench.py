@@ -248,10 +248,10 @@ def run_cache_bench(args, world, rank, local):
     """Config 5: the cache-op microbenchmark. Per step, for B streams and all 24 layers: append k new frames of
     projected K and V plus conv rows after each stream's head, roll (metadata), gather every stream's 70-frame
     K/V window and 8 conv rows into contiguous buffers, then evict and refill 5% of the streams. Stream ids are
-    a fresh random permutation every step. GB/s = algorithmic bytes (oracle/cache_ring.py
-    bytes_per_stream_step x B) / device time."""
+    a fresh random permutation every step. GB/s = algorithmic bytes (ud_synthetic.cache_bytes_per_stream_step
+    x B) / device time."""
     import ud
-    from oracle.cache_ring import bytes_per_stream_step
+    from ud_synthetic import cache_bytes_per_stream_step as bytes_per_stream_step
 
     B, k, NL, D, L = args.cache_streams, args.cache_k, 24, 1024, 70
     dev = torch.device("cuda", local)
@@ -341,7 +341,7 @@ def run_streamer_bench(args, world, rank, local):
     host pool, all of it available at admission. Timing is the host wall clock around synchronous streamer steps
     (host rows in, tokens out), max over ranks; value = stream-steps of all ranks per second."""
     import ud
-    from oracle.weights import NEMOTRON, make_weights
+    from ud_synthetic import NEMOTRON, make_weights
 
     R, slots, fps = 6, args.c4_streams, 100
     chunk_s = (8 + 8 * R) / fps
@@ -558,7 +558,7 @@ def main():
         return
 
     import ud
-    from oracle.weights import NEMOTRON, make_weights
+    from ud_synthetic import NEMOTRON, make_weights
 
     torch.cuda.set_device(local)
     dist = None

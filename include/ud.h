@@ -248,6 +248,34 @@ UD_API ud_status ud_streamer_tokens(ud_streamer* s, ud_streamer_id id, int32_t* 
 /* Forgets a stream (closing its engine slot if it has not finished); its id may be reused. */
 UD_API ud_status ud_streamer_release(ud_streamer* s, ud_streamer_id id);
 
+/* ---- Log-mel frontend (NemoMelFrontend / NemoMelStream, Sources/DictatorCore/Audio/NemoMel.swift:10-161)
+ *
+ * NeMo's FilterbankFeatures at inference on the engine's device and CUDA stream: preemphasis 0.97, centred
+ * STFT (n_fft 512, hop 160, the 400-tap window at taps 56..455), power, mel filterbank, log(x + 2^-24); frames
+ * at or beyond n_samples / 160 are 0. fb [n_mels, 257] is the checkpoint's preprocessor.featurizer.fb and
+ * window [400] its preprocessor.featurizer.window (NemoMelFrontend.init, :22-39). max_streams live streams can
+ * be open at once. Output rows are time-major [frames, n_mels] fp32, the encoder's mel input. */
+typedef struct ud_mel ud_mel;
+UD_API ud_status ud_mel_create(ud_engine* e, const float* fb, int n_mels, const float* window, int max_streams,
+                               ud_mel** out);
+UD_API ud_status ud_mel_destroy(ud_mel* m);
+/* Full utterance (NemoMelFrontend.features, :45-66): n_samples / 160 + 1 frames into mel_out (capacity
+ * cap_frames rows), the last one 0; *frames_out = their count. */
+UD_API ud_status ud_mel_features(ud_mel* m, const float* audio, int n_samples, float* mel_out, int cap_frames,
+                                 int* frames_out);
+/* Device-resident batch of n utterances, asynchronous on the engine stream: utterance i is n_samples[i] samples
+ * at audio_dev + sample_off[i]; its n_samples[i] / 160 + 1 frames go to rows [row_off[i], ...) of mel_dev. */
+UD_API ud_status ud_mel_features_device(ud_mel* m, int n, const float* audio_dev, const int64_t* sample_off,
+                                        const int* n_samples, float* mel_dev, const int64_t* row_off);
+/* Live streams (NemoMelStream, :110-161): push samples in any sizes; a frame is returned once its window is
+ * complete (sample 160 t + 199 has arrived); finish != 0 ends the stream and returns the remaining frames with
+ * the right zero padding and the zeroed last frame, so the frames equal ud_mel_features of the whole stream.
+ * Stream i's new frames go to mel_out + i * cap_frames * n_mels, their count to frames_out[i]. */
+UD_API ud_status ud_mel_stream_open(ud_mel* m, int* id);
+UD_API ud_status ud_mel_stream_close(ud_mel* m, int id);
+UD_API ud_status ud_mel_push_batch(ud_mel* m, int n, const int* ids, const float* const* audio, const int* n_samples,
+                                   const int* finish, float* mel_out, int cap_frames, int* frames_out);
+
 /* Text of the last error on this thread ("" if none). Returns the full length. */
 UD_API size_t ud_last_error(char* buf, size_t len);
 UD_API const char* ud_status_string(ud_status s);

@@ -21,6 +21,7 @@ fixture stores what it needs: inputs, outputs and the seeds/dims used.
 from __future__ import annotations
 
 import argparse
+import math
 import contextlib
 import sys
 import types
@@ -193,6 +194,28 @@ def gen_greedy(cs, seed, std, T, name, blank_offset=0.0, sharp_seed=0):
     print(f"wrote {name}: {len(toks)} tokens over {T} frames")
 
 
+def gen_mel(cs):
+    """check_spec.mel_spec (the nemotron frontend, normalize=False) over seeded audio: a tone plus noise of
+    16000 + 123 samples, a length that is a multiple of the hop, and one shorter than a window. The filterbank
+    is oracle.mel.slaney_filterbank and the window oracle.mel.hann_symmetric; both are stored."""
+    from oracle.mel import hann_symmetric, slaney_filterbank
+
+    fb, win = slaney_filterbank(), hann_symmetric()
+    out = {"fb": fb.numpy(), "window": win.numpy()}
+    g = torch.Generator().manual_seed(21)
+    for i, n in enumerate([16000 + 123, 4800, 333]):
+        t = torch.arange(n, dtype=torch.float64) / 16000
+        a = (0.3 * torch.sin(2 * math.pi * 440 * t) + 0.05 * torch.randn(n, generator=g, dtype=torch.float64))
+        a = a.to(torch.float32)
+        with torch.no_grad():
+            m, t_valid = cs.mel_spec(a, fb, win, normalize=False)
+        out[f"audio{i}"] = a.numpy()
+        out[f"mel{i}"] = m.T.contiguous().numpy()      # time-major [T, 128]
+        out[f"valid{i}"] = np.int64(t_valid)
+    np.savez_compressed(HERE / "mel_spec.npz", **out)
+    print("wrote mel_spec.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
@@ -202,6 +225,7 @@ def main():
     gen_block1(na)
     gen_offline_layer(cs)
     gen_offline_subsample(cs)
+    gen_mel(cs)
     gen_greedy(cs, seed=0, std=0.02, T=24, name="greedy_std002.npz")
     gen_greedy(cs, seed=0, std=0.02, T=24, name="greedy_std002_blank.npz", blank_offset=0.5)
     gen_greedy(cs, seed=3, std=0.02, T=24, name="greedy_sharp_joint.npz", blank_offset=100.0, sharp_seed=77)

@@ -1023,6 +1023,13 @@ namespace ud {
 ud_status host_fail(ud_status s, const char* msg) { return fail(s, msg); }
 }  // namespace ud
 
+// Engine properties for the other translation units of the library (C++ linkage, outside the C ABI).
+namespace ud {
+cudaStream_t engine_stream(ud_engine* e) { return e->stream; }
+int engine_device(ud_engine* e) { return e->device; }
+int engine_num_sms(ud_engine* e) { return e->num_sms; }
+}  // namespace ud
+
 extern "C" {
 
 void ud_config_default(ud_config* c) {

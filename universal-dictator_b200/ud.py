@@ -41,7 +41,8 @@ ABI_SYMBOLS = [
     "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
     "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
-    "ud_streamer_release",
+    "ud_streamer_release", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
+    "ud_mel_stream_open", "ud_mel_stream_close", "ud_mel_push_batch",
 ]
 
 
@@ -114,6 +115,13 @@ def lib() -> C.CDLL:
             "ud_streamer_finished": (I, [VP, P(C.c_int32), I, P(I)]),
             "ud_streamer_tokens": (I, [VP, C.c_int32, P(C.c_int32), I, P(I), P(I)]),
             "ud_streamer_release": (I, [VP, C.c_int32]),
+            "ud_mel_create": (I, [eng, P(F), I, P(F), I, P(VP)]),
+            "ud_mel_destroy": (I, [VP]),
+            "ud_mel_features": (I, [VP, P(F), I, P(F), I, P(I)]),
+            "ud_mel_features_device": (I, [VP, I, VP, P(C.c_int64), P(I), VP, P(C.c_int64)]),
+            "ud_mel_stream_open": (I, [VP, P(I)]),
+            "ud_mel_stream_close": (I, [VP, I]),
+            "ud_mel_push_batch": (I, [VP, I, P(I), P(P(F)), P(I), P(I), P(F), I, P(I)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -425,6 +433,69 @@ class Streamer:
             check(lib().ud_streamer_destroy(self.h))
             self.h = C.c_void_p()
             self._bufs.clear()
+
+
+class MelFrontend:
+    """Log-mel frontend on an engine's device and stream (NemoMelFrontend / NemoMelStream,
+    Sources/DictatorCore/Audio/NemoMel.swift:10-161): fb [n_mels, 257] and window [400] are the checkpoint's
+    preprocessor.featurizer buffers."""
+
+    HOP = 160
+
+    def __init__(self, engine: "Engine", fb: np.ndarray, window: np.ndarray, max_streams: int = 0):
+        self.engine = engine
+        self.fb = np.ascontiguousarray(np.asarray(fb, np.float32).reshape(-1, 257))
+        self.n_mels = self.fb.shape[0]
+        w = np.ascontiguousarray(np.asarray(window, np.float32))
+        if w.shape != (400,):
+            raise ValueError("window must have 400 taps")
+        self.h = C.c_void_p()
+        check(lib().ud_mel_create(engine.h, _ptr(self.fb), self.n_mels, _ptr(w), max_streams, C.byref(self.h)))
+
+    def features(self, audio: np.ndarray) -> np.ndarray:
+        """Full utterance: [n // 160 + 1, n_mels], the last frame 0."""
+        a = np.ascontiguousarray(np.asarray(audio, np.float32))
+        T = a.shape[0] // self.HOP + 1
+        out = np.empty((T, self.n_mels), np.float32)
+        nf = C.c_int()
+        check(lib().ud_mel_features(self.h, _ptr(a), a.shape[0], _ptr(out), T, C.byref(nf)))
+        return out[:nf.value]
+
+    def features_device(self, audio_dev_ptr: int, sample_off, n_samples, mel_dev_ptr: int, row_off):
+        """Device-resident batch, asynchronous on the engine stream (see ud_mel_features_device)."""
+        so = np.ascontiguousarray(np.asarray(sample_off, np.int64))
+        ro = np.ascontiguousarray(np.asarray(row_off, np.int64))
+        ns = _i32(n_samples)
+        check(lib().ud_mel_features_device(self.h, len(ns), C.c_void_p(audio_dev_ptr), _ptr(so, C.c_int64),
+                                           _ptr(ns, C.c_int), C.c_void_p(mel_dev_ptr), _ptr(ro, C.c_int64)))
+
+    def open(self) -> int:
+        i = C.c_int()
+        check(lib().ud_mel_stream_open(self.h, C.byref(i)))
+        return i.value
+
+    def close_stream(self, sid: int):
+        check(lib().ud_mel_stream_close(self.h, sid))
+
+    def push(self, ids, chunks, finish=None, cap_frames: int | None = None) -> list[np.ndarray]:
+        """Pushes one chunk of samples per stream; returns each stream's new frames [k, n_mels]."""
+        n = len(ids)
+        arrs = [np.ascontiguousarray(np.asarray(c, np.float32)) for c in chunks]
+        if cap_frames is None:
+            cap_frames = max([a.shape[0] // self.HOP + 4 for a in arrs] + [4])
+        ptrs = (C.POINTER(C.c_float) * n)(*[_ptr(a) for a in arrs])
+        ids_a, ns = _i32(ids), _i32([a.shape[0] for a in arrs])
+        fin = _i32([int(bool(f)) for f in finish]) if finish is not None else _i32([0] * n)
+        out = np.empty((n, cap_frames, self.n_mels), np.float32)
+        nf = np.zeros(n, np.int32)
+        check(lib().ud_mel_push_batch(self.h, n, _ptr(ids_a, C.c_int), ptrs, _ptr(ns, C.c_int), _ptr(fin, C.c_int),
+                                      _ptr(out), cap_frames, _ptr(nf, C.c_int)))
+        return [out[i, :nf[i]].copy() for i in range(n)]
+
+    def close(self):
+        if self.h:
+            check(lib().ud_mel_destroy(self.h))
+            self.h = C.c_void_p()
 
 
 def wait_probe(engine: "Engine", limit_ns: int):
