@@ -332,6 +332,133 @@ def run_cache_bench(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_mel_bench(args, world, rank, local):
+    """Log-mel frontend (ud_mel_*): per step, `--mel-streams` utterances of `--mel-seconds` of seeded audio
+    (0.1 N(0,1) plus a 440 Hz tone), resident in HBM, through one ud_mel_features_device call. value = mel frames
+    of all ranks per second (CUDA events on the engine stream, max over ranks); the roofline counts each audio
+    sample read once and each mel row written once. e2e: the same audio through live pushes (ud_mel_push_batch,
+    host samples in, host frames out), one push of the whole utterance per stream and step. The CPU baseline is
+    the oracle (check_spec's torch fp32 arithmetic) on one utterance."""
+    import ud
+    from ud_synthetic import hann_window, mel_filterbank
+
+    B, secs, sr = args.mel_streams, args.mel_seconds, 16000
+    n = int(secs * sr)
+    T = n // 160 + 1
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle.mel import features
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        fb, win = torch.from_numpy(mel_filterbank()), torch.from_numpy(hann_window())
+        a = torch.randn(n, generator=torch.Generator().manual_seed(0)) * 0.1
+        features(a, fb, win)
+        ts = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            features(a, fb, win)
+            ts.append(time.perf_counter() - t0)
+        v = T / statistics.median(ts)
+        print(json.dumps({"metric": "mel frames/s (log-mel frontend)", "value": v, "unit": "frames/s", "impl": "reference",
+                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "config": {"workload": f"one utterance of {secs} s per step (of {B} per GPU step)"},
+                          "cpu_baseline": {"value": v, "unit": "frames/s", "cores": torch.get_num_threads(),
+                                           "kind": "port", "sample": f"{args.steps} utterances of {secs} s"},
+                          "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    eng = ud.Engine(ud.default_config(n_layers=1, sub_channels=0, joint_dim=0, max_streams=1, max_batch=1),
+                    device=local)
+    fe = ud.MelFrontend(eng, mel_filterbank(), hann_window(), max_streams=B)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    t = torch.arange(n, device=dev, dtype=torch.float32) / sr
+    audio = (torch.randn(B, n, device=dev, generator=g) * 0.1 + 0.3 * torch.sin(2 * math.pi * 440 * t)).contiguous()
+    mel = torch.empty(B * T, fe.n_mels, device=dev)
+    so = np.arange(B, dtype=np.int64) * n
+    ro = np.arange(B, dtype=np.int64) * T
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(eng.cuda_stream(), device=dev)
+    for _ in range(args.warmup):
+        fe.features_device(audio.data_ptr(), so, [n] * B, mel.data_ptr(), ro)
+    eng.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            fe.features_device(audio.data_ptr(), so, [n] * B, mel.data_ptr(), ro)
+        e1.record(stream)
+        e1.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist, dev) / args.steps
+    frames = B * T * world
+    value = frames / (ms / 1e3)
+    nbytes = B * (4 * n + 4 * fe.n_mels * T)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    hbm, _, _, src = peaks()
+    # e2e: live pushes from host memory, frames back to host memory.
+    e2e = None
+    if not args.no_e2e:
+        host = audio.cpu().numpy()
+        ids = [fe.open() for _ in range(B)]
+        reps = max(1, min(args.steps, 5))
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fe.push(ids, [host[i] for i in range(B)], finish=[True] * B, cap_frames=T)
+            for i in ids:
+                fe.close_stream(i)
+            ids = [fe.open() for _ in range(B)]
+        dt = (time.perf_counter() - t0) / reps
+        for i in ids:
+            fe.close_stream(i)
+        e2e = {"value": B * T * world / max_over_ranks(dt, dist, dev), "unit": "frames/s",
+               "h2d_bytes_per_step": 4 * B * n, "d2h_bytes_per_step": 4 * B * T * fe.n_mels,
+               "timing": "host wall clock, ud_mel_push_batch of every stream's whole utterance (finish)"}
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        from oracle.mel import features
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        a = audio[0].cpu()
+        fb, win = torch.from_numpy(mel_filterbank()), torch.from_numpy(hann_window())
+        features(a, fb, win)
+        t0 = time.perf_counter()
+        k = 0
+        while k < 20 and time.perf_counter() - t0 < 10:
+            features(a, fb, win)
+            k += 1
+        dt = (time.perf_counter() - t0) / k
+        cpu = {"value": T / dt, "unit": "frames/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{k} utterances of {secs} s through the oracle (torch fp32 rfft)"}
+    if rank == 0:
+        print(json.dumps({"metric": "mel frames/s (log-mel frontend)", "value": value, "unit": "frames/s",
+                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                          "data": "synthetic",
+                          "config": {"workload": f"{B} utterances/GPU of {secs} s (16 kHz) per step, 128 mel bins",
+                                     "l2": "audio and mel larger than L2", "frames_per_step": B * T,
+                                     "parallelism": f"utterance-sharded x{world}, no collectives"},
+                          "e2e": e2e, "gpu_launches": args.steps,
+                          "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                       "frac": gbs / hbm, "traffic": None, "kernel": "mel_kernel",
+                                       "note": f"audio read once + mel written once per step / step time; peak = "
+                                               f"{src} HBM copy"},
+                          "cpu_baseline": cpu, "clocks": clk.summary()}), flush=True)
+    fe.close()
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_streamer_bench(args, world, rank, local):
     """Config 4: concurrent streams through the host-side streamer (ud_streamer_*, NemotronStreamer's chunk walk)
     at [70,6], `--c4-streams` slots per GPU (512 = 4096 over 8 GPUs). Streams arrive as a Poisson process of
@@ -521,10 +648,12 @@ def main():
                     help="also run greedy RNN-T decoding in each step (configs 2 and 4; C3 is the encoder step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "gemm"], default="c3",
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5", "gemm", "mel"], default="c3",
                     help="c3: the encoder step (default); c2: one stream at [70,1] with RNN-T decoding (latency); "
                          "c4: concurrent streams through the host-side streamer; c5: the cache-op microbenchmark; "
-                         "gemm: the tensor-core GEMM on one layer's shapes")
+                         "gemm: the tensor-core GEMM on one layer's shapes; mel: the log-mel frontend")
+    ap.add_argument("--mel-streams", type=int, default=512, help="mel: utterances per GPU step")
+    ap.add_argument("--mel-seconds", type=float, default=10.0, help="mel: seconds of audio per utterance")
     ap.add_argument("--c4-streams", type=int, default=512, help="c4: stream slots per GPU")
     ap.add_argument("--blank-offset", type=float, default=1.0,
                     help="c2/c4: added to the joint's blank bias. With N(0,0.02) weights greedy decoding emits the "
@@ -543,6 +672,9 @@ def main():
 
     if args.workload == "c5":
         run_cache_bench(args, world, rank, local)
+        return
+    if args.workload == "mel":
+        run_mel_bench(args, world, rank, local)
         return
     if args.workload == "c4":
         run_streamer_bench(args, world, rank, local)

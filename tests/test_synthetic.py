@@ -7,6 +7,7 @@ import torch
 
 import ud_synthetic as syn
 from oracle import cache_ring
+from oracle import mel as om
 from oracle import weights as ow
 
 
@@ -29,3 +30,8 @@ def test_full_model_names_and_dims():
 @pytest.mark.parametrize("k", [1, 2, 7, 14])
 def test_cache_bytes_identical(k):
     assert syn.cache_bytes_per_stream_step(24, 1024, 2, k) == cache_ring.bytes_per_stream_step(24, 1024, 2, k)
+
+
+def test_mel_buffers_identical():
+    assert (syn.mel_filterbank() == om.slaney_filterbank().numpy()).all()
+    assert (syn.hann_window() == om.hann_symmetric().numpy()).all()

@@ -5,9 +5,11 @@
 //   power |X|^2 (magnitude, then squared), mel = fb . power, log(mel + 2^-24)        (:91-107)
 //   frames t >= N / 160 are 0 (the last frame of an utterance)                        (:104-106)
 // The reference evaluates the DFT as two matrix products against cos/sin tables (:86-97). Here one warp takes
-// one frame: the 512 real samples become a 256-point complex sequence, transformed in shared memory by eight
-// radix-2 stages and unpacked into the 257 bins; the mel projection visits only each filter's non-zero bins.
-// Frames are independent, so any mix of utterances and live streams runs in one launch from a per-frame list.
+// one frame: the 512 real samples become a 256-point complex sequence, transformed in registers and across the
+// warp's lanes (decimation in frequency: three in-lane stages, five shuffle stages), unpacked into the 257 bins
+// through shared memory; the mel projection visits only each filter's non-zero bins.
+// Frames are independent, so any mix of utterances and live streams runs in one launch: a table of utterance
+// segments (24 bytes each) describes them, and each warp finds its frame's segment by binary search.
 //
 // Live streams keep, on the host, the raw samples the next frames still need; each push stages
 // [kept tail ; new samples] of every stream in one host-to-device copy and returns the frames whose windows are
@@ -35,12 +37,15 @@ using ud::host_fail;
 constexpr int kFFT = 512, kHalf = 256, kBins = 257, kHop = 160, kWin = 400, kWinOff = 56;
 constexpr int kMelWarps = 8;
 
-struct MelFrame {
-    int64_t base;    // buffer index of the utterance's sample 0 (only samples the frame reads are present)
+// A run of consecutive frames of one utterance.
+struct MelSeg {
+    int64_t base;    // buffer index of the utterance's sample 0 (only samples its frames read are present)
     int32_t n;       // samples of the utterance that exist (the right edge)
-    int32_t t;       // frame index within the utterance
-    int32_t zero;    // frame at or beyond the valid frames: written as zeros
-    int32_t row;     // output row
+    int32_t t0;      // first frame index of the run within the utterance
+    int32_t valid;   // frames t >= valid are written as zeros
+    int32_t f0;      // index of the run's first frame among all frames of the launch (runs in order)
+    int32_t row0;    // output row of frame t0
+    int32_t pad;
 };
 
 struct MelGeom {
@@ -54,10 +59,15 @@ struct MelGeom {
     int n_mels;
 };
 
+// Storage index of FFT point i in a warp's spectrum buffer: one pad word per 32 keeps both the lane-ordered
+// stores and the bit-reversed reads of the unpacking free of bank conflicts.
+__device__ __forceinline__ int zpad(int i) { return i + (i >> 5); }
+
 __global__ void __launch_bounds__(kMelWarps * 32) mel_kernel(const float* __restrict__ audio,
-                                                             const MelFrame* __restrict__ frames, int n_frames,
-                                                             const MelGeom g, float* __restrict__ out) {
-    __shared__ float re[kMelWarps][kHalf], im[kMelWarps][kHalf], pw[kMelWarps][kBins + 3];
+                                                             const MelSeg* __restrict__ segs, int n_segs,
+                                                             int n_frames, const MelGeom g, float* __restrict__ out) {
+    constexpr int kZ = kHalf + kHalf / 32;
+    __shared__ float re[kMelWarps][kZ], im[kMelWarps][kZ], pw[kMelWarps][kBins + 3];
     __shared__ float win[kWin], tc[kBins], ts[kBins];
     for (int i = threadIdx.x; i < kWin; i += blockDim.x) win[i] = g.window[i];
     for (int i = threadIdx.x; i < kBins; i += blockDim.x) {
@@ -69,59 +79,98 @@ __global__ void __launch_bounds__(kMelWarps * 32) mel_kernel(const float* __rest
     float* zr = re[warp];
     float* zi = im[warp];
     float* P = pw[warp];
+    // The 256-point FFT is decimation in frequency over i = lane + 32 j: the distances 128, 64 and 32 pair
+    // values of one lane (registers), 16 .. 1 pair lanes (shuffles). W_N^n = exp(-2 pi i n / N) = tc - i ts at
+    // table index n * 512 / N; each lane's twiddles depend only on the lane and are loaded once.
+    float w1c[4], w1s[4], w2c[2], w2s[2], wxc[5], wxs[5];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { w1c[j] = tc[2 * (lane + 32 * j)]; w1s[j] = ts[2 * (lane + 32 * j)]; }  // W_256
+#pragma unroll
+    for (int j = 0; j < 2; ++j) { w2c[j] = tc[4 * (lane + 32 * j)]; w2s[j] = ts[4 * (lane + 32 * j)]; }  // W_128
+    const float w3c = tc[8 * lane], w3s = ts[8 * lane];                                           // W_64^lane
+#pragma unroll
+    for (int st = 0; st < 5; ++st) {
+        const int d = 16 >> st;
+        const int k = (lane & (d - 1)) * (256 / d);                                               // W_2d^(lane mod d)
+        wxc[st] = tc[k];
+        wxs[st] = ts[k];
+    }
     for (int fi = blockIdx.x * kMelWarps + warp; fi < n_frames; fi += gridDim.x * kMelWarps) {
-        const MelFrame f = frames[fi];
-        float* orow = out + static_cast<size_t>(f.row) * g.n_mels;
-        if (f.zero) {
+        int lo = 0, hi = n_segs - 1;   // last run with f0 <= fi
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (segs[mid].f0 <= fi) lo = mid;
+            else hi = mid - 1;
+        }
+        const MelSeg f = segs[lo];
+        const int t = f.t0 + (fi - f.f0);
+        float* orow = out + static_cast<size_t>(f.row0 + (fi - f.f0)) * g.n_mels;
+        if (t >= f.valid) {
             for (int m = lane; m < g.n_mels; m += 32) orow[m] = 0.f;
             continue;
         }
-        // z[n] = v[2n] + i v[2n+1], v = windowed preemphasised samples of the frame, stored bit-reversed.
-        const int64_t s0 = static_cast<int64_t>(f.t) * kHop - kWin / 2;   // utterance index of window tap 0
+        // z[i] = v[2i] + i v[2i+1], v = the windowed preemphasised samples at frame positions 0..511.
+        const int64_t s0 = static_cast<int64_t>(t) * kHop - kWin / 2;   // utterance index of window tap 0
+        float vr[8], vi[8];
 #pragma unroll
-        for (int q = 0; q < kHalf / 32; ++q) {
-            const int nn = lane + 32 * q;
+        for (int j = 0; j < 8; ++j) {
+            const int i = lane + 32 * j;
             float v[2];
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const int j = 2 * nn + c;
+                const int pos = 2 * i + c;
                 v[c] = 0.f;
-                if (j >= kWinOff && j < kWinOff + kWin) {
-                    const int64_t s = s0 + (j - kWinOff);
-                    if (s >= 0 && s < f.n) {
-                        const float x = audio[f.base + s];
-                        const float y = s == 0 ? x : __fsub_rn(x, __fmul_rn(0.97f, audio[f.base + s - 1]));
-                        v[c] = __fmul_rn(y, win[j - kWinOff]);
+                if (pos >= kWinOff && pos < kWinOff + kWin) {
+                    const int64_t smp = s0 + (pos - kWinOff);
+                    if (smp >= 0 && smp < f.n) {
+                        const float x = audio[f.base + smp];
+                        const float y = smp == 0 ? x : __fsub_rn(x, __fmul_rn(0.97f, audio[f.base + smp - 1]));
+                        v[c] = __fmul_rn(y, win[pos - kWinOff]);
                     }
                 }
             }
-            const int r = __brev(nn) >> 24;
-            zr[r] = v[0];
-            zi[r] = v[1];
+            vr[j] = v[0];
+            vi[j] = v[1];
         }
-        // 256-point decimation-in-time FFT, W = exp(-2 pi i pos / 2h) = tc - i ts at k = pos * 256 / h.
-        for (int h = 1; h < kHalf; h <<= 1) {
-            __syncwarp();
+        // Butterfly (a, b) -> (a + b, (a - b) W).
+        auto bfly = [](float& ar, float& ai, float& br, float& bi, float c, float s) {
+            const float dr = ar - br, di = ai - bi;
+            ar += br;
+            ai += bi;
+            br = dr * c + di * s;
+            bi = di * c - dr * s;
+        };
 #pragma unroll
-            for (int q = 0; q < kHalf / 64; ++q) {
-                const int b = lane + 32 * q;
-                const int pos = b & (h - 1);
-                const int i0 = ((b - pos) << 1) + pos, i1 = i0 + h;
-                const int k = pos * (kHalf / h);
-                const float c = tc[k], s = ts[k];
-                const float xr = zr[i1], xi = zi[i1];
-                const float tr = c * xr + s * xi, ti = c * xi - s * xr;
-                const float ar = zr[i0], ai = zi[i0];
-                zr[i1] = ar - tr;
-                zi[i1] = ai - ti;
-                zr[i0] = ar + tr;
-                zi[i0] = ai + ti;
+        for (int j = 0; j < 4; ++j) bfly(vr[j], vi[j], vr[j + 4], vi[j + 4], w1c[j], w1s[j]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if ((j & 2) == 0) bfly(vr[j], vi[j], vr[j + 2], vi[j + 2], w2c[j & 1], w2s[j & 1]);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) bfly(vr[j], vi[j], vr[j + 1], vi[j + 1], w3c, w3s);
+#pragma unroll
+        for (int st = 0; st < 5; ++st) {
+            const int d = 16 >> st;
+            const bool upper = (lane & d) != 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float pr = __shfl_xor_sync(0xffffffffu, vr[j], d);
+                const float pi = __shfl_xor_sync(0xffffffffu, vi[j], d);
+                const float dr = pr - vr[j], di = pi - vi[j];
+                const float sr = vr[j] + pr, si = vi[j] + pi;
+                vr[j] = upper ? dr * wxc[st] + di * wxs[st] : sr;
+                vi[j] = upper ? di * wxc[st] - dr * wxs[st] : si;
             }
+        }
+        // Point i now holds Z[bitrev8(i)].
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            zr[zpad(lane + 32 * j)] = vr[j];
+            zi[zpad(lane + 32 * j)] = vi[j];
         }
         __syncwarp();
         // Real-input spectrum: X[k] = E[k] - i W^k D[k], E/D the even/odd parts of Z[k] and conj(Z[256-k]).
         for (int k = lane; k < kBins; k += 32) {
-            const int ka = k & (kHalf - 1), kb = (kHalf - k) & (kHalf - 1);
+            const int ka = zpad(__brev(k & (kHalf - 1)) >> 24), kb = zpad(__brev((kHalf - k) & (kHalf - 1)) >> 24);
             const float Ar = zr[ka], Ai = zi[ka], Br = zr[kb], Bi = -zi[kb];
             const float Er = 0.5f * (Ar + Br), Ei = 0.5f * (Ai + Bi);
             const float Dr = 0.5f * (Ar - Br), Di = 0.5f * (Ai - Bi);
@@ -132,10 +181,10 @@ __global__ void __launch_bounds__(kMelWarps * 32) mel_kernel(const float* __rest
         }
         __syncwarp();
         for (int m = lane; m < g.n_mels; m += 32) {
-            const int lo = g.fb_lo[m], len = g.fb_len[m];
+            const int lo2 = g.fb_lo[m], len = g.fb_len[m];
             const float* w = g.fb_w + g.fb_off[m];
             float acc = 0.f;
-            for (int j = 0; j < len; ++j) acc = fmaf(w[j], P[lo + j], acc);
+            for (int j = 0; j < len; ++j) acc = fmaf(w[j], P[lo2 + j], acc);
             orow[m] = logf(acc + 5.9604644775390625e-8f);   // + 2^-24
         }
         __syncwarp();
@@ -162,9 +211,9 @@ struct ud_mel {
     float* samples_h = nullptr;
     float* samples_d = nullptr;
     size_t samples_cap = 0;
-    MelFrame* frames_h = nullptr;
-    MelFrame* frames_d = nullptr;
-    size_t frames_cap = 0;
+    MelSeg* segs_h = nullptr;
+    MelSeg* segs_d = nullptr;
+    size_t segs_cap = 0;
     float* mel_h = nullptr;
     float* mel_d = nullptr;
     size_t mel_cap = 0;   // rows
@@ -213,10 +262,10 @@ ud_status grow(ud_mel* m, T** h, T** d, size_t* cap, size_t need) {
     return UD_OK;
 }
 
-void launch_frames(ud_mel* m, const float* audio_d, const MelFrame* frames_d, int n_frames, float* out_d) {
+void launch_frames(ud_mel* m, const float* audio_d, const MelSeg* segs_d, int n_segs, int n_frames, float* out_d) {
     if (n_frames <= 0) return;
     const int blocks = std::min((n_frames + kMelWarps - 1) / kMelWarps, m->num_sms * 8);
-    mel_kernel<<<blocks, kMelWarps * 32, 0, m->stream>>>(audio_d, frames_d, n_frames, m->g, out_d);
+    mel_kernel<<<blocks, kMelWarps * 32, 0, m->stream>>>(audio_d, segs_d, n_segs, n_frames, m->g, out_d);
 }
 
 // Waits until the previous call's uploads have left the pinned staging buffers.
@@ -296,7 +345,7 @@ ud_status ud_mel_destroy(ud_mel* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     for (void* p : m->allocs) cudaFree(p);
     if (m->samples_h) cudaFreeHost(m->samples_h);
-    if (m->frames_h) cudaFreeHost(m->frames_h);
+    if (m->segs_h) cudaFreeHost(m->segs_h);
     if (m->mel_h) cudaFreeHost(m->mel_h);
     if (m->staged) cudaEventDestroy(m->staged);
     delete m;
@@ -317,21 +366,18 @@ ud_status ud_mel_features_device(ud_mel* m, int n, const float* audio_dev, const
     if (cudaSetDevice(m->device) != cudaSuccess) return host_fail(UD_ERR_CUDA, "cudaSetDevice failed");
     ud_status st = wait_staged(m);
     if (st != UD_OK) return st;
-    if ((st = grow(m, &m->frames_h, &m->frames_d, &m->frames_cap, total)) != UD_OK) return st;
-    size_t k = 0;
+    if ((st = grow(m, &m->segs_h, &m->segs_d, &m->segs_cap, static_cast<size_t>(n))) != UD_OK) return st;
+    int k = 0, f0 = 0;
     for (int i = 0; i < n; ++i) {
-        const int T = n_samples[i] / kHop + 1, valid = n_samples[i] / kHop;
-        for (int t = 0; t < T; ++t) {
-            const int64_t row = row_off[i] + t;
-            if (row > INT32_MAX) return host_fail(UD_ERR_INVALID_ARGUMENT, "output row out of range");
-            m->frames_h[k++] = MelFrame{sample_off[i], n_samples[i], t, t >= valid ? 1 : 0, static_cast<int32_t>(row)};
-        }
+        const int T = n_samples[i] / kHop + 1;
+        if (row_off[i] + T > INT32_MAX) return host_fail(UD_ERR_INVALID_ARGUMENT, "output row out of range");
+        m->segs_h[k++] = MelSeg{sample_off[i], n_samples[i], 0, n_samples[i] / kHop, f0, static_cast<int32_t>(row_off[i]), 0};
+        f0 += T;
     }
-    if (total > 0 &&
-        cudaMemcpyAsync(m->frames_d, m->frames_h, sizeof(MelFrame) * total, cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
-        return host_fail(UD_ERR_CUDA, "frame list upload failed");
+    if (k > 0 && cudaMemcpyAsync(m->segs_d, m->segs_h, sizeof(MelSeg) * k, cudaMemcpyHostToDevice, m->stream) != cudaSuccess)
+        return host_fail(UD_ERR_CUDA, "segment table upload failed");
     cudaEventRecord(m->staged, m->stream);
-    launch_frames(m, audio_dev, m->frames_d, static_cast<int>(total), mel_dev);
+    launch_frames(m, audio_dev, m->segs_d, k, f0, mel_dev);
     if (cudaGetLastError() != cudaSuccess) return host_fail(UD_ERR_CUDA, "mel kernel launch failed");
     return UD_OK;
 }
@@ -398,27 +444,26 @@ ud_status ud_mel_push_batch(ud_mel* m, int n, const int* ids, const float* const
         frames_out[i] = std::max(0, end[i] - s.frames);
     }
     if ((st = grow(m, &m->samples_h, &m->samples_d, &m->samples_cap, samples)) != UD_OK) return st;
-    if ((st = grow(m, &m->frames_h, &m->frames_d, &m->frames_cap, total)) != UD_OK) return st;
+    if ((st = grow(m, &m->segs_h, &m->segs_d, &m->segs_cap, static_cast<size_t>(n))) != UD_OK) return st;
     if ((st = grow(m, &m->mel_h, &m->mel_d, &m->mel_cap, total * m->n_mels)) != UD_OK) return st;
-    size_t k = 0;
+    int k = 0, f0 = 0;
     for (int i = 0; i < n; ++i) {
         MelStream& s = m->streams[ids[i]];
         const int64_t cnt = s.n - first[i];
         if (cnt > 0) std::memcpy(m->samples_h + stage_off[i], s.tail.data() + (first[i] - s.tail0), sizeof(float) * cnt);
-        for (int t = s.frames; t < end[i]; ++t) {
-            m->frames_h[k] = MelFrame{stage_off[i] - first[i], static_cast<int32_t>(s.n), t, t >= valid[i] ? 1 : 0,
-                                      static_cast<int32_t>(k)};
-            ++k;
-        }
+        const int nf = std::max(0, end[i] - s.frames);
+        if (nf == 0) continue;
+        m->segs_h[k++] = MelSeg{stage_off[i] - first[i], static_cast<int32_t>(s.n), s.frames, valid[i], f0, f0, 0};
+        f0 += nf;
     }
     if (total > 0) {
         bool ok = samples == 0 || cudaMemcpyAsync(m->samples_d, m->samples_h, sizeof(float) * samples,
                                                   cudaMemcpyHostToDevice, m->stream) == cudaSuccess;
-        ok = ok && cudaMemcpyAsync(m->frames_d, m->frames_h, sizeof(MelFrame) * total, cudaMemcpyHostToDevice,
+        ok = ok && cudaMemcpyAsync(m->segs_d, m->segs_h, sizeof(MelSeg) * k, cudaMemcpyHostToDevice,
                                    m->stream) == cudaSuccess;
         if (!ok) return host_fail(UD_ERR_CUDA, "mel staging upload failed");
         cudaEventRecord(m->staged, m->stream);
-        launch_frames(m, m->samples_d, m->frames_d, static_cast<int>(total), m->mel_d);
+        launch_frames(m, m->samples_d, m->segs_d, k, static_cast<int>(total), m->mel_d);
         if (cudaGetLastError() != cudaSuccess) return host_fail(UD_ERR_CUDA, "mel kernel launch failed");
         if (cudaMemcpyAsync(m->mel_h, m->mel_d, sizeof(float) * total * m->n_mels, cudaMemcpyDeviceToHost,
                             m->stream) != cudaSuccess ||

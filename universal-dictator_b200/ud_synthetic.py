@@ -9,8 +9,10 @@ The test suite checks that these tensors are identical to the ones its CPU oracl
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 
@@ -120,3 +122,31 @@ def cache_bytes_per_stream_step(n_layers: int, d: int, elem: int, k: int, left_c
     kv = 2 * (k + k + left_context + left_context)
     conv = min(k, conv_rows) + k + conv_rows + conv_rows
     return n_layers * row * (kv + conv)
+
+
+def hann_window(n: int = 400) -> np.ndarray:
+    """Symmetric Hann window (the formula of the checkpoint's preprocessor.featurizer.window buffer)."""
+    k = np.arange(n, dtype=np.float64)
+    return (0.5 - 0.5 * np.cos(2 * math.pi * k / (n - 1))).astype(np.float32)
+
+
+def mel_filterbank(n_mels: int = 128, sr: int = 16000, n_fft: int = 512, fmin: float = 0.0,
+                   fmax: float = 8000.0) -> np.ndarray:
+    """[n_mels, n_fft // 2 + 1] Slaney-scale triangular filters with Slaney (unit-area) normalisation, the
+    published construction of the checkpoint's preprocessor.featurizer.fb buffer."""
+    def hz_to_mel(f):
+        f = np.asarray(f, np.float64)
+        return np.where(f >= 1000.0, 15.0 + np.log(np.maximum(f, 1e-10) / 1000.0) / (np.log(6.4) / 27.0),
+                        f / (200.0 / 3))
+
+    def mel_to_hz(m):
+        m = np.asarray(m, np.float64)
+        return np.where(m >= 15.0, 1000.0 * np.exp((np.log(6.4) / 27.0) * (m - 15.0)), m * (200.0 / 3))
+
+    fft_f = np.linspace(0, sr / 2, n_fft // 2 + 1)
+    hz = mel_to_hz(np.linspace(hz_to_mel(fmin), hz_to_mel(fmax), n_mels + 2))
+    fdiff = np.diff(hz)
+    ramps = hz[:, None] - fft_f[None, :]
+    w = np.maximum(0.0, np.minimum(-ramps[:-2] / fdiff[:-1, None], ramps[2:] / fdiff[1:, None]))
+    w *= (2.0 / (hz[2:] - hz[:-2]))[:, None]
+    return w.astype(np.float32)
