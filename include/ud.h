@@ -276,6 +276,21 @@ UD_API ud_status ud_mel_stream_close(ud_mel* m, int id);
 UD_API ud_status ud_mel_push_batch(ud_mel* m, int n, const int* ids, const float* const* audio, const int* n_samples,
                                    const int* finish, float* mel_out, int cap_frames, int* frames_out);
 
+/* ---- SentencePiece detokenizer (SentencePieceDecoder, Sources/DictatorCore/Text/SentencePiece.swift:5-32)
+ *
+ * Host code, no GPU. The vocabulary is the tokenizer.vocab text: one "piece\tscore" line per id, empty lines
+ * skipped. Decoding joins the pieces of the valid ids: "<0xHH>" pieces give the byte, <unk> <s> </s> <pad>
+ * nothing, other pieces their UTF-8 with U+2581 turned into a space; ill-formed UTF-8 becomes U+FFFD and one
+ * leading space is dropped. ud_detok_decode writes at most cap - 1 bytes plus a NUL and the full length to
+ * *len_out (call with cap 0 to size the buffer). */
+typedef struct ud_detok ud_detok;
+UD_API ud_status ud_detok_create(const char* vocab_text, size_t len, ud_detok** out);
+UD_API ud_status ud_detok_create_file(const char* path, ud_detok** out);
+UD_API ud_status ud_detok_destroy(ud_detok* d);
+UD_API int ud_detok_size(const ud_detok* d);
+UD_API ud_status ud_detok_decode(const ud_detok* d, const int32_t* ids, int n, char* out, size_t cap,
+                                 size_t* len_out);
+
 /* Text of the last error on this thread ("" if none). Returns the full length. */
 UD_API size_t ud_last_error(char* buf, size_t len);
 UD_API const char* ud_status_string(ud_status s);

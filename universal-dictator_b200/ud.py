@@ -42,7 +42,8 @@ ABI_SYMBOLS = [
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
     "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
     "ud_streamer_release", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
-    "ud_mel_stream_open", "ud_mel_stream_close", "ud_mel_push_batch",
+    "ud_mel_stream_open", "ud_mel_stream_close", "ud_mel_push_batch", "ud_detok_create", "ud_detok_create_file",
+    "ud_detok_destroy", "ud_detok_size", "ud_detok_decode",
 ]
 
 
@@ -122,6 +123,11 @@ def lib() -> C.CDLL:
             "ud_mel_stream_open": (I, [VP, P(I)]),
             "ud_mel_stream_close": (I, [VP, I]),
             "ud_mel_push_batch": (I, [VP, I, P(I), P(P(F)), P(I), P(I), P(F), I, P(I)]),
+            "ud_detok_create": (I, [C.c_char_p, C.c_size_t, P(VP)]),
+            "ud_detok_create_file": (I, [C.c_char_p, P(VP)]),
+            "ud_detok_destroy": (I, [VP]),
+            "ud_detok_size": (I, [VP]),
+            "ud_detok_decode": (I, [VP, P(C.c_int32), I, C.c_char_p, C.c_size_t, P(C.c_size_t)]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -495,6 +501,35 @@ class MelFrontend:
     def close(self):
         if self.h:
             check(lib().ud_mel_destroy(self.h))
+            self.h = C.c_void_p()
+
+
+class SentencePieceDecoder:
+    """SentencePiece detokenizer (SentencePiece.swift:5-32) over the C ABI; host only, no GPU."""
+
+    def __init__(self, vocab_text: str | bytes | None = None, vocab_file: str | None = None):
+        self.h = C.c_void_p()
+        if vocab_file is not None:
+            check(lib().ud_detok_create_file(str(vocab_file).encode(), C.byref(self.h)))
+        else:
+            b = vocab_text.encode() if isinstance(vocab_text, str) else bytes(vocab_text or b"")
+            check(lib().ud_detok_create(b, len(b), C.byref(self.h)))
+
+    @property
+    def count(self) -> int:
+        return lib().ud_detok_size(self.h)
+
+    def decode(self, ids) -> str:
+        a = _i32(list(ids))
+        n = C.c_size_t()
+        check(lib().ud_detok_decode(self.h, _ptr(a, C.c_int32), len(a), None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value + 1)
+        check(lib().ud_detok_decode(self.h, _ptr(a, C.c_int32), len(a), buf, n.value + 1, C.byref(n)))
+        return buf.raw[:n.value].decode("utf-8")
+
+    def close(self):
+        if self.h:
+            lib().ud_detok_destroy(self.h)
             self.h = C.c_void_p()
 
 
