@@ -213,41 +213,6 @@ UD_API ud_status ud_debug_wait_probe(ud_engine* e, uint64_t limit_ns);
 /* The configuration the engine was created with. */
 UD_API ud_status ud_get_config(ud_engine* e, ud_config* out);
 
-/* ---- Host-side batched streamer (NemotronStreamer, Sources/DictatorCore/Nemotron/NemotronStreamer.swift:16-163)
- *
- * The chunk walk of one stream (runBuffered, NemotronStreamer.swift:70-91, and the live drainChunks, :109-154):
- * the stream has consumed `idx` of the `avail` mel rows it has so far; `last` says no more rows will come.
- * Returns 1 when a chunk is ready and fills rows [*start, *start + *n_rows) (the first chunk 1+8R rows with no
- * pre-encode cache, later chunks 9 cached rows + 8+8R new rows, the final chunk shorter), *keep_all (the final
- * chunk) and *next_idx; 0 when the stream must wait for rows (a full chunk is run only once more rows, or the
- * end, have arrived, so the final chunk is known); -1 when it has ended (what remains is too short to encode). */
-UD_API int ud_chunk_next(int lookahead, int idx, int avail, int last, int* start, int* n_rows, int* keep_all,
-                         int* next_idx);
-
-/* A streamer drives many streams of one engine: each step runs every stream with a ready chunk in one batched
- * encoder pass (ud_step_batch, with greedy RNN-T decoding when decode != 0) and appends the tokens to the
- * stream. Streams read their mel from a caller-owned host buffer [capacity_rows, mel_bins] that stays valid
- * until the stream is released; rows become available through ud_streamer_push. A stream's engine slot is
- * taken at open (UD_ERR_POOL_EXHAUSTED when the engine has none free) and freed when its final chunk has run.
- * Calls on one streamer are serialised by the caller. */
-typedef struct ud_streamer ud_streamer;
-typedef int32_t ud_streamer_id;
-UD_API ud_status ud_streamer_create(ud_engine* e, int lookahead, int decode, ud_streamer** out);
-UD_API ud_status ud_streamer_destroy(ud_streamer* s);
-UD_API ud_status ud_streamer_open(ud_streamer* s, const float* mel, int capacity_rows, ud_streamer_id* out);
-/* n_rows more rows are valid at the end of the stream's buffer; last != 0: the stream ends there. */
-UD_API ud_status ud_streamer_push(ud_streamer* s, ud_streamer_id id, int n_rows, int last);
-/* One batched step (at most max_batch streams, in order of id); *n_stepped streams advanced one chunk,
- * *n_finished of them ran their final chunk (or ended with a remainder too short to encode). */
-UD_API ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished);
-/* The ids of the streams that finished in the last ud_streamer_step (up to cap copied) and their count. */
-UD_API ud_status ud_streamer_finished(ud_streamer* s, ud_streamer_id* out, int cap, int* n);
-/* Tokens so far (up to cap copied), the total count, and whether the stream has finished. */
-UD_API ud_status ud_streamer_tokens(ud_streamer* s, ud_streamer_id id, int32_t* out, int cap, int* n_tokens,
-                                    int* finished);
-/* Forgets a stream (closing its engine slot if it has not finished); its id may be reused. */
-UD_API ud_status ud_streamer_release(ud_streamer* s, ud_streamer_id id);
-
 /* ---- Log-mel frontend (NemoMelFrontend / NemoMelStream, Sources/DictatorCore/Audio/NemoMel.swift:10-161)
  *
  * NeMo's FilterbankFeatures at inference on the engine's device and CUDA stream: preemphasis 0.97, centred
@@ -275,6 +240,52 @@ UD_API ud_status ud_mel_stream_open(ud_mel* m, int* id);
 UD_API ud_status ud_mel_stream_close(ud_mel* m, int id);
 UD_API ud_status ud_mel_push_batch(ud_mel* m, int n, const int* ids, const float* const* audio, const int* n_samples,
                                    const int* finish, float* mel_out, int cap_frames, int* frames_out);
+
+/* ---- Host-side batched streamer (NemotronStreamer, Sources/DictatorCore/Nemotron/NemotronStreamer.swift:16-163)
+ *
+ * The live chunk walk of one stream (drainChunks, NemotronStreamer.swift:109-154): the stream has consumed `idx`
+ * of the `avail` mel rows it has so far; `last` says no more rows will come. Returns 1 when a chunk is ready:
+ * rows [*start, *start + *valid_rows) (the first chunk 1+8R rows with no pre-encode cache, later chunks 9
+ * cached rows + 8+8R new rows, run as soon as they exist; the final chunk shorter) followed by
+ * *n_rows - *valid_rows zero rows that extend a final tail shorter than the minimum chunk (8 rows, 1 for a first
+ * chunk) when end_padding != 0 (the reference's endPadding, :29-31; with end_padding 0 such a tail is dropped
+ * as NeMo's batch-1 schedule and runBuffered, :70-91, do), *keep_all (the final chunk) and *next_idx. Returns 0
+ * when the stream must wait for rows, -1 when it has ended. */
+UD_API int ud_chunk_next(int lookahead, int idx, int avail, int last, int end_padding, int* start, int* n_rows,
+                         int* valid_rows, int* keep_all, int* next_idx);
+
+/* A streamer drives many streams of one engine: each step runs every stream with a ready chunk in one batched
+ * encoder pass (ud_step_batch, with greedy RNN-T decoding when decode != 0) and appends the tokens to the
+ * stream. A stream takes mel rows from a caller-owned host buffer [capacity_rows, mel_bins] that stays valid
+ * until the stream is released (rows become available through ud_streamer_push), or audio through a mel
+ * frontend of the same engine (ud_streamer_open_audio / ud_streamer_push_audio, NemotronStreamer.push(samples:)
+ * and flush(), :95-107). A stream's engine slot is taken at open (UD_ERR_POOL_EXHAUSTED when the engine has none
+ * free) and freed when its final chunk has run. End padding is on by default. Calls on one streamer are
+ * serialised by the caller. */
+typedef struct ud_streamer ud_streamer;
+typedef int32_t ud_streamer_id;
+UD_API ud_status ud_streamer_create(ud_engine* e, int lookahead, int decode, ud_streamer** out);
+UD_API ud_status ud_streamer_destroy(ud_streamer* s);
+UD_API ud_status ud_streamer_set_end_padding(ud_streamer* s, int on);
+UD_API ud_status ud_streamer_open(ud_streamer* s, const float* mel, int capacity_rows, ud_streamer_id* out);
+/* n_rows more rows are valid at the end of the stream's buffer; last != 0: the stream ends there. */
+UD_API ud_status ud_streamer_push(ud_streamer* s, ud_streamer_id id, int n_rows, int last);
+/* An audio stream: its mel comes from frontend `mel` (one frontend for all audio streams of a streamer). */
+UD_API ud_status ud_streamer_open_audio(ud_streamer* s, ud_mel* mel, ud_streamer_id* out);
+/* n_samples[i] more samples of stream ids[i] (one frontend call for all of them); last[i] != 0 ends the stream
+ * (NemotronStreamer.flush). last may be NULL. */
+UD_API ud_status ud_streamer_push_audio(ud_streamer* s, int n, const ud_streamer_id* ids, const float* const* samples,
+                                        const int* n_samples, const int* last);
+/* One batched step (at most max_batch streams, in order of id); *n_stepped streams advanced one chunk,
+ * *n_finished of them ran their final chunk (or ended with nothing left to encode). */
+UD_API ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished);
+/* The ids of the streams that finished in the last ud_streamer_step (up to cap copied) and their count. */
+UD_API ud_status ud_streamer_finished(ud_streamer* s, ud_streamer_id* out, int cap, int* n);
+/* Tokens so far (up to cap copied), the total count, and whether the stream has finished. */
+UD_API ud_status ud_streamer_tokens(ud_streamer* s, ud_streamer_id id, int32_t* out, int cap, int* n_tokens,
+                                    int* finished);
+/* Forgets a stream (closing its engine slot if it has not finished); its id may be reused. */
+UD_API ud_status ud_streamer_release(ud_streamer* s, ud_streamer_id id);
 
 /* ---- SentencePiece detokenizer (SentencePieceDecoder, Sources/DictatorCore/Text/SentencePiece.swift:5-32)
  *

@@ -232,6 +232,43 @@ class Encoder:
         return proj, keep, out, T, valid_t
 
 
+def drain_next(lookahead: int, idx: int, have: int, final: bool, end_padding: bool):
+    """One iteration of NemotronStreamer.drainChunks (NemotronStreamer.swift:109-154), the live chunk walk, for a
+    stream that has consumed mel rows up to `idx` of the `have` it holds: returns None to wait (final False) or
+    when the stream has ended (final True), else (cache_start, rows, pad_rows, keep_all, next_idx). A full chunk
+    runs as soon as its rows exist; at the end a tail shorter than the minimum chunk (8 rows, 1 for a first
+    chunk) is zero-extended to it and masked when `end_padding` (the reference's default), else dropped."""
+    sch = Schedule(lookahead)
+    first = idx == 0
+    size = sch.first_chunk if first else sch.chunk
+    end = idx + size
+    if end > have and not final:
+        return None
+    chunk_len = min(end, have) - idx
+    min_len = 1 if first else 8
+    if chunk_len <= 0 or (chunk_len < min_len and not (final and end_padding)):
+        return None
+    cache_start = idx if first else max(0, idx - sch.pre_encode_cache)
+    rows = min(end, have) - cache_start
+    pad = max(0, min_len - chunk_len)
+    is_last = final and end >= have
+    return cache_start, rows, pad, (pad > 0) or is_last, end
+
+
+def live_plan(total_rows: int, lookahead: int, end_padding: bool = True):
+    """drainChunks over a complete mel buffer: yields (row_start, n_rows, valid_rows, keep_all), n_rows including
+    the zero rows of a padded tail. Without end padding it equals runBuffered's walk (chunk_plan)."""
+    idx = 0
+    while True:
+        c = drain_next(lookahead, idx, total_rows, True, end_padding)
+        if c is None:
+            return
+        start, rows, pad, keep, idx = c
+        yield start, rows + pad, rows, keep
+        if keep:
+            return
+
+
 def chunk_plan(total_rows: int, lookahead: int, valid_frames: int | None = None):
     """NemotronStreamer.runBuffered's chunk walk (NemotronStreamer.swift:70-91) over a full mel
     buffer of `total_rows` rows: yields (row_start, n_rows, valid_rows, keep_all)."""

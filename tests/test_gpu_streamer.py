@@ -4,7 +4,11 @@
     (runBuffered's chunk walk, Encoder.stream_step, then RNNT.greedy with carried state);
   * the same streams fed row by row in random increments (live input) give the same tokens;
   * admission: opening more streams than the engine has slots is refused as a status, and a slot freed by a
-    finished stream is reused.
+    finished stream is reused;
+  * a short final tail is zero-extended and masked (end padding, the default) or dropped (end padding off);
+  * audio streams (NemotronStreamer.push(samples:) / flush()): the GPU mel frontend feeds the chunk walk; tokens
+    equal the oracle pipeline (oracle mel, drainChunks, encoder, greedy), and audio pushed in random sizes gives
+    exactly the tokens of the whole utterance pushed at once.
 The model is 2 layers with subsampling and a 1-layer prediction net (fp32 engine, 1e-4 tolerance class); the
 joint is sharpened so that token choices are decided by clear logit margins."""
 
@@ -16,13 +20,15 @@ import torch
 
 import ud
 from oracle.rnnt import RNNT, DecoderState
-from oracle.stream_step import Encoder, StreamState, chunk_plan
+from oracle.mel import features as mel_features
+from oracle.mel import hann_symmetric, slaney_filterbank
+from oracle.stream_step import Encoder, StreamState, live_plan
 from oracle.weights import ModelDims, make_weights, sharpen_joint
 
 pytestmark = pytest.mark.gpu
 
 R = 6
-LENGTHS = [500, 57, 230, 131, 9]   # includes a stream whose only chunk is its first, and a 1-chunk remainder
+LENGTHS = [500, 57, 230, 131, 9, 117]   # a stream whose only chunk is its first, a 1-chunk remainder, a 3-row tail
 
 
 @pytest.fixture(scope="module")
@@ -40,22 +46,25 @@ def _mels():
             for i, n in enumerate(LENGTHS)]
 
 
-def _oracle_tokens(sd, dims, mel: np.ndarray) -> list[int]:
+def _oracle_tokens(sd, dims, mel: np.ndarray, end_padding: bool = True) -> list[int]:
     enc, dec = Encoder(sd, dims), RNNT(sd, dims)
     st, ds = StreamState(dims), DecoderState(dims)
     toks: list[int] = []
-    m = torch.from_numpy(mel)
-    for start, n, valid, keep_all in chunk_plan(mel.shape[0], R):
-        proj, keep, *_ = enc.stream_step(st, m[start:start + n], n, valid, keep_all, R)
+    m = torch.from_numpy(np.ascontiguousarray(mel, np.float32))
+    for start, n, valid, keep_all in live_plan(mel.shape[0], R, end_padding):
+        rows = torch.zeros(n, m.shape[1])
+        rows[:valid] = m[start:start + valid]
+        proj, keep, *_ = enc.stream_step(st, rows, n, valid, keep_all, R)
         if keep:
             toks += dec.greedy(proj, ds)
     return toks
 
 
-def _run(eng, mels, live: bool, seed: int = 0) -> list[list[int]]:
+def _run(eng, mels, live: bool, seed: int = 0, end_padding: bool = True) -> list[list[int]]:
     """Admits streams as slots allow (4 of them), feeds them buffered or in random increments, steps until all
     are done; returns tokens per stream in input order."""
     s = ud.Streamer(eng, R, decode=True)
+    s.set_end_padding(end_padding)
     rng = random.Random(seed)
     try:
         pending = list(range(len(mels)))
@@ -84,12 +93,13 @@ def _run(eng, mels, live: bool, seed: int = 0) -> list[list[int]]:
         s.close()
 
 
-def test_buffered_streams_match_the_oracle(model):
+@pytest.mark.parametrize("end_padding", [True, False])
+def test_buffered_streams_match_the_oracle(model, end_padding):
     eng, sd, dims = model
     mels = _mels()
-    got = _run(eng, mels, live=False)
+    got = _run(eng, mels, live=False, end_padding=end_padding)
     for i, mel in enumerate(mels):
-        assert got[i] == _oracle_tokens(sd, dims, mel), i
+        assert got[i] == _oracle_tokens(sd, dims, mel, end_padding), i
     assert any(len(t) > 0 for t in got)
 
 
@@ -117,3 +127,58 @@ def test_admission_is_a_status_and_slots_are_reused(model):
             s.push(ids[1], 61)        # beyond the stream's buffer
     finally:
         s.close()
+
+
+def _audio(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    t = torch.arange(n, dtype=torch.float64) / 16000
+    return (0.2 * torch.sin(2 * np.pi * (300 + 40 * seed) * t) + 0.05 * torch.randn(n, generator=g,
+                                                                                    dtype=torch.float64)).float().numpy()
+
+
+def _run_audio(eng, fe, audios, sizes=None, seed=0):
+    s = ud.Streamer(eng, R, decode=True)
+    rng = random.Random(seed)
+    try:
+        ids = [s.open_audio(fe) for _ in audios]
+        pos = [0] * len(audios)
+        while any(p < len(a) for p, a in zip(pos, audios)):
+            sel = [i for i in range(len(audios)) if pos[i] < len(audios[i])]
+            chunks, last = [], []
+            for i in sel:
+                m = len(audios[i]) - pos[i] if sizes is None else min(len(audios[i]) - pos[i], rng.choice(sizes))
+                chunks.append(audios[i][pos[i]:pos[i] + m])
+                pos[i] += m
+                last.append(pos[i] == len(audios[i]))
+            s.push_audio([ids[i] for i in sel], chunks, last)
+            s.step()
+        for _ in range(64):
+            n, _ = s.step()
+            if all(s.tokens(i)[1] for i in ids):
+                break
+        out = []
+        for i in ids:
+            toks, fin = s.tokens(i)
+            assert fin
+            out.append(toks)
+            s.release(i)
+        return out
+    finally:
+        s.close()
+
+
+def test_audio_streams_match_the_oracle_pipeline(model):
+    eng, sd, dims = model
+    fb, win = slaney_filterbank(), hann_symmetric()
+    fe = ud.MelFrontend(eng, fb.numpy(), win.numpy(), max_streams=4)
+    try:
+        audios = [_audio(n, i) for i, n in enumerate([16000 * 3 + 77, 9000, 2500])]
+        got = _run_audio(eng, fe, audios)
+        for i, a in enumerate(audios):
+            mel, _ = mel_features(torch.from_numpy(a), fb, win)    # NeMo streaming counts every frame as valid
+            assert got[i] == _oracle_tokens(sd, dims, mel.numpy()), i
+        assert any(len(t) > 0 for t in got)
+        live = _run_audio(eng, fe, audios, sizes=[1, 160, 333, 1600, 4000], seed=5)
+        assert live == got
+    finally:
+        fe.close()

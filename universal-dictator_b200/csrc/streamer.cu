@@ -3,14 +3,21 @@
 // queue; here many streams share one engine and every step runs all streams with a ready chunk as one batched
 // encoder pass (ud_step_batch) followed by greedy RNN-T decoding with each stream's carried decoder state.
 //
-// The chunk walk is runBuffered's (NemotronStreamer.swift:70-91): the first chunk is 1 + 8R mel rows with no
-// pre-encode cache (and no subsampled frames dropped by the engine), later chunks are 8 + 8R new rows behind a
-// 9-row pre-encode cache, the final chunk is whatever remains (at least 8 rows; 1 for a stream's only chunk)
-// and keeps all its valid frames (keepAll). For live input (drainChunks, :109-154) a full chunk runs only once
-// more rows or the end have arrived, so the final chunk is recognised as such and the outputs of a stream fed
-// row by row equal those of the same stream fed at once.
+// The chunk walk is the live one, drainChunks (NemotronStreamer.swift:109-154): the first chunk is 1 + 8R mel
+// rows with no pre-encode cache (and no subsampled frames dropped by the engine), later chunks are 8 + 8R new
+// rows behind a 9-row pre-encode cache, each run as soon as its rows exist; at the end the rest runs as the final
+// chunk (keepAll), a tail shorter than the minimum chunk (8 rows; 1 for a stream's only chunk) zero-extended to
+// it and masked when end padding is on (the reference's default, endPadding :29-31) or dropped when it is off
+// (NeMo's batch-1 schedule and runBuffered, :70-91). Over a complete buffer without end padding the walk is
+// runBuffered's, and a stream fed row by row gives the chunks of the same stream fed at once.
 //
-// Only the public C ABI of the engine is used.
+// Streams take mel rows from a caller-owned buffer (ud_streamer_open / ud_streamer_push), or audio through the
+// GPU mel frontend (ud_streamer_open_audio / ud_streamer_push_audio: NemotronStreamer.push(samples:) and
+// flush(), :95-107), whose rows the streamer keeps only as far back as the pre-encode cache needs.
+//
+// Only the public C ABI of the engine and the mel frontend is used.
+#include <algorithm>
+#include <cstddef>
 #include <cstring>
 #include <vector>
 
@@ -26,10 +33,14 @@ constexpr int kPreEncodeCache = 9;   // NemotronSchedule.swift:7-16
 
 struct StreamRec {
     bool used = false, finished = false, last = false;
-    const float* mel = nullptr;
+    const float* mel = nullptr;     // caller-owned rows [capacity, mel_bins] (mel streams)
     int capacity = 0, avail = 0, idx = 0;
     ud_stream_id slot = -1;
     std::vector<int32_t> tokens;
+    // audio streams: the frontend's stream and the rows kept from row `own_start` on
+    int mel_id = -1;
+    std::vector<float> own;
+    int own_start = 0;
 };
 
 }  // namespace
@@ -41,9 +52,12 @@ struct ud_streamer {
     std::vector<StreamRec> recs;
     std::vector<int> free_ids;
     // per-step scratch, sized for max_batch streams
+    int end_padding = 1;
+    ud_mel* mel = nullptr;          // the frontend of the audio streams (all of them use one)
     std::vector<ud_stream_id> ids;
     std::vector<const float*> mels;
-    std::vector<int> rows, keep, frames, ntok, who, next;
+    std::vector<int> rows, valid, keep, frames, ntok, who, next;
+    std::vector<float> pad;         // padded final tails, max_batch x (9 + 8) rows
     std::vector<float> proj;
     std::vector<int32_t> toks;
     std::vector<ud_streamer_id> just_finished;   // ids that finished in the last step
@@ -51,27 +65,25 @@ struct ud_streamer {
 
 extern "C" {
 
-int ud_chunk_next(int lookahead, int idx, int avail, int last, int* start, int* n_rows, int* keep_all,
-                  int* next_idx) {
+int ud_chunk_next(int lookahead, int idx, int avail, int last, int end_padding, int* start, int* n_rows,
+                  int* valid_rows, int* keep_all, int* next_idx) {
     if (lookahead < 0 || idx < 0 || avail < idx) return -1;
     const bool first = idx == 0;
     const int size = first ? 1 + 8 * lookahead : 8 + 8 * lookahead;
-    int chunk_len, keep;
-    if (!last) {
-        if (avail - idx <= size) return 0;   // not yet known whether this chunk is the final one
-        chunk_len = size;
-        keep = 0;
-    } else {
-        if (idx >= avail) return -1;
-        chunk_len = (idx + size < avail ? idx + size : avail) - idx;
-        if (chunk_len < (first ? 1 : 8)) return -1;
-        keep = idx + size >= avail ? 1 : 0;
-    }
+    const int end = idx + size;
+    if (end > avail && !last) return 0;   // the chunk's rows are not all here yet
+    const int chunk_end = end < avail ? end : avail;
+    const int chunk_len = chunk_end - idx;
+    const int min_len = first ? 1 : 8;
+    if (chunk_len <= 0 || (chunk_len < min_len && !end_padding)) return -1;   // the stream has ended
     const int cache_start = first ? idx : (idx - kPreEncodeCache > 0 ? idx - kPreEncodeCache : 0);
+    const int rows = chunk_end - cache_start;
+    const int pad = chunk_len < min_len ? min_len - chunk_len : 0;   // zero rows of a short final tail
     if (start) *start = cache_start;
-    if (n_rows) *n_rows = (idx - cache_start) + chunk_len;
-    if (keep_all) *keep_all = keep;
-    if (next_idx) *next_idx = idx + size;
+    if (n_rows) *n_rows = rows + pad;
+    if (valid_rows) *valid_rows = rows;
+    if (keep_all) *keep_all = (pad > 0 || (last && end >= avail)) ? 1 : 0;
+    if (next_idx) *next_idx = end;
     return 1;
 }
 
@@ -94,7 +106,9 @@ ud_status ud_streamer_create(ud_engine* e, int lookahead, int decode, ud_streame
     s->ids.resize(B);
     s->mels.resize(B);
     s->rows.resize(B);
+    s->valid.resize(B);
     s->keep.resize(B);
+    s->pad.resize(B * (kPreEncodeCache + 8) * static_cast<size_t>(cfg.mel_bins));
     s->frames.resize(B);
     s->ntok.resize(B);
     s->who.resize(B);
@@ -105,17 +119,23 @@ ud_status ud_streamer_create(ud_engine* e, int lookahead, int decode, ud_streame
     return UD_OK;
 }
 
+ud_status ud_streamer_set_end_padding(ud_streamer* s, int on) {
+    if (!s) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL streamer");
+    s->end_padding = on ? 1 : 0;
+    return UD_OK;
+}
+
 ud_status ud_streamer_destroy(ud_streamer* s) {
     if (!s) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL streamer");
-    for (StreamRec& r : s->recs)
+    for (StreamRec& r : s->recs) {
         if (r.used && !r.finished && r.slot >= 0) ud_stream_close(s->e, r.slot);
+        if (r.used && r.mel_id >= 0 && s->mel) ud_mel_stream_close(s->mel, r.mel_id);
+    }
     delete s;
     return UD_OK;
 }
 
-ud_status ud_streamer_open(ud_streamer* s, const float* mel, int capacity_rows, ud_streamer_id* out) {
-    if (!s || !mel || !out) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
-    if (capacity_rows < 1) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "empty mel buffer");
+static ud_status open_rec(ud_streamer* s, ud_streamer_id* out) {
     ud_stream_id slot = -1;
     ud_status st = ud_stream_open(s->e, s->lookahead, &slot);
     if (st != UD_OK) return st;
@@ -130,10 +150,35 @@ ud_status ud_streamer_open(ud_streamer* s, const float* mel, int capacity_rows, 
     StreamRec& r = s->recs[id];
     r = StreamRec();
     r.used = true;
-    r.mel = mel;
-    r.capacity = capacity_rows;
     r.slot = slot;
     *out = id;
+    return UD_OK;
+}
+
+ud_status ud_streamer_open(ud_streamer* s, const float* mel, int capacity_rows, ud_streamer_id* out) {
+    if (!s || !mel || !out) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (capacity_rows < 1) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "empty mel buffer");
+    ud_status st = open_rec(s, out);
+    if (st != UD_OK) return st;
+    StreamRec& r = s->recs[*out];
+    r.mel = mel;
+    r.capacity = capacity_rows;
+    return UD_OK;
+}
+
+ud_status ud_streamer_open_audio(ud_streamer* s, ud_mel* mel, ud_streamer_id* out) {
+    if (!s || !mel || !out) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (s->mel && s->mel != mel) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "a streamer's audio streams share one frontend");
+    int mid = -1;
+    ud_status st = ud_mel_stream_open(mel, &mid);
+    if (st != UD_OK) return st;
+    st = open_rec(s, out);
+    if (st != UD_OK) {
+        ud_mel_stream_close(mel, mid);
+        return st;
+    }
+    s->mel = mel;
+    s->recs[*out].mel_id = mid;
     return UD_OK;
 }
 
@@ -142,9 +187,43 @@ static StreamRec* rec_of(ud_streamer* s, ud_streamer_id id) {
     return &s->recs[id];
 }
 
+ud_status ud_streamer_push_audio(ud_streamer* s, int n, const ud_streamer_id* ids, const float* const* samples,
+                                 const int* n_samples, const int* last) {
+    if (!s || n < 0 || (n > 0 && (!ids || !samples || !n_samples))) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (n == 0) return UD_OK;
+    std::vector<int> mids(static_cast<size_t>(n)), fin(static_cast<size_t>(n)), frames(static_cast<size_t>(n));
+    int cap = 1;
+    for (int i = 0; i < n; ++i) {
+        StreamRec* r = rec_of(s, ids[i]);
+        if (!r) return ud::host_fail(UD_ERR_NO_STREAM, "unknown streamer id");
+        if (r->last) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "audio pushed after the end of the stream");
+        if (r->mel_id < 0) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "not an audio stream");
+        for (int j = 0; j < i; ++j)
+            if (ids[j] == ids[i]) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "a stream appears twice in one push");
+        if (n_samples[i] < 0) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "negative sample count");
+        mids[i] = r->mel_id;
+        fin[i] = last && last[i] ? 1 : 0;
+        cap = std::max(cap, n_samples[i] / 160 + 4);   // frames one push can complete (hop 160)
+    }
+    const size_t bins = static_cast<size_t>(s->cfg.mel_bins);
+    std::vector<float> out(static_cast<size_t>(n) * cap * bins);
+    ud_status st = ud_mel_push_batch(s->mel, n, mids.data(), samples, n_samples, fin.data(), out.data(), cap,
+                                     frames.data());
+    if (st != UD_OK) return st;
+    for (int i = 0; i < n; ++i) {
+        StreamRec& r = s->recs[ids[i]];
+        const float* f = out.data() + static_cast<size_t>(i) * cap * bins;
+        r.own.insert(r.own.end(), f, f + static_cast<size_t>(frames[i]) * bins);
+        r.avail += frames[i];
+        if (fin[i]) r.last = true;
+    }
+    return UD_OK;
+}
+
 ud_status ud_streamer_push(ud_streamer* s, ud_streamer_id id, int n_rows, int last) {
     StreamRec* r = rec_of(s, id);
     if (!r) return ud::host_fail(UD_ERR_NO_STREAM, "unknown streamer id");
+    if (r->mel_id >= 0) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "an audio stream takes ud_streamer_push_audio");
     if (r->last) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "rows pushed after the end of the stream");
     if (n_rows < 0 || r->avail + n_rows > r->capacity)
         return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "pushed rows exceed the stream's buffer");
@@ -156,31 +235,50 @@ ud_status ud_streamer_push(ud_streamer* s, ud_streamer_id id, int n_rows, int la
 ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
     if (!s) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL streamer");
     int n = 0, done = 0;
-    const int mel_bins = s->cfg.mel_bins;
+    const size_t bins = static_cast<size_t>(s->cfg.mel_bins);
+    const size_t pad_rows = kPreEncodeCache + 8;
     s->just_finished.clear();
+    auto finish = [&](StreamRec& r, int id) {   // frees the engine slot and the frontend stream
+        ud_stream_close(s->e, r.slot);
+        if (r.mel_id >= 0) {
+            ud_mel_stream_close(s->mel, r.mel_id);
+            r.mel_id = -2;   // an audio stream whose frontend stream is closed
+            std::vector<float>().swap(r.own);
+        }
+        r.finished = true;
+        s->just_finished.push_back(id);
+        ++done;
+    };
     for (int id = 0; id < static_cast<int>(s->recs.size()) && n < s->cfg.max_batch; ++id) {
         StreamRec& r = s->recs[id];
         if (!r.used || r.finished) continue;
-        int start, rows, keep, nxt;
-        const int c = ud_chunk_next(s->lookahead, r.idx, r.avail, r.last ? 1 : 0, &start, &rows, &keep, &nxt);
+        int start, rows, valid, keep, nxt;
+        const int c = ud_chunk_next(s->lookahead, r.idx, r.avail, r.last ? 1 : 0, s->end_padding, &start, &rows,
+                                    &valid, &keep, &nxt);
         if (c == 0) continue;
-        if (c < 0) {   // what remains is too short to encode: the stream ends here
-            ud_stream_close(s->e, r.slot);
-            r.finished = true;
-            s->just_finished.push_back(id);
-            ++done;
+        if (c < 0) {   // nothing left, or a tail too short to encode without end padding: the stream ends here
+            finish(r, id);
             continue;
         }
+        const float* src = r.mel_id != -1 ? r.own.data() + static_cast<size_t>(start - r.own_start) * bins
+                                          : r.mel + static_cast<size_t>(start) * bins;
+        if (rows > valid) {   // a padded final tail: the valid rows, then zero rows
+            float* dst = s->pad.data() + static_cast<size_t>(n) * pad_rows * bins;
+            std::memcpy(dst, src, sizeof(float) * valid * bins);
+            std::memset(dst + static_cast<size_t>(valid) * bins, 0, sizeof(float) * (rows - valid) * bins);
+            src = dst;
+        }
         s->ids[n] = r.slot;
-        s->mels[n] = r.mel + static_cast<size_t>(start) * mel_bins;
+        s->mels[n] = src;
         s->rows[n] = rows;
+        s->valid[n] = valid;
         s->keep[n] = keep;
         s->who[n] = id;
         s->next[n] = nxt;
         ++n;
     }
     if (n > 0) {
-        ud_status st = ud_step_batch(s->e, n, s->ids.data(), s->mels.data(), s->rows.data(), s->rows.data(),
+        ud_status st = ud_step_batch(s->e, n, s->ids.data(), s->mels.data(), s->rows.data(), s->valid.data(),
                                      s->keep.data(), s->decode ? nullptr : s->proj.data(), s->frames.data(),
                                      s->decode ? s->toks.data() : nullptr, s->decode ? s->ntok.data() : nullptr);
         if (st != UD_OK) return st;
@@ -192,11 +290,15 @@ ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
                 r.tokens.insert(r.tokens.end(), t, t + s->ntok[i]);
             }
             r.idx = s->next[i];
-            if (s->keep[i]) {   // the final chunk: free the engine slot
-                ud_stream_close(s->e, r.slot);
-                r.finished = true;
-                s->just_finished.push_back(s->who[i]);
-                ++done;
+            if (s->keep[i]) {   // the final chunk
+                finish(r, s->who[i]);
+            } else if (r.mel_id >= 0) {   // keep only the pre-encode cache window of an audio stream
+                const int keep_from = r.idx - kPreEncodeCache;
+                if (keep_from > r.own_start) {
+                    const size_t drop = std::min(r.own.size(), static_cast<size_t>(keep_from - r.own_start) * bins);
+                    r.own.erase(r.own.begin(), r.own.begin() + static_cast<std::ptrdiff_t>(drop));
+                    r.own_start = keep_from;
+                }
             }
         }
     }
@@ -227,6 +329,7 @@ ud_status ud_streamer_release(ud_streamer* s, ud_streamer_id id) {
     StreamRec* r = rec_of(s, id);
     if (!r) return ud::host_fail(UD_ERR_NO_STREAM, "unknown streamer id");
     if (!r->finished && r->slot >= 0) ud_stream_close(s->e, r->slot);
+    if (r->mel_id >= 0) ud_mel_stream_close(s->mel, r->mel_id);
     *r = StreamRec();
     s->free_ids.push_back(id);
     return UD_OK;

@@ -41,7 +41,7 @@ ABI_SYMBOLS = [
     "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
     "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
-    "ud_streamer_release", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
+    "ud_streamer_release", "ud_streamer_set_end_padding", "ud_streamer_open_audio", "ud_streamer_push_audio", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
     "ud_mel_stream_open", "ud_mel_stream_close", "ud_mel_push_batch", "ud_detok_create", "ud_detok_create_file",
     "ud_detok_destroy", "ud_detok_size", "ud_detok_decode",
 ]
@@ -107,7 +107,7 @@ def lib() -> C.CDLL:
             "ud_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
             "ud_status_string": (C.c_char_p, [I]),
             "ud_get_config": (I, [eng, P(Config)]),
-            "ud_chunk_next": (I, [I, I, I, I, P(I), P(I), P(I), P(I)]),
+            "ud_chunk_next": (I, [I, I, I, I, I, P(I), P(I), P(I), P(I), P(I)]),
             "ud_streamer_create": (I, [eng, I, I, P(VP)]),
             "ud_streamer_destroy": (I, [VP]),
             "ud_streamer_open": (I, [VP, P(F), I, P(C.c_int32)]),
@@ -116,6 +116,9 @@ def lib() -> C.CDLL:
             "ud_streamer_finished": (I, [VP, P(C.c_int32), I, P(I)]),
             "ud_streamer_tokens": (I, [VP, C.c_int32, P(C.c_int32), I, P(I), P(I)]),
             "ud_streamer_release": (I, [VP, C.c_int32]),
+            "ud_streamer_set_end_padding": (I, [VP, I]),
+            "ud_streamer_open_audio": (I, [VP, VP, P(C.c_int32)]),
+            "ud_streamer_push_audio": (I, [VP, I, P(C.c_int32), P(P(F)), P(I), P(I)]),
             "ud_mel_create": (I, [eng, P(F), I, P(F), I, P(VP)]),
             "ud_mel_destroy": (I, [VP]),
             "ud_mel_features": (I, [VP, P(F), I, P(F), I, P(I)]),
@@ -379,12 +382,13 @@ class Engine:
                                   int(out_bf16)))
 
 
-def chunk_next(lookahead: int, idx: int, avail: int, last: bool):
-    """ud_chunk_next: (1, start, n_rows, keep_all, next_idx) for a ready chunk, (0, ...) to wait, (-1, ...) when the
-    stream has ended."""
-    st, rows, keep, nxt = C.c_int(), C.c_int(), C.c_int(), C.c_int()
-    r = lib().ud_chunk_next(lookahead, idx, avail, int(last), C.byref(st), C.byref(rows), C.byref(keep), C.byref(nxt))
-    return r, st.value, rows.value, bool(keep.value), nxt.value
+def chunk_next(lookahead: int, idx: int, avail: int, last: bool, end_padding: bool = True):
+    """ud_chunk_next: (1, start, n_rows, valid_rows, keep_all, next_idx) for a ready chunk, (0, ...) to wait,
+    (-1, ...) when the stream has ended."""
+    st, rows, valid, keep, nxt = C.c_int(), C.c_int(), C.c_int(), C.c_int(), C.c_int()
+    r = lib().ud_chunk_next(lookahead, idx, avail, int(last), int(end_padding), C.byref(st), C.byref(rows),
+                            C.byref(valid), C.byref(keep), C.byref(nxt))
+    return r, st.value, rows.value, valid.value, bool(keep.value), nxt.value
 
 
 class Streamer:
@@ -408,6 +412,24 @@ class Streamer:
 
     def push(self, sid: int, n_rows: int, last: bool = False):
         check(lib().ud_streamer_push(self.h, sid, n_rows, int(last)))
+
+    def set_end_padding(self, on: bool):
+        check(lib().ud_streamer_set_end_padding(self.h, int(on)))
+
+    def open_audio(self, frontend: "MelFrontend") -> int:
+        """An audio stream whose mel comes from `frontend` (NemotronStreamer.push(samples:))."""
+        sid = C.c_int32()
+        check(lib().ud_streamer_open_audio(self.h, frontend.h, C.byref(sid)))
+        return sid.value
+
+    def push_audio(self, ids, chunks, last=None):
+        n = len(ids)
+        arrs = [np.ascontiguousarray(np.asarray(c, np.float32)) for c in chunks]
+        ptrs = (C.POINTER(C.c_float) * n)(*[_ptr(a) for a in arrs])
+        ids_a, ns = np.ascontiguousarray(np.asarray(ids, np.int32)), _i32([a.shape[0] for a in arrs])
+        fin = _i32([int(bool(f)) for f in last]) if last is not None else None
+        check(lib().ud_streamer_push_audio(self.h, n, _ptr(ids_a, C.c_int32), ptrs, _ptr(ns, C.c_int),
+                                           _ptr(fin, C.c_int) if fin is not None else None))
 
     def step(self) -> tuple[int, int]:
         """One batched step: (streams advanced, streams finished)."""
