@@ -67,8 +67,8 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
             if (t < vt) {
                 const T* pr = pw + static_cast<size_t>(row_off + t) * ld_pw + c;
                 const float2 val = Pair<T>::ld(pr), gate = Pair<T>::ld(pr + D);
-                g0 = val.x / (1.f + expf(-gate.x));
-                g1 = val.y / (1.f + expf(-gate.y));
+                g0 = __fdividef(val.x, 1.f + __expf(-gate.x));   // value * sigmoid(gate)
+                g1 = __fdividef(val.y, 1.f + __expf(-gate.y));
             }
             *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(g0, g1);
             if (t >= T_ - R) Pair<T>::st(ring + ((head + t) % R) * D + c, g0, g1);
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
             const float2 gg = *reinterpret_cast<const float2*>(g + c), bb = *reinterpret_cast<const float2*>(beta + c);
             const float z0 = (v.x - mean) * rstd * gg.x + bb.x;
             const float z1 = (v.y - mean) * rstd * gg.y + bb.y;
-            Pair<T>::st(orow + c, z0 / (1.f + expf(-z0)), z1 / (1.f + expf(-z1)));
+            Pair<T>::st(orow + c, silu(z0), silu(z1));
         }
     }
 }
