@@ -338,6 +338,24 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
         VP[r] = vs;
     }
     __syncthreads();
+    // ---- append this chunk's K/V rows at frames head + t. Those pool rows are not read by this launch (the
+    //      window is frames head - cacheLen .. head - 1, and the 8 page slots hold 128 frames), so the copy is
+    //      issued first and overlaps the staging below.
+    bf16* kw = reinterpret_cast<bf16*>(cg.kpool);
+    bf16* vw = reinterpret_cast<bf16*>(cg.vpool);
+    for (int idx = tid; idx < T_ * 16; idx += kAttnThreads) {
+        const int t = idx >> 4, c = (idx & 15) * 8;
+        const int f = head + t;
+        const int page = me.pages[(f / PF) % kPageSlots];
+        if (page < 0 || page >= cg.n_pages) {
+            report_error(err, DEV_BAD_PAGE);
+            continue;
+        }
+        const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
+        const bf16* src = qkv + static_cast<size_t>(row_off + t) * ld_qkv + hoff + c;
+        *reinterpret_cast<uint4*>(kw + off) = *reinterpret_cast<const uint4*>(src + D);
+        *reinterpret_cast<uint4*>(vw + off) = *reinterpret_cast<const uint4*>(src + 2 * D);
+    }
 
     // ---- stage K and P (group 0) and V (group 1) with cp.async; zero the padding rows.
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
@@ -480,22 +498,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
                 __floats2bfloat162_rn(acc[2], acc[3]);
     }
 
-    // ---- append this chunk's K/V rows at frames head + t
-    bf16* kw = reinterpret_cast<bf16*>(cg.kpool);
-    bf16* vw = reinterpret_cast<bf16*>(cg.vpool);
-    for (int idx = tid; idx < T_ * 16; idx += kAttnThreads) {
-        const int t = idx >> 4, c = (idx & 15) * 8;
-        const int f = head + t;
-        const int page = me.pages[(f / PF) % kPageSlots];
-        if (page < 0 || page >= cg.n_pages) {
-            report_error(err, DEV_BAD_PAGE);
-            continue;
-        }
-        const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
-        const bf16* src = qkv + static_cast<size_t>(row_off + t) * ld_qkv + hoff + c;
-        *reinterpret_cast<uint4*>(kw + off) = *reinterpret_cast<const uint4*>(src + D);
-        *reinterpret_cast<uint4*>(vw + off) = *reinterpret_cast<const uint4*>(src + 2 * D);
-    }
 }
 
 }  // namespace tc
