@@ -150,6 +150,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // The weights do not depend on the previous kernel: the producer stages the W halves of the first tile's
+    // first stages (all free at this point) before the dependency wait, so only the A loads follow it. Those
+    // stages' barriers get the W bytes now (no arrival) and the A bytes with the producer's arrival below.
+    int w_early = 0;
+    if (warp == 0 && lane == 0 && pair < num_tiles) {
+        const int nb = pair / num_m;
+        const int c0 = nb * tn, w = min(tn, N - c0);
+        w_early = min(C::STAGES, num_kb);
+        for (int kb = 0; kb < w_early; ++kb) {
+            if (rank == 0) mbar_expect_tx(&full[kb], 2 * C::B_BYTES);
+            tma_load_2d_pair(sB + kb * C::B_BYTES, &mapW, peer_addr(smem_u32(&full[kb]), 0), kb * BK,
+                             c0 + static_cast<int>(rank) * (w / 2));
+        }
+    }
     pdl_wait();  // the prologue above overlaps the previous kernel; its outputs are read only from here on
 
     if (warp == 0) {
@@ -162,9 +176,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, err, DEV_TIMEOUT_EMPTY, abort_v)) goto producer_done;
                     const uint32_t leader_full = peer_addr(smem_u32(&full[stage]), 0);
-                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+                    const bool w_loaded = tile == pair && kb < w_early;
+                    if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (w_loaded ? C::A_BYTES : C::STAGE_BYTES));
                     tma_load_2d_pair(sA + stage * C::A_BYTES, &mapA, leader_full, kb * BK, mb * BM2 + rank * 128);
-                    tma_load_2d_pair(sB + stage * C::B_BYTES, &mapW, leader_full, kb * BK, c0 + static_cast<int>(rank) * (w / 2));
+                    if (!w_loaded)
+                        tma_load_2d_pair(sB + stage * C::B_BYTES, &mapW, leader_full, kb * BK,
+                                         c0 + static_cast<int>(rank) * (w / 2));
                     if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
                 }
             }
