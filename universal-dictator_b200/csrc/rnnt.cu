@@ -18,31 +18,42 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+constexpr int kSpec = 16;   // frames whose joints one pass of the per-stream kernel evaluates together
 
-// out[r] = bias[r] + W1[r] . x1 (+ W2[r] . x2), rows split across warps, float4 loads along K.
+// out[r] = bias[r] + W1[r] . x1 (+ W2[r] . x2), rows split across warps, float4 loads along K. Each warp takes
+// four rows at a time (four independent accumulators), so four rows' weight loads are in flight together.
 __device__ void matvec(const float* __restrict__ W1, const float* __restrict__ x1, const float* __restrict__ W2,
                        const float* __restrict__ x2, const float* __restrict__ bias, float* __restrict__ out,
                        int rows, int K) {
+    constexpr int RB = 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int k4 = K / 4;
-    for (int r = warp; r < rows; r += kWarps) {
-        const float4* w1 = reinterpret_cast<const float4*>(W1 + static_cast<size_t>(r) * K);
-        const float4* xa = reinterpret_cast<const float4*>(x1);
-        float acc = 0.f;
+    const float4* xa = reinterpret_cast<const float4*>(x1);
+    const float4* xb = reinterpret_cast<const float4*>(x2);
+    for (int r0 = warp * RB; r0 < rows; r0 += kWarps * RB) {
+        float acc[RB];
+#pragma unroll
+        for (int u = 0; u < RB; ++u) acc[u] = 0.f;
         for (int i = lane; i < k4; i += 32) {
-            const float4 w = w1[i], x = xa[i];
-            acc = fmaf(w.x, x.x, fmaf(w.y, x.y, fmaf(w.z, x.z, fmaf(w.w, x.w, acc))));
-        }
-        if (W2) {
-            const float4* w2 = reinterpret_cast<const float4*>(W2 + static_cast<size_t>(r) * K);
-            const float4* xb = reinterpret_cast<const float4*>(x2);
-            for (int i = lane; i < k4; i += 32) {
-                const float4 w = w2[i], x = xb[i];
-                acc = fmaf(w.x, x.x, fmaf(w.y, x.y, fmaf(w.z, x.z, fmaf(w.w, x.w, acc))));
+            const float4 x = xa[i];
+            const float4 y = W2 ? xb[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < RB; ++u) {
+                if (r0 + u < rows) {
+                    const float4 w = reinterpret_cast<const float4*>(W1 + static_cast<size_t>(r0 + u) * K)[i];
+                    acc[u] = fmaf(w.x, x.x, fmaf(w.y, x.y, fmaf(w.z, x.z, fmaf(w.w, x.w, acc[u]))));
+                    if (W2) {
+                        const float4 v = reinterpret_cast<const float4*>(W2 + static_cast<size_t>(r0 + u) * K)[i];
+                        acc[u] = fmaf(v.x, y.x, fmaf(v.y, y.y, fmaf(v.z, y.z, fmaf(v.w, y.w, acc[u]))));
+                    }
+                }
             }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) out[r] = acc + (bias ? bias[r] : 0.f);
+#pragma unroll
+        for (int u = 0; u < RB; ++u) {
+            const float v = warp_sum(acc[u]);
+            if (lane == 0 && r0 + u < rows) out[r0 + u] = v + (bias ? bias[r0 + u] : 0.f);
+        }
     }
 }
 
@@ -59,16 +70,17 @@ __global__ void __launch_bounds__(kThreads) rnnt_kernel(const RnntWeights w, con
     const int Hp = w.Hp, J = w.J, V = w.V, NLp = w.layers;
     float* f = sm;                  // [J]
     float* g = f + J;               // [J]  pending prediction output
-    float* hs = g + J;              // [J]  relu(f + g)
-    float* x = hs + J;              // [Hp] layer input
+    float* x = g + J;               // [Hp] layer input
     float* hc = x + Hp;             // [NLp][Hp] committed h
     float* cc = hc + NLp * Hp;      // [NLp][Hp] committed c
     float* ph = cc + NLp * Hp;      // [NLp][Hp] pending h
     float* pc = ph + NLp * Hp;      // [NLp][Hp] pending c
     float* gates = pc + NLp * Hp;   // [4 Hp]
-    __shared__ float red_v[kWarps];
-    __shared__ int red_i[kWarps];
-    __shared__ int s_best, s_pend, s_last;
+    float* hsm = gates + 4 * Hp;    // [kSpec][J] relu(f_t + g) of the frames of one joint pass
+    __shared__ float red_v[kWarps][kSpec];
+    __shared__ int red_i[kWarps][kSpec];
+    __shared__ int s_bestf[kSpec];
+    __shared__ int s_pend, s_last;
 
     const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const BatchEntry& me = meta[b];
@@ -87,61 +99,103 @@ __global__ void __launch_bounds__(kThreads) rnnt_kernel(const RnntWeights w, con
     }
     __syncthreads();
 
-    int ntok = 0;
-    for (int t = 0; t < me.keep; ++t) {
-        for (int i = tid; i < J; i += kThreads) f[i] = proj[static_cast<size_t>(me.row_off + t) * ld_proj + i];
+    // The prediction for the last token (LSTM + joint.pred) into g, when it is not pending.
+    auto predict = [&]() {
+        const int tok = s_last;
+        for (int i = tid; i < Hp; i += kThreads) x[i] = tok != blank ? w.embed[static_cast<size_t>(tok) * Hp + i] : 0.f;
         __syncthreads();
-        for (int emitted = 0; emitted < w.max_symbols;) {
-            if (!s_pend) {
-                const int tok = s_last;
-                for (int i = tid; i < Hp; i += kThreads)
-                    x[i] = tok != blank ? w.embed[static_cast<size_t>(tok) * Hp + i] : 0.f;
-                __syncthreads();
-                for (int l = 0; l < NLp; ++l) {
-                    const float* in = l == 0 ? x : ph + (l - 1) * Hp;
-                    matvec(w.w_ih[l], in, w.w_hh[l], hc + l * Hp, w.bias[l], gates, 4 * Hp, Hp);
-                    __syncthreads();
-                    for (int k = tid; k < Hp; k += kThreads) {
-                        const float ig = sigm(gates[k]), fg = sigm(gates[Hp + k]);
-                        const float gg = tanhf(gates[2 * Hp + k]), og = sigm(gates[3 * Hp + k]);
-                        const float cn = fg * cc[l * Hp + k] + ig * gg;
-                        pc[l * Hp + k] = cn;
-                        ph[l * Hp + k] = og * tanhf(cn);
+        for (int l = 0; l < NLp; ++l) {
+            const float* in = l == 0 ? x : ph + (l - 1) * Hp;
+            matvec(w.w_ih[l], in, w.w_hh[l], hc + l * Hp, w.bias[l], gates, 4 * Hp, Hp);
+            __syncthreads();
+            for (int k = tid; k < Hp; k += kThreads) {
+                const float ig = sigm(gates[k]), fg = sigm(gates[Hp + k]);
+                const float gg = tanhf(gates[2 * Hp + k]), og = sigm(gates[3 * Hp + k]);
+                const float cn = fg * cc[l * Hp + k] + ig * gg;
+                pc[l * Hp + k] = cn;
+                ph[l * Hp + k] = og * tanhf(cn);
+            }
+            __syncthreads();
+        }
+        matvec(w.pred_w, ph + (NLp - 1) * Hp, nullptr, nullptr, w.pred_b, g, J, Hp);
+        if (tid == 0) s_pend = 1;
+        __syncthreads();
+    };
+    // Joint logits of F frames (rows of hsm) and each frame's first-maximum argmax into s_bestf[0, F).
+    auto joint = [&](int F) {
+        float bv[kSpec];
+        int bi[kSpec];
+#pragma unroll
+        for (int ff = 0; ff < kSpec; ++ff) { bv[ff] = -INFINITY; bi[ff] = 0x7fffffff; }
+        for (int r = warp; r < V; r += kWarps) {
+            const float4* wr = reinterpret_cast<const float4*>(w.out_w + static_cast<size_t>(r) * J);
+            float acc[kSpec];
+#pragma unroll
+            for (int ff = 0; ff < kSpec; ++ff) acc[ff] = 0.f;
+            for (int i = lane; i < J / 4; i += 32) {
+                const float4 a = wr[i];
+#pragma unroll
+                for (int ff = 0; ff < kSpec; ++ff) {
+                    if (ff < F) {
+                        const float4 h4 = reinterpret_cast<const float4*>(hsm + ff * J)[i];
+                        acc[ff] = fmaf(a.x, h4.x, fmaf(a.y, h4.y, fmaf(a.z, h4.z, fmaf(a.w, h4.w, acc[ff]))));
                     }
-                    __syncthreads();
                 }
-                matvec(w.pred_w, ph + (NLp - 1) * Hp, nullptr, nullptr, w.pred_b, g, J, Hp);
-                if (tid == 0) s_pend = 1;
-                __syncthreads();
             }
-            for (int i = tid; i < J; i += kThreads) hs[i] = fmaxf(f[i] + g[i], 0.f);
-            __syncthreads();
-            // Joint logits and first-maximum argmax.
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-            for (int r = warp; r < V; r += kWarps) {
-                const float4* wr = reinterpret_cast<const float4*>(w.out_w + static_cast<size_t>(r) * J);
-                const float4* hv = reinterpret_cast<const float4*>(hs);
-                float acc = 0.f;
-                for (int i = lane; i < J / 4; i += 32) {
-                    const float4 a = wr[i], h4 = hv[i];
-                    acc = fmaf(a.x, h4.x, fmaf(a.y, h4.y, fmaf(a.z, h4.z, fmaf(a.w, h4.w, acc))));
+            const float ob = w.out_b[r];
+#pragma unroll
+            for (int ff = 0; ff < kSpec; ++ff) {
+                if (ff < F) {
+                    const float v = warp_sum(acc[ff]) + ob;
+                    if (v > bv[ff] || (v == bv[ff] && r < bi[ff])) { bv[ff] = v; bi[ff] = r; }
                 }
-                acc = warp_sum(acc) + w.out_b[r];
-                if (acc > bv || (acc == bv && r < bi)) { bv = acc; bi = r; }
             }
-            if (lane == 0) { red_v[warp] = bv; red_i[warp] = bi; }
-            __syncthreads();
-            if (tid == 0) {
-                float v0 = red_v[0];
-                int i0 = red_i[0];
-                for (int k = 1; k < kWarps; ++k)
-                    if (red_v[k] > v0 || (red_v[k] == v0 && red_i[k] < i0)) { v0 = red_v[k]; i0 = red_i[k]; }
-                s_best = i0;
-            }
-            __syncthreads();
-            const int best = s_best;
-            if (best == blank) break;
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int ff = 0; ff < kSpec; ++ff)
+                if (ff < F) { red_v[warp][ff] = bv[ff]; red_i[warp][ff] = bi[ff]; }
+        __syncthreads();
+        if (tid < F) {
+            float v0 = red_v[0][tid];
+            int i0 = red_i[0][tid];
+            for (int k = 1; k < kWarps; ++k)
+                if (red_v[k][tid] > v0 || (red_v[k][tid] == v0 && red_i[k][tid] < i0)) { v0 = red_v[k][tid]; i0 = red_i[k][tid]; }
+            s_bestf[tid] = i0;
+        }
+        __syncthreads();
+    };
+
+    // While no symbol is emitted the prediction g does not change, so the joints of the next frames are
+    // computed in one pass over the joint weights (the weight rows are read once for up to kSpec frames; the
+    // pass length adapts to the gaps between emissions, so frames evaluated past an emission stay few). The
+    // first frame whose maximum is not blank continues the reference's loop exactly: it emits that symbol,
+    // then alternates prediction and joint until blank or max_symbols; later frames of the pass are discarded.
+    int ntok = 0;
+    int t = 0;
+    int spec = kSpec;   // frames per pass: doubled after a pass of blanks, the last gap to an emission after one
+    while (t < me.keep) {
+        if (!s_pend) predict();
+        const int F = min(spec, me.keep - t);
+        for (int i = tid; i < F * J; i += kThreads) {
+            const int ff = i / J, j = i - ff * J;
+            hsm[ff * J + j] = fmaxf(proj[static_cast<size_t>(me.row_off + t + ff) * ld_proj + j] + g[j], 0.f);
+        }
+        __syncthreads();
+        joint(F);
+        int first = F;
+        for (int ff = 0; ff < F; ++ff)
+            if (s_bestf[ff] != blank) { first = ff; break; }
+        t += first;   // frames before it end with blank
+        if (first == F) {
+            spec = min(kSpec, 2 * spec);
+            continue;
+        }
+        spec = max(2, first + 1);
+        int best = s_bestf[first];
+        __syncthreads();   // every thread has read s_bestf
+        for (int i = tid; i < J; i += kThreads) f[i] = proj[static_cast<size_t>(me.row_off + t) * ld_proj + i];
+        for (int emitted = 0;;) {
             if (tid == 0) {
                 tokens[static_cast<size_t>(b) * tok_stride + ntok] = best;
                 s_last = best;
@@ -151,7 +205,16 @@ __global__ void __launch_bounds__(kThreads) rnnt_kernel(const RnntWeights w, con
             ++ntok;
             ++emitted;
             __syncthreads();
+            if (emitted >= w.max_symbols) break;
+            predict();
+            for (int i = tid; i < J; i += kThreads) hsm[i] = fmaxf(f[i] + g[i], 0.f);
+            __syncthreads();
+            joint(1);
+            best = s_bestf[0];
+            __syncthreads();   // every thread has read s_bestf before the next joint rewrites it
+            if (best == blank) break;
         }
+        ++t;
     }
     for (int i = tid; i < NLp * Hp; i += kThreads) {
         st.h[static_cast<size_t>(slot) * NLp * Hp + i] = hc[i];
@@ -518,7 +581,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) rnnt_lockstep_kernel(
 }  // namespace
 
 size_t rnnt_smem_bytes(const RnntWeights& w) {
-    return sizeof(float) * (3 * w.J + w.Hp + 4 * w.layers * w.Hp + 4 * w.Hp);
+    return sizeof(float) * (2 * w.J + w.Hp + 4 * w.layers * w.Hp + 4 * w.Hp + kSpec * w.J);
 }
 
 void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, int ld_proj, const BatchEntry* meta,
