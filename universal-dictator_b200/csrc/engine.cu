@@ -434,23 +434,6 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         g.out_scale = scale;
         return g;
     };
-    // LayerNorm of x feeding one GEMM: fused into the few-row GEMV as its prologue, else normalised into h first.
-    const bool ln_fused = M <= 16 && gemv_ln_fits(M, D, e->bf);
-    auto ln_gemm = [&](const float* g, const float* b, const WeightMat& W, const GemmEpilogue& epi) -> ud_status {
-        if (!ln_fused) {
-            ln(g, b);
-            return gemm(e, e->h, D, M, W, epi);
-        }
-        Launch L_(e, UD_KIND_GEMM_SIMT);
-        LnPrologue p;
-        p.x = e->x;
-        p.ldx = D;
-        p.g = g;
-        p.b = b;
-        if (e->bf) gemm_simt<bf16, bf16>(nullptr, D, static_cast<const bf16*>(W.p), M, W.N, W.K, epi, st, &p);
-        else gemm_simt<float, float>(nullptr, D, static_cast<const float*>(W.p), M, W.N, W.K, epi, st, &p);
-        return UD_OK;
-    };
     if (NL > 0) ln(e->layers[0].ln_ff1_g, e->layers[0].ln_ff1_b);
     for (int l = 0; l < NL; ++l) {
         LayerW& w = e->layers[l];
@@ -458,7 +441,8 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         gs.act = ACT_SILU;
         UD_TRY(gemm(e, e->h, D, M, w.ff1_w1, gs));
         UD_TRY(gemm(e, e->hid, e->F, M, w.ff1_w2, resid(0.5f)));
-        UD_TRY(ln_gemm(w.ln_att_g, w.ln_att_b, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
+        ln(w.ln_att_g, w.ln_att_b);
+        UD_TRY(gemm(e, e->h, D, M, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
         {
         Launch L_(e, UD_KIND_ATTENTION);
         if (e->bf)
@@ -469,7 +453,8 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
                                     l, (float*)e->att, D, e->H, e->err_d, st);
         }
         UD_TRY(gemm(e, e->att, D, M, w.wo, resid(1.0f)));
-        UD_TRY(ln_gemm(w.ln_conv_g, w.ln_conv_b, w.pw1, epi_out(e->pw, 2 * D, true, e)));
+        ln(w.ln_conv_g, w.ln_conv_b);
+        UD_TRY(gemm(e, e->h, D, M, w.pw1, epi_out(e->pw, 2 * D, true, e)));
         {
         Launch L_(e, UD_KIND_CONV);
         if (e->bf)
@@ -480,7 +465,8 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
                                (float*)e->y, D, st);
         }
         UD_TRY(gemm(e, e->y, D, M, w.pw2, resid(1.0f)));
-        UD_TRY(ln_gemm(w.ln_ff2_g, w.ln_ff2_b, w.ff2_w1, gs));
+        ln(w.ln_ff2_g, w.ln_ff2_b);
+        UD_TRY(gemm(e, e->h, D, M, w.ff2_w1, gs));
         UD_TRY(gemm(e, e->hid, e->F, M, w.ff2_w2, resid(0.5f)));
         if (l + 1 < NL) {
             LayerW& nx = e->layers[l + 1];

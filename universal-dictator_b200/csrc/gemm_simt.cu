@@ -1,11 +1,10 @@
 // SIMT GEMMs: the few-row GEMV used at batch 1 (the reference's gemv_nt role, 11_gemv.metal:45-128, M <= 8
 // there) and a tiled FFMA GEMM for the fp32 engine at larger M. C = epilogue(A . W^T), W [N, K] row-major.
 //
-// The GEMV is bound by streaming W from HBM once (A is a few rows that stay in L1). One warp owns one output
-// column; each lane issues all of its 16-byte weight loads for a block of U chunks at once, and the first
-// block is issued before the grid-dependency wait, since W does not depend on the previous kernel. With the
-// LayerNorm prologue A is not read from memory: each CTA normalises the M fp32 rows of x into shared memory
-// (the arithmetic of ln_kernel, so the values equal the separate LayerNorm's) and the GEMV reads them there.
+// The GEMV is bound by streaming W from HBM once (A is a few rows). One warp owns one output column; each lane
+// issues all of its 16-byte weight loads for a block of U chunks at once, and the first block is issued before the
+// grid-dependency wait, since W does not depend on the previous kernel, so the weight fetch overlaps the kernel
+// before. A is staged once per CTA in shared memory.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -69,60 +68,17 @@ __global__ void __launch_bounds__(256) gemv_rows_kernel(const T* __restrict__ A,
 }
 
 constexpr int kGemvWarps = 8;
-constexpr int kGemvLnSmem = 64 * 1024;   // largest LayerNorm staging (M x K x sizeof(T)) the prologue takes
+constexpr int kGemvStageSmem = 64 * 1024;   // largest A staging (M x K x sizeof(T)) in shared memory
 
-// One row of the LayerNorm prologue: the statistics and the normalised row exactly as ln_kernel computes them
-// (lane i holds float4 chunks i, i+32, ...; the row stays in registers; two passes for mean and variance;
-// eps 1e-5). K <= 1024, K % 128 == 0.
-template <typename T>
-__device__ __forceinline__ void ln_row_to_smem(const float* __restrict__ xr, const float* __restrict__ g,
-                                               const float* __restrict__ b, int K, int lane, T* __restrict__ out) {
-    constexpr int NV = 8;
-    float v[NV][4];
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        const int c = (i * 32 + lane) * 4;
-        const float4 t = c < K ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
-    }
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) s += v[i][0] + v[i][1] + v[i][2] + v[i][3];
-    const float mean = warp_sum(s) / static_cast<float>(K);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i)
-        if ((i * 32 + lane) * 4 < K)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float d = v[i][j] - mean;
-                q += d * d;
-            }
-    const float var = warp_sum(q) / static_cast<float>(K);
-    const float rstd = rsqrtf(var + 1e-5f);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-        const int c = (i * 32 + lane) * 4;
-        if (c < K) {
-            const float4 g4 = *reinterpret_cast<const float4*>(g + c), b4 = *reinterpret_cast<const float4*>(b + c);
-            out[c + 0] = from_f<T>((v[i][0] - mean) * rstd * g4.x + b4.x);
-            out[c + 1] = from_f<T>((v[i][1] - mean) * rstd * g4.y + b4.y);
-            out[c + 2] = from_f<T>((v[i][2] - mean) * rstd * g4.z + b4.z);
-            out[c + 3] = from_f<T>((v[i][3] - mean) * rstd * g4.w + b4.w);
-        }
-    }
-}
-
-// Where the GEMV's A rows come from: global memory (read by every warp), staged once per CTA into shared memory
-// by 16-byte loads of all threads (one memory round trip instead of one per chunk), or computed into shared
-// memory by the LayerNorm prologue.
-enum GemvSrc { kSrcGlobal = 0, kSrcStaged = 1, kSrcLn = 2 };
+// Where the GEMV's A rows come from: global memory (read by every warp), or staged once per CTA into shared
+// memory by 16-byte loads of all threads (one memory round trip instead of one per chunk).
+enum GemvSrc { kSrcGlobal = 0, kSrcStaged = 1 };
 // Few-row GEMV, M <= MR rows. K % VW == 0 and 16-byte aligned A, W and lda (checked by the host).
 // U 16-byte weight chunks per lane are in flight at once (4 for K <= 1024 bf16, 16 above, where the extra
 // registers are worth it).
 template <typename T, int MR, int SRC, int U>
 __global__ void __launch_bounds__(256) gemv_kernel(const T* __restrict__ A, int lda, const T* __restrict__ W, int M,
-                                                   int N, int K, const GemmEpilogue epi, const LnPrologue ln) {
+                                                   int N, int K, const GemmEpilogue epi) {
     constexpr int VW = Vec16<T>::N;
     extern __shared__ __align__(16) unsigned char gemv_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -143,18 +99,13 @@ __global__ void __launch_bounds__(256) gemv_kernel(const T* __restrict__ A, int 
     pdl_wait();
     const T* a_rows = A;
     int a_ld = lda;
-    if constexpr (SRC != kSrcGlobal) {
+    if constexpr (SRC == kSrcStaged) {
         T* as = reinterpret_cast<T*>(gemv_smem);
-        if constexpr (SRC == kSrcLn) {
-            for (int r = warp; r < M; r += kGemvWarps)
-                ln_row_to_smem<T>(ln.x + static_cast<size_t>(r) * ln.ldx, ln.g, ln.b, K, lane, as + static_cast<size_t>(r) * K);
-        } else {
-            const int total = M * nchunks;
-            for (int i = threadIdx.x; i < total; i += 256) {
-                const int r = i / nchunks, c = i - r * nchunks;
-                reinterpret_cast<uint4*>(as)[i] =
-                    *reinterpret_cast<const uint4*>(A + static_cast<size_t>(r) * lda + static_cast<size_t>(c) * VW);
-            }
+        const int total = M * nchunks;
+        for (int i = threadIdx.x; i < total; i += 256) {
+            const int r = i / nchunks, c = i - r * nchunks;
+            reinterpret_cast<uint4*>(as)[i] =
+                *reinterpret_cast<const uint4*>(A + static_cast<size_t>(r) * lda + static_cast<size_t>(c) * VW);
         }
         __syncthreads();
         a_rows = as;
@@ -242,54 +193,37 @@ template <typename T, int MR, int U>
 void launch_gemv_u(const T* A, int lda, const T* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s) {
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(gemv_kernel<T, MR, kSrcStaged, U>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvLnSmem);
+        cudaFuncSetAttribute(gemv_kernel<T, MR, kSrcStaged, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kGemvStageSmem);
         attr = true;
     }
     const dim3 grid((N + kGemvWarps - 1) / kGemvWarps), block(256);
     const size_t smem = static_cast<size_t>(M) * K * sizeof(T);
-    if (smem <= static_cast<size_t>(kGemvLnSmem))
-        launch_pdl(gemv_kernel<T, MR, kSrcStaged, U>, grid, block, smem, s, A, lda, W, M, N, K, epi, LnPrologue{});
-    else launch_pdl(gemv_kernel<T, MR, kSrcGlobal, U>, grid, block, 0, s, A, lda, W, M, N, K, epi, LnPrologue{});
+    if (smem <= static_cast<size_t>(kGemvStageSmem))
+        launch_pdl(gemv_kernel<T, MR, kSrcStaged, U>, grid, block, smem, s, A, lda, W, M, N, K, epi);
+    else launch_pdl(gemv_kernel<T, MR, kSrcGlobal, U>, grid, block, 0, s, A, lda, W, M, N, K, epi);
 }
 
 template <typename T, int MR>
-void launch_gemv(const T* A, int lda, const T* W, int M, int N, int K, const GemmEpilogue& epi, const LnPrologue* ln,
-                 cudaStream_t s) {
-    if (ln) {
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(gemv_kernel<T, MR, kSrcLn, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvLnSmem);
-            attr = true;
-        }
-        const size_t smem = static_cast<size_t>(M) * K * sizeof(T);
-        launch_pdl(gemv_kernel<T, MR, kSrcLn, 4>, dim3((N + kGemvWarps - 1) / kGemvWarps), dim3(256), smem, s, A, lda,
-                   W, M, N, K, epi, *ln);
-    } else if (K / Vec16<T>::N <= 4 * 32) {
-        launch_gemv_u<T, MR, 4>(A, lda, W, M, N, K, epi, s);
-    } else {
-        launch_gemv_u<T, MR, 16>(A, lda, W, M, N, K, epi, s);
-    }
+void launch_gemv(const T* A, int lda, const T* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s) {
+    if (K / Vec16<T>::N <= 4 * 32) launch_gemv_u<T, MR, 4>(A, lda, W, M, N, K, epi, s);
+    else launch_gemv_u<T, MR, 16>(A, lda, W, M, N, K, epi, s);
 }
 
 }  // namespace
 
-bool gemv_ln_fits(int M, int K, bool bf16_rows) {
-    return M >= 1 && M <= 16 && K % 128 == 0 && K <= 1024 && static_cast<size_t>(M) * K * (bf16_rows ? 2 : 4) <= kGemvLnSmem;
-}
-
 template <typename TA, typename TW>
-void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s,
-               const LnPrologue* ln) {
+void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s) {
     static_assert(std::is_same<TA, TW>::value, "A and W share a type");
     if (M <= 16) {
         constexpr int VW = Vec16<TA>::N;
         const bool vec = K % VW == 0 && lda % VW == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(W) & 15) == 0;
-        if (vec || ln) {
-            if (M <= 2) launch_gemv<TA, 2>(A, lda, W, M, N, K, epi, ln, s);
-            else if (M <= 4) launch_gemv<TA, 4>(A, lda, W, M, N, K, epi, ln, s);
-            else if (M <= 8) launch_gemv<TA, 8>(A, lda, W, M, N, K, epi, ln, s);
-            else launch_gemv<TA, 16>(A, lda, W, M, N, K, epi, ln, s);
+        if (vec) {
+            if (M <= 2) launch_gemv<TA, 2>(A, lda, W, M, N, K, epi, s);
+            else if (M <= 4) launch_gemv<TA, 4>(A, lda, W, M, N, K, epi, s);
+            else if (M <= 8) launch_gemv<TA, 8>(A, lda, W, M, N, K, epi, s);
+            else launch_gemv<TA, 16>(A, lda, W, M, N, K, epi, s);
         } else {
             launch_pdl(gemv_rows_kernel<TA, 8, false>, dim3((N + 7) / 8), dim3(256), 0, s, A, lda, W, M, N, K, epi);
         }
@@ -299,9 +233,7 @@ void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const Gem
     }
 }
 
-template void gemm_simt<float, float>(const float*, int, const float*, int, int, int, const GemmEpilogue&, cudaStream_t,
-                                      const LnPrologue*);
-template void gemm_simt<bf16, bf16>(const bf16*, int, const bf16*, int, int, int, const GemmEpilogue&, cudaStream_t,
-                                    const LnPrologue*);
+template void gemm_simt<float, float>(const float*, int, const float*, int, int, int, const GemmEpilogue&, cudaStream_t);
+template void gemm_simt<bf16, bf16>(const bf16*, int, const bf16*, int, int, int, const GemmEpilogue&, cudaStream_t);
 
 }  // namespace ud

@@ -67,18 +67,8 @@ void gemm_tc2(const TmaMatrix& A, const TmaMatrix& W_half, int M, int N, int K, 
               int* dev_err, int num_sms, const TmaMatrix* out_map, cudaStream_t s);
 
 // ---- SIMT GEMM for few rows (M small) and for the fp32 engine. TA/TW in {float, bf16}.
-// LayerNorm prologue of the few-row GEMV: A = LN(x) (eps 1e-5), x fp32 [M, ldx] with K columns; A is then unused.
-// Only for M <= 16 when gemv_ln_fits(M, K, TA is bf16); epi.out must not alias x.
-struct LnPrologue {
-    const float* x = nullptr;
-    int ldx = 0;
-    const float* g = nullptr;
-    const float* b = nullptr;
-};
-bool gemv_ln_fits(int M, int K, bool bf16_rows);
 template <typename TA, typename TW>
-void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s,
-               const LnPrologue* ln = nullptr);
+void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s);
 
 // ---- LayerNorm over rows of width D (eps 1e-5). x fp32 [M, D] -> y (TO) [M, D].
 template <typename TO>
