@@ -178,6 +178,44 @@ def test_bf16_batched_ragged_streams_with_decode(full24):
         eng.close_stream(sid)
 
 
+def test_bf16_long_chunks_next_to_short_ones():
+    """Chunks of more than 16 frames (lookahead 30: 31 frames per steady chunk) take the bf16 CUDA-core attention
+    kernel instead of the tensor-core one; batched with a lookahead-1 stream in the same call, the batch is ragged
+    from 2 to 31 frames. Both streams match the oracle at 2e-2 and their caches stay within the same bound."""
+    dims = ModelDims(n_layers=2)
+    sd = make_weights(dims, seed=4)
+    eng = ud.Engine(ud.default_config(n_layers=2, max_streams=2, max_batch=2, max_chunk_frames=32))
+    eng.load_weights(sd)
+    enc = Encoder(round_bf16(sd), dims)
+    las, lengths = [30, 1], [700, 90]
+    ids = [eng.open(r) for r in las]
+    mels = [torch.randn(n, 128, generator=torch.Generator().manual_seed(40 + i)) for i, n in enumerate(lengths)]
+    plans = [list(chunk_plan(n, r)) for n, r in zip(lengths, las)]
+    sts = [StreamState(dims) for _ in las]
+    for k in range(max(len(p) for p in plans)):
+        act = [i for i in range(2) if k < len(plans[i])]
+        chunks, rows, vr, ka = [], [], [], []
+        for i in act:
+            start, n, v, keep_all = plans[i][k]
+            chunks.append(mels[i][start:start + n].numpy())
+            rows.append(n)
+            vr.append(v)
+            ka.append(keep_all)
+        projs, frames, _ = eng.step_batch([ids[i] for i in act], chunks, rows, vr, ka)
+        for j, i in enumerate(act):
+            ref, keep, *_ = enc.stream_step(sts[i], torch.from_numpy(chunks[j]), rows[j], vr[j], ka[j], las[i])
+            assert frames[j] == keep
+            if keep:
+                assert rel(projs[j], ref) < 2e-2, (k, i)
+    for i, sid in enumerate(ids):
+        n = sts[i].cache_len
+        for li in (0, 1):
+            assert rel(cache_f32(eng, sid, li, 0)[70 - n:], sts[i].k[li, 70 - n:]) < 2e-2
+            assert rel(cache_f32(eng, sid, li, 2), sts[i].conv[li]) < 2e-2
+        eng.close_stream(sid)
+    eng.close()
+
+
 def test_protocol_object_matches_batched_path(full24):
     """CudaNemotronEncoder.step (the NemotronEncoder mirror, one stream per call) gives the same result as
     the batched entry point for the same stream history."""

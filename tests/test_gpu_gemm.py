@@ -102,6 +102,32 @@ def test_residual_in_place_and_bf16_output(eng):
     assert err.max().item() < 1e-2
 
 
+@pytest.mark.parametrize("shape", [(3584, 1024, 4096), (777, 1024, 1024), (300, 2048, 1024), (2000, 1040, 256)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("act", [0, 2], ids=["none", "silu"])
+def test_in_place_residual_equals_separate_residual(eng, shape, act):
+    """x += 0.5 * act(A W^T + bias) in place (the encoder's residual form; on the 2-CTA kernel with 256-wide
+    tiles an fp32 reduce-add into x) is bit-identical to the same epilogue with a separate residual buffer and
+    output (the register epilogue), and within the GEMM tolerance of a float64 reference."""
+    M, N, K = shape
+    dt = torch.bfloat16 if eng.cfg.dtype == ud.DTYPE_BF16 else torch.float32
+    A, W = _inputs(M, N, K, dt, 6)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    bias = torch.rand(N, device="cuda", generator=g) - 0.5
+    X = (torch.rand(M, N, device="cuda", generator=g) - 0.5) * 4
+    R = X.clone()
+    C = torch.empty(M, N, device="cuda")
+    _gemm(eng, A.data_ptr(), W.data_ptr(), M, N, K, C.data_ptr(), bias_ptr=bias.data_ptr(), act=act, out_scale=0.5,
+          res_ptr=R.data_ptr())
+    _gemm(eng, A.data_ptr(), W.data_ptr(), M, N, K, X.data_ptr(), bias_ptr=bias.data_ptr(), act=act, out_scale=0.5,
+          res_ptr=X.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(X, C)
+    z = A.double() @ W.double().T + bias.double()
+    z = z * torch.sigmoid(z) if act == 2 else z
+    assert (X.double() - (0.5 * z + R.double())).abs().max().item() < 1e-4 * K ** 0.5 + 1e-5
+
+
 def test_repeatable_and_counts_launches(eng):
     M, N, K = 512, 1024, 1024
     dt = torch.bfloat16 if eng.cfg.dtype == ud.DTYPE_BF16 else torch.float32

@@ -259,7 +259,12 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
                     }
                     return &jt->second;
                 };
-                const TmaMatrix* om = (epi.out_bf16 && !epi.residual) ? emap(epi.out, epi.ldo, true) : nullptr;
+                // output maps for the TMA epilogues: bf16 stores, and fp32 reduce-adds when the residual is the output
+                const TmaMatrix* om = nullptr;
+                if (epi.out_bf16 && !epi.residual)
+                    om = emap(epi.out, epi.ldo, true);
+                else if (!epi.out_bf16 && epi.residual == epi.out && epi.ldr == epi.ldo && epi.res_scale == 1.f)
+                    om = emap(epi.out, epi.ldo, false);
                 gemm_tc2(it->second, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, om, e->stream);
             } else {
                 const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;

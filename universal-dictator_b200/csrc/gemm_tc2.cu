@@ -14,16 +14,19 @@
 // their width balanced and rounded up to a multiple of 16 (N = 1024 -> 256; N = 1040 -> 5 tiles of 208; the
 // last tile of a row may be narrower). The MMA's N, the W rows each CTA loads (tile width / 2) and the epilogue
 // width are read from the tile. Narrower tiles that would fill a partial last round of pairs measured slower
-// than the wide tiles on the encoder's shapes, so the host does not trade width for rounds.
+// than the wide tiles on the encoder's shapes, so the host does not trade width for rounds: an MMA of N = 128
+// took as long as one of N = 256 (256 x 128 tiles, two per pair, doubled the MMA time of every shape).
 //
-// TMA epilogue (TE: bf16 outputs without residual, every tile 256 wide, host-supplied tensor map of the output):
-// each epilogue warp owns two 4 KB shared-memory blocks of 32 rows x 128 bytes (64 bf16 columns) in the
+// TMA epilogues (every tile 256 wide, host-supplied tensor map of the output): bf16 outputs without a residual,
+// and fp32 outputs whose residual is the output itself with unit scale (the encoder's x += s * f(x)). Each
+// epilogue warp owns two 4 KB shared-memory blocks of 32 rows x 128 bytes (64 bf16 or 32 fp32 columns) in the
 // 128-byte swizzled layout. Per block it reads its TMEM rows, applies bias / activation / scale, writes the block
-// (conflict-free: lane = row, 16-byte chunk k at position k ^ (row % 8)) and one lane stores it with a TMA bulk
-// store; out-of-range rows are clipped by the copy. A buffer is rewritten only after the store issued from it
-// two blocks earlier has read it (cp.async.bulk.wait_group.read). Five pipeline stages leave room for the
-// 64 KB of blocks. For bf16 outputs this measured faster than the register epilogue; fp32 outputs with a
-// residual (HBM-bound either way) keep the register epilogue.
+// (conflict-free: lane = row, 16-byte chunk k at position k ^ (row % 8)) and one lane issues a TMA bulk store
+// (bf16) or a TMA bulk reduce-add (fp32: the L2 adds the block to the output, so the residual never travels to
+// the SM); out-of-range rows are clipped by the copy. A buffer is rewritten only after the copy issued from it
+// two blocks earlier has read it (cp.async.bulk.wait_group.read). Five pipeline stages leave room for the 64 KB
+// of blocks. The register epilogue (staged through shared memory, residual read by the SM) serves every other
+// output form.
 #include <cstdlib>
 
 #include "common.cuh"
@@ -38,16 +41,19 @@ constexpr int BK = 64;
 constexpr int kThreads = 320;
 constexpr int kEpiWarps = 8;
 
-template <int BN, bool TE>
+// Epilogue modes: register epilogue (any output), TMA store of bf16 blocks, TMA reduce-add of fp32 blocks.
+enum Tc2Epi { kEpiReg = 0, kEpiStoreBf16 = 1, kEpiAddF32 = 2 };
+
+template <int BN, int EP>
 struct Tc2Cfg {
-    static constexpr int STAGES = TE ? 5 : 6;
+    static constexpr int STAGES = EP != kEpiReg ? 5 : 6;
     static constexpr int A_BYTES = 128 * BK * 2;        // this CTA's half of the A tile
     static constexpr int B_BYTES = (BN / 2) * BK * 2;   // this CTA's half of the W tile (a full 128-row box)
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int BAR_BYTES = 256;                // pipeline and accumulator barriers
     static constexpr int EPI_OFF = (STAGES * STAGE_BYTES + BAR_BYTES + 1023) / 1024 * 1024;   // 1 KB aligned
-    static constexpr int EPI_BYTES = TE ? kEpiWarps * 2 * 4096 : kEpiWarps * kEpiStageBytes;
+    static constexpr int EPI_BYTES = EP != kEpiReg ? kEpiWarps * 2 * 4096 : kEpiWarps * kEpiStageBytes;
     static constexpr int SMEM = EPI_OFF + EPI_BYTES + 1024;
 };
 
@@ -96,12 +102,12 @@ __device__ __forceinline__ void tc2_commit_both(uint64_t* bar) {
         : "memory");
 }
 
-template <int BN, bool TE>
+template <int BN, int EP>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW,
                     const __grid_constant__ CUtensorMap mapO, int M, int N,
                     int K, int tn, const GemmEpilogue epi, int* err) {
-    using C = Tc2Cfg<BN, TE>;
+    using C = Tc2Cfg<BN, EP>;
     pdl_launch_dependents();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -138,7 +144,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         fence_mbarrier_init();
         prefetch_tensormap(&mapA);
         prefetch_tensormap(&mapW);
-        if (TE) prefetch_tensormap(&mapO);
+        if (EP != kEpiReg) prefetch_tensormap(&mapO);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -215,9 +221,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
         mma_done:;
         }
-    } else if constexpr (TE) {
+    } else if constexpr (EP != kEpiReg) {
+        // Blocks of 32 rows x 128 bytes: 64 bf16 columns (store) or 32 fp32 columns (reduce-add).
+        constexpr int BC = EP == kEpiStoreBf16 ? 64 : 32;
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;   // the two warps of a lane quadrant take column halves of the tile
+        const int hw = tn / 2;              // columns per warp: 128 or 64 (a multiple of BC)
         uint8_t* eb = smem + C::EPI_OFF + (warp - 2) * 8192;   // this warp's two blocks
         const int swz = lane & 7;
         int acc = 0, g = 0;
@@ -229,41 +238,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t t_base =
-                tmem_base + static_cast<uint32_t>(acc * BN + half * 128) + (static_cast<uint32_t>(q * 32) << 16);
+                tmem_base + static_cast<uint32_t>(acc * BN + half * hw) + (static_cast<uint32_t>(q * 32) << 16);
             const int y = (tile % num_m) * BM2 + static_cast<int>(rank) * 128 + q * 32;
-            for (int ch = 0; ch < 2; ++ch, ++g) {   // two blocks of 64 columns
+            for (int ch = 0; ch < hw / BC; ++ch, ++g) {
                 uint8_t* buf = eb + (g & 1) * 4096;
-                const int x = (tile / num_m) * 256 + half * 128 + ch * 64;
-                if (lane == 0) tma_store_wait_read<1>();   // the store issued from buf two blocks ago has read it
+                const int x = (tile / num_m) * tn + half * hw + ch * BC;
+                if (lane == 0) tma_store_wait_read<1>();   // the copy issued from buf two blocks ago has read it
                 __syncwarp();
-                float v[64];
-                tmem_ld32(t_base + static_cast<uint32_t>(ch * 64), v);
-                tmem_ld32(t_base + static_cast<uint32_t>(ch * 64 + 32), v + 32);
+                float v[BC];
+                tmem_ld32(t_base + static_cast<uint32_t>(ch * BC), v);
+                if constexpr (BC == 64) tmem_ld32(t_base + static_cast<uint32_t>(ch * BC + 32), v + 32);
                 uint8_t* row = buf + lane * 128;
+                constexpr int PER = BC / 8;   // values per 16-byte chunk
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                    float e[8];
+                    float e[PER];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) e[j] = v[8 * k + j];
+                    for (int j = 0; j < PER; ++j) e[j] = v[PER * k + j];
                     if (epi.bias) {
-                        const float4 b0 = *reinterpret_cast<const float4*>(epi.bias + x + 8 * k);
-                        const float4 b1 = *reinterpret_cast<const float4*>(epi.bias + x + 8 * k + 4);
-                        e[0] += b0.x; e[1] += b0.y; e[2] += b0.z; e[3] += b0.w;
-                        e[4] += b1.x; e[5] += b1.y; e[6] += b1.z; e[7] += b1.w;
-                    }
-                    uint32_t w[4];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        __nv_bfloat162 h = __floats2bfloat162_rn(epi_act(epi.act, e[2 * j]) * epi.out_scale,
-                                                                 epi_act(epi.act, e[2 * j + 1]) * epi.out_scale);
-                        w[j] = *reinterpret_cast<uint32_t*>(&h);
+                        for (int j = 0; j < PER; j += 4) {
+                            const float4 b = *reinterpret_cast<const float4*>(epi.bias + x + PER * k + j);
+                            e[j] += b.x; e[j + 1] += b.y; e[j + 2] += b.z; e[j + 3] += b.w;
+                        }
                     }
-                    *reinterpret_cast<uint4*>(row + ((k ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    uint4 u;
+                    if constexpr (EP == kEpiStoreBf16) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            __nv_bfloat162 h = __floats2bfloat162_rn(epi_act(epi.act, e[2 * j]) * epi.out_scale,
+                                                                     epi_act(epi.act, e[2 * j + 1]) * epi.out_scale);
+                            w[j] = *reinterpret_cast<uint32_t*>(&h);
+                        }
+                        u = make_uint4(w[0], w[1], w[2], w[3]);
+                    } else {
+                        u = make_uint4(__float_as_uint(epi_act(epi.act, e[0]) * epi.out_scale),
+                                       __float_as_uint(epi_act(epi.act, e[1]) * epi.out_scale),
+                                       __float_as_uint(epi_act(epi.act, e[2]) * epi.out_scale),
+                                       __float_as_uint(epi_act(epi.act, e[3]) * epi.out_scale));
+                    }
+                    *reinterpret_cast<uint4*>(row + ((k ^ swz) << 4)) = u;
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&mapO, buf, x, y);
+                    if constexpr (EP == kEpiStoreBf16) tma_store_2d(&mapO, buf, x, y);
+                    else tma_reduce_add_2d(&mapO, buf, x, y);
                     tma_store_commit();
                 }
             }
@@ -311,12 +332,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 template <int BN>
 void launch2(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const GemmEpilogue& epi, int* err,
              int num_sms, const TmaMatrix* out_map, cudaStream_t s) {
-    using C = Tc2Cfg<BN, false>;
-    using CT = Tc2Cfg<BN, true>;
+    using C = Tc2Cfg<BN, kEpiReg>;
+    using CT = Tc2Cfg<BN, kEpiStoreBf16>;
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(gemm_tc2_kernel<BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        cudaFuncSetAttribute(gemm_tc2_kernel<BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
+        cudaFuncSetAttribute(gemm_tc2_kernel<BN, kEpiReg>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaFuncSetAttribute(gemm_tc2_kernel<BN, kEpiStoreBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
+        cudaFuncSetAttribute(gemm_tc2_kernel<BN, kEpiAddF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
         attr = true;
     }
     // Persistent grid: no more pairs than can be resident at once (clusters are placed within GPCs).
@@ -334,7 +356,7 @@ void launch2(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const 
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BN, false>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BN, kEpiReg>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = num_sms / 2;
         }
@@ -346,19 +368,28 @@ void launch2(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const 
     const int tn = ((N + per_row - 1) / per_row + 15) / 16 * 16;
     const int tiles = num_m * ((N + tn - 1) / tn);
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
+    // UD_TMA_EPI: unset = both TMA epilogues, 1 = bf16 stores only, 0 = the register epilogue everywhere.
     static int te_env = -1;
     if (te_env < 0) {
         const char* v = std::getenv("UD_TMA_EPI");
-        te_env = (v && std::atoi(v) == 0) ? 0 : 1;
+        te_env = v ? std::atoi(v) : 2;
     }
-    const bool te = BN == 256 && te_env && out_map && tn == 256 && N % 256 == 0 && epi.out_bf16 &&
-                    epi.residual == nullptr;
-    if (te)
-        launch_pdl(gemm_tc2_kernel<BN, true>, dim3(2 * pairs), dim3(kThreads), CT::SMEM, s, A.map, W.map, out_map->map,
-                   M, N, K, tn, epi, err);
+    const bool full_tiles = BN == 256 && out_map && tn == 256 && N % 256 == 0;
+    int ep = kEpiReg;
+    if (full_tiles && te_env >= 1 && epi.out_bf16 && epi.residual == nullptr) ep = kEpiStoreBf16;
+    // out += out_scale * act(acc + bias): the residual is the output itself, added once per element at L2.
+    if (full_tiles && te_env >= 2 && !epi.out_bf16 && epi.residual == epi.out && epi.ldr == epi.ldo &&
+        epi.res_scale == 1.f)
+        ep = kEpiAddF32;
+    const dim3 grid(2 * pairs), block(kThreads);
+    if (ep == kEpiStoreBf16)
+        launch_pdl(gemm_tc2_kernel<BN, kEpiStoreBf16>, grid, block, CT::SMEM, s, A.map, W.map, out_map->map, M, N, K,
+                   tn, epi, err);
+    else if (ep == kEpiAddF32)
+        launch_pdl(gemm_tc2_kernel<BN, kEpiAddF32>, grid, block, CT::SMEM, s, A.map, W.map, out_map->map, M, N, K,
+                   tn, epi, err);
     else
-        launch_pdl(gemm_tc2_kernel<BN, false>, dim3(2 * pairs), dim3(kThreads), C::SMEM, s, A.map, W.map, A.map, M, N,
-                   K, tn, epi, err);
+        launch_pdl(gemm_tc2_kernel<BN, kEpiReg>, grid, block, C::SMEM, s, A.map, W.map, A.map, M, N, K, tn, epi, err);
 }
 
 }  // namespace
