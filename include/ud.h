@@ -124,6 +124,23 @@ UD_API ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, con
                         const int* n_rows, const int* valid_rows, const int* keep_all,
                         float* proj_out, int* frames_out, int32_t* tokens_out, int* n_tokens_out);
 
+/* Pipelined form of ud_step_batch (no reference counterpart: a serving loop's overlap of host copies with
+ * compute). Same arguments and results; the call enqueues the step's input copy, encoder pass and output copy
+ * and returns without waiting for them. The input copy runs on a copy stream of its own while the previous step
+ * computes, and the output copy on another while the next one computes (two staging buffers alternate). On return the
+ * PREVIOUS asynchronous step is complete: its outputs are in its caller's buffers and its input rows may be
+ * reused. This step's host buffers must stay untouched until the next ud_step_batch_async or ud_step_sync
+ * returns. frames_out is filled on return. The copies are DMA only from pinned (page-locked) host memory
+ * given as one buffer with a fixed stride between streams; other inputs are gathered through a pinned staging
+ * buffer first. Device errors of a step are reported by the call that completes it. Every other entry point
+ * that runs a step waits for outstanding asynchronous steps first. */
+UD_API ud_status ud_step_batch_async(ud_engine* e, int n, const ud_stream_id* ids, const float* const* mel,
+                              const int* n_rows, const int* valid_rows, const int* keep_all,
+                              float* proj_out, int* frames_out, int32_t* tokens_out, int* n_tokens_out);
+
+/* Waits until every asynchronous step is complete (outputs in place); reports a device error of the last one. */
+UD_API ud_status ud_step_sync(ud_engine* e);
+
 /* Same with device-resident input and outputs, asynchronous on the engine's CUDA stream:
  * mel_dev [n, rows_stride, mel_bins] fp32 (stream i's rows at i*rows_stride), proj_dev
  * [n, max_chunk_frames, joint_dim], tokens_dev / n_tokens_dev as above or NULL. frames_out (host)

@@ -116,6 +116,17 @@ struct ud_engine {
     float* h_in = nullptr;
     int* h_ntok = nullptr;
 
+    // Pipelined host-buffer steps (ud_step_batch_async): staging buffer 1 and the copy streams (inputs, outputs:
+    // separate, so step k+1's input copy does not queue behind step k's output copy), allocated on first use
+    // (buffer 0 is in_stage / out_stage / tok_dev / ntok_dev / h_in). Step k uses buffer k % 2.
+    cudaStream_t cstream = nullptr, ostream = nullptr;
+    float *in_stage2 = nullptr, *out_stage2 = nullptr, *h_in2 = nullptr;
+    int32_t* tok_dev2 = nullptr;
+    int* ntok_dev2 = nullptr;
+    int* err_async_h = nullptr;                                   // pinned [2]: device error flag after each step
+    cudaEvent_t ev_in[2] = {}, ev_done[2] = {}, ev_out[2] = {};   // input copied, step computed, output copied
+    int64_t async_issued = 0, async_completed = 0;
+
     static constexpr int kRing = 4;
     BatchEntry* meta_h[kRing] = {};
     BatchEntry* meta_d[kRing] = {};
@@ -136,8 +147,8 @@ struct ud_engine {
     bool graphs_on = true;
     bool tc2_on = true;  // 2-CTA tcgen05 tiles for M >= 256, N % 256 == 0
     BatchEntry* meta_graph_d = nullptr;
-    std::map<std::tuple<int, int, int, int, int>, GraphEntry> graphs;
-    std::map<std::tuple<int, int, int, int, int>, int> graph_seen;
+    std::map<std::tuple<int, int, int, int, int, int>, GraphEntry> graphs;   // + staging buffer index
+    std::map<std::tuple<int, int, int, int, int, int>, int> graph_seen;
     // per-kernel-class timing
     bool prof = false;
     std::vector<cudaEvent_t> prof_events;
@@ -287,20 +298,58 @@ GemmEpilogue epi_out(void* out, int ldo, bool out_act_dtype, const ud_engine* e)
     return g;
 }
 
+// The status of a nonzero device error flag value; clears the flag.
+ud_status device_error_status(ud_engine* e, int code) {
+    UD_CK(cudaMemsetAsync(e->err_d, 0, sizeof(int), e->stream));
+    UD_CK(cudaStreamSynchronize(e->stream));
+    static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
+                                  "GEMM TMEM drain wait", "unmapped cache page", "test wait",
+                                  "RNN-T grid barrier wait"};
+    const char* nm = (code >= 0 && code <= 7) ? names[code] : "unknown";
+    if (code == DEV_BAD_PAGE) return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
+    return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
+}
+
 ud_status check_device_error(ud_engine* e) {
     UD_CK(cudaMemcpyAsync(e->err_h, e->err_d, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     UD_CK(cudaStreamSynchronize(e->stream));
     const int code = *e->err_h;
-    if (code != 0) {
-        UD_CK(cudaMemsetAsync(e->err_d, 0, sizeof(int), e->stream));
-        UD_CK(cudaStreamSynchronize(e->stream));
-        static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
-                                      "GEMM TMEM drain wait", "unmapped cache page", "test wait",
-                                      "RNN-T grid barrier wait"};
-        const char* nm = (code >= 0 && code <= 7) ? names[code] : "unknown";
-        if (code == DEV_BAD_PAGE) return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
-        return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
+    return code != 0 ? device_error_status(e, code) : UD_OK;
+}
+
+// Completes every outstanding pipelined step (output copies done); the first device error among them is the
+// status.
+ud_status drain_async(ud_engine* e) {
+    if (!e->cstream || e->async_completed == e->async_issued) return UD_OK;
+    UD_CK(cudaStreamSynchronize(e->cstream));
+    UD_CK(cudaStreamSynchronize(e->ostream));
+    int code = 0;
+    for (; e->async_completed < e->async_issued; ++e->async_completed) {
+        const int b = static_cast<int>(e->async_completed & 1);
+        if (code == 0) code = e->err_async_h[b];
     }
+    return code != 0 ? device_error_status(e, code) : UD_OK;
+}
+
+// Staging buffer 1, the copy stream and the events of the pipelined steps, on first use.
+ud_status async_setup(ud_engine* e) {
+    if (e->cstream) return UD_OK;
+    const size_t B = static_cast<size_t>(e->cfg.max_batch);
+    const size_t in_elems = B * e->max_rows_in * e->in_width;
+    const size_t out_elems = B * e->tmax * e->out_width;
+    const size_t tok_elems = B * e->tmax * e->cfg.max_symbols;
+    UD_TRY(dalloc(e, &e->in_stage2, in_elems));
+    UD_TRY(dalloc(e, &e->out_stage2, out_elems));
+    UD_TRY(dalloc(e, &e->tok_dev2, tok_elems));
+    UD_TRY(dalloc(e, &e->ntok_dev2, B));
+    UD_TRY(halloc(e, &e->h_in2, in_elems));
+    UD_TRY(halloc(e, &e->err_async_h, 2));
+    e->err_async_h[0] = e->err_async_h[1] = 0;
+    for (int b = 0; b < 2; ++b)
+        for (cudaEvent_t* ev : {&e->ev_in[b], &e->ev_done[b], &e->ev_out[b]})
+            if (!*ev) UD_CK(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+    UD_CK(cudaStreamCreateWithFlags(&e->ostream, cudaStreamNonBlocking));
+    UD_CK(cudaStreamCreateWithFlags(&e->cstream, cudaStreamNonBlocking));
     return UD_OK;
 }
 
@@ -563,7 +612,8 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
         }
         std::memcpy(mh[i].pages, e->slots[ids[i]].pages, sizeof(mh[i].pages));
     }
-    const std::tuple<int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0};
+    const std::tuple<int, int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0,
+                                                       in_dev == e->in_stage ? 0 : 1};
     const bool use_graph = graph_ok && e->graphs_on && !e->prof;
     if (!use_graph) {
         UD_TRY(upload_meta(e, mi, n));
@@ -1241,8 +1291,15 @@ ud_status ud_shutdown(ud_engine* e) {
     if (e->stream) cudaStreamSynchronize(e->stream);
     for (void* p : e->allocs) cudaFree(p);
     for (void* p : e->host_allocs) cudaFreeHost(p);
+    if (e->cstream) cudaStreamSynchronize(e->cstream);
+    if (e->ostream) cudaStreamSynchronize(e->ostream);
     for (int r = 0; r < ud_engine::kRing; ++r)
         if (e->meta_ev[r]) cudaEventDestroy(e->meta_ev[r]);
+    for (int b = 0; b < 2; ++b)
+        for (cudaEvent_t ev : {e->ev_in[b], e->ev_done[b], e->ev_out[b]})
+            if (ev) cudaEventDestroy(ev);
+    if (e->cstream) cudaStreamDestroy(e->cstream);
+    if (e->ostream) cudaStreamDestroy(e->ostream);
     for (cudaEvent_t ev : e->prof_events) cudaEventDestroy(ev);
     for (auto& g : e->graphs) cudaGraphExecDestroy(g.second.exec);
     if (e->stream) cudaStreamDestroy(e->stream);
@@ -1352,6 +1409,7 @@ ud_status ud_step_batch_device(ud_engine* e, int n, const ud_stream_id* ids, con
     if (!mel_dev || !proj_dev || !n_rows) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
     if (n < 1 || n > e->cfg.max_batch) return fail(UD_ERR_INVALID_ARGUMENT, "batch size out of range");
     UD_CK(cudaSetDevice(e->device));
+    UD_TRY(drain_async(e));
     int rows_max = 1;
     for (int i = 0; i < n; ++i) {
         if (n_rows[i] < 1 || n_rows[i] > e->max_rows_in || n_rows[i] > rows_stride)
@@ -1390,6 +1448,7 @@ ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const floa
         rows_max = std::max(rows_max, n_rows[i]);
     }
     const int W = e->in_width;
+    UD_TRY(drain_async(e));
     // The pinned staging buffer may still be read by a previous asynchronous call.
     UD_CK(cudaStreamSynchronize(e->stream));
     // Rows of all streams in one caller buffer at a fixed stride: one strided copy straight from it (a DMA when
@@ -1421,6 +1480,79 @@ ud_status ud_step_batch(ud_engine* e, int n, const ud_stream_id* ids, const floa
     UD_TRY(check_device_error(e));
     if (frames_out) std::memcpy(frames_out, frames.data(), sizeof(int) * n);
     return UD_OK;
+}
+
+ud_status ud_step_batch_async(ud_engine* e, int n, const ud_stream_id* ids, const float* const* mel, const int* n_rows,
+                              const int* valid_rows, const int* keep_all, float* proj_out, int* frames_out,
+                              int32_t* tokens_out, int* n_tokens_out) {
+    if (!e || !mel || !n_rows || (!proj_out && !tokens_out)) return fail(UD_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (n < 1 || n > e->cfg.max_batch) return fail(UD_ERR_INVALID_ARGUMENT, "batch size out of range");
+    if (tokens_out && !n_tokens_out) return fail(UD_ERR_INVALID_ARGUMENT, "n_tokens_out is NULL");
+    UD_CK(cudaSetDevice(e->device));
+    const int stride = e->max_rows_in;
+    int rows_max = 1;
+    for (int i = 0; i < n; ++i) {
+        if (!mel[i]) return fail(UD_ERR_INVALID_ARGUMENT, "NULL input rows");
+        if (n_rows[i] < 1 || n_rows[i] > e->max_rows_in)
+            return fail(UD_ERR_INVALID_ARGUMENT, "n_rows out of range");
+        rows_max = std::max(rows_max, n_rows[i]);
+    }
+    UD_TRY(async_setup(e));
+    // Step k uses staging buffer k % 2. Step k - 2, its last user, completed before call k - 1 returned.
+    const int b = static_cast<int>(e->async_issued & 1);
+    float* in_d = b ? e->in_stage2 : e->in_stage;
+    float* out_d = b ? e->out_stage2 : e->out_stage;
+    float* h_in = b ? e->h_in2 : e->h_in;
+    int32_t* tok_d = b ? e->tok_dev2 : e->tok_dev;
+    int* ntok_d = b ? e->ntok_dev2 : e->ntok_dev;
+    const int W = e->in_width;
+    bool uniform = true;
+    const ptrdiff_t sstride = n > 1 ? mel[1] - mel[0] : static_cast<ptrdiff_t>(W) * stride;
+    for (int i = 1; i < n && uniform; ++i) uniform = mel[i] - mel[0] == sstride * i;
+    uniform = uniform && sstride >= static_cast<ptrdiff_t>(W) * rows_max;
+    const float* src = mel[0];
+    size_t spitch = sizeof(float) * sstride;
+    if (!uniform) {
+        for (int i = 0; i < n; ++i)
+            std::memcpy(h_in + static_cast<size_t>(i) * stride * W, mel[i], sizeof(float) * n_rows[i] * W);
+        src = h_in;
+        spitch = sizeof(float) * W * stride;
+    }
+    UD_CK(cudaMemcpy2DAsync(in_d, sizeof(float) * W * stride, src, spitch, sizeof(float) * W * rows_max, n,
+                            cudaMemcpyHostToDevice, e->cstream));
+    UD_CK(cudaEventRecord(e->ev_in[b], e->cstream));
+    UD_CK(cudaStreamWaitEvent(e->stream, e->ev_in[b], 0));
+    std::vector<int> frames(n);
+    UD_TRY(run_batch(e, n, ids, in_d, stride, n_rows, valid_rows, keep_all, out_d, frames.data(),
+                     tokens_out ? tok_d : nullptr, ntok_d, true));
+    UD_CK(cudaMemcpyAsync(e->err_async_h + b, e->err_d, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    UD_CK(cudaEventRecord(e->ev_done[b], e->stream));
+    UD_CK(cudaStreamWaitEvent(e->ostream, e->ev_done[b], 0));
+    const size_t out_n = static_cast<size_t>(n) * e->tmax * e->out_width;
+    if (proj_out)
+        UD_CK(cudaMemcpyAsync(proj_out, out_d, sizeof(float) * out_n, cudaMemcpyDeviceToHost, e->ostream));
+    if (tokens_out) {
+        UD_CK(cudaMemcpyAsync(tokens_out, tok_d, sizeof(int32_t) * n * e->tmax * e->cfg.max_symbols,
+                              cudaMemcpyDeviceToHost, e->ostream));
+        UD_CK(cudaMemcpyAsync(n_tokens_out, ntok_d, sizeof(int) * n, cudaMemcpyDeviceToHost, e->ostream));
+    }
+    UD_CK(cudaEventRecord(e->ev_out[b], e->ostream));
+    ++e->async_issued;
+    if (frames_out) std::memcpy(frames_out, frames.data(), sizeof(int) * n);
+    // complete the previous step: its outputs are in place, its buffers free for the next call
+    if (e->async_issued - e->async_completed > 1) {
+        const int pb = b ^ 1;
+        UD_CK(cudaEventSynchronize(e->ev_out[pb]));
+        ++e->async_completed;
+        if (e->err_async_h[pb] != 0) return device_error_status(e, e->err_async_h[pb]);
+    }
+    return UD_OK;
+}
+
+ud_status ud_step_sync(ud_engine* e) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_CK(cudaSetDevice(e->device));
+    return drain_async(e);
 }
 
 ud_status ud_stream_step(ud_engine* e, ud_stream_id id, const float* mel, int n_rows, int valid_rows, int keep_all,

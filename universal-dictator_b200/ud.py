@@ -34,7 +34,8 @@ KINDS = ["gemm_tc", "gemm_simt", "attention", "conv", "norm", "subsample", "rnnt
 # Every symbol include/ud.h declares (the test suite checks the library exports exactly these).
 ABI_SYMBOLS = [
     "ud_config_default", "ud_init", "ud_shutdown", "ud_load_weights", "ud_load_safetensors", "ud_stream_open",
-    "ud_stream_close", "ud_stream_step", "ud_step_batch", "ud_step_batch_device", "ud_rnnt_decode",
+    "ud_stream_close", "ud_stream_step", "ud_step_batch", "ud_step_batch_async", "ud_step_sync",
+    "ud_step_batch_device", "ud_rnnt_decode",
     "ud_rnnt_decode_static",
     "ud_cache_append", "ud_cache_roll", "ud_cache_gather", "ud_cache_evict", "ud_cache_read", "ud_stream_info",
     "ud_get_cuda_stream", "ud_pool_info", "ud_synchronize", "ud_launch_count", "ud_debug_gemm",
@@ -87,6 +88,9 @@ def lib() -> C.CDLL:
             "ud_stream_close": (I, [eng, C.c_int32]),
             "ud_stream_step": (I, [eng, C.c_int32, P(F), I, I, I, P(F), P(I)]),
             "ud_step_batch": (I, [eng, I, P(C.c_int32), P(P(F)), P(I), P(I), P(I), P(F), P(I), P(C.c_int32), P(I)]),
+            "ud_step_batch_async": (I, [eng, I, P(C.c_int32), P(P(F)), P(I), P(I), P(I), P(F), P(I), P(C.c_int32),
+                                        P(I)]),
+            "ud_step_sync": (I, [eng]),
             "ud_step_batch_device": (I, [eng, I, P(C.c_int32), VP, I, P(I), P(I), P(I), VP, P(I), VP, VP]),
             "ud_rnnt_decode": (I, [eng, C.c_int32, P(F), I, P(C.c_int32), P(I)]),
             "ud_rnnt_decode_static": (I, [eng, C.c_int32, P(F), I, P(C.c_int32), P(I)]),
@@ -284,6 +288,42 @@ class Engine:
         projs = [out[i, :frames[i]] for i in range(n)]     # views into one result block
         tok_lists = [toks[i, :ntok[i]].tolist() for i in range(n)] if decode else None
         return projs, frames.tolist(), tok_lists
+
+    def step_batch_async(self, ids: Sequence[int], mels: Sequence[np.ndarray], n_rows: Sequence[int],
+                         valid_rows: Sequence[int], keep_all: Sequence[bool], out: np.ndarray,
+                         tokens: np.ndarray | None = None, n_tokens: np.ndarray | None = None) -> list[int]:
+        """ud_step_batch_async: enqueues the step and returns its frames; the previous asynchronous step is
+        complete on return. `out` [n, max_chunk_frames, out_width] fp32 (and `tokens` [n, max_chunk_frames *
+        max_symbols] int32 with `n_tokens` [n] int32 when decoding) receive this step's results once the next
+        step_batch_async or step_sync returns. Inputs and outputs should be pinned host memory (views of
+        torch.empty(..., pin_memory=True)) for the copies to overlap compute; this object keeps them alive until
+        the step completes."""
+        n = len(ids)
+        tm, W = self.cfg.max_chunk_frames, self.out_width
+        if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < n * tm * W:
+            raise ValueError("out must be a C-contiguous float32 array of at least n * max_chunk_frames * out_width")
+        if tokens is not None and (tokens.dtype != np.int32 or n_tokens is None or n_tokens.dtype != np.int32
+                                   or not tokens.flags.c_contiguous or tokens.size < n * tm * self.cfg.max_symbols
+                                   or n_tokens.size < n):
+            raise ValueError("tokens / n_tokens: int32 arrays of n * max_chunk_frames * max_symbols and n")
+        arrs = [m if (m.dtype == np.float32 and m.flags.c_contiguous) else np.ascontiguousarray(m, np.float32)
+                for m in mels]
+        ptrs = (C.POINTER(C.c_float) * n)(*[_ptr(a) for a in arrs])
+        frames = np.zeros(n, np.int32)
+        ids_a, nr, vr, ka = _i32(ids), _i32(n_rows), _i32(valid_rows), _i32([int(k) for k in keep_all])
+        check(lib().ud_step_batch_async(self.h, n, _ptr(ids_a, C.c_int32), ptrs, _ptr(nr, C.c_int),
+                                        _ptr(vr, C.c_int), _ptr(ka, C.c_int), _ptr(out),
+                                        _ptr(frames, C.c_int),
+                                        _ptr(tokens, C.c_int32) if tokens is not None else None,
+                                        _ptr(n_tokens, C.c_int) if tokens is not None else None))
+        refs = getattr(self, "_async_refs", [])
+        self._async_refs = (refs + [(arrs, out, tokens, n_tokens)])[-2:]   # this step and the one in flight
+        return frames.tolist()
+
+    def step_sync(self):
+        """ud_step_sync: every asynchronous step complete."""
+        check(lib().ud_step_sync(self.h))
+        self._async_refs = []
 
     def step_batch_device(self, ids, mel_dev_ptr: int, rows_stride: int, n_rows, valid_rows, keep_all,
                           proj_dev_ptr: int, tokens_dev_ptr: int | None = None, ntok_dev_ptr: int | None = None):
