@@ -301,6 +301,15 @@ UD_API ud_status ud_streamer_finished(ud_streamer* s, ud_streamer_id* out, int c
 /* Tokens so far (up to cap copied), the total count, and whether the stream has finished. */
 UD_API ud_status ud_streamer_tokens(ud_streamer* s, ud_streamer_id id, int32_t* out, int cap, int* n_tokens,
                                     int* finished);
+/* Emission records (Emission, Sources/DictatorCore/Nemotron/Streaming.swift:6-15, filled as drainChunks does,
+ * NemotronStreamer.swift:141): for each token so far, the input the stream had received when the step that
+ * emitted it ran (audio samples for an audio stream; 160 x the mel rows pushed for a mel stream) and that step's
+ * wall seconds (its batched encoder pass and decoding). Up to cap of each copied (any pointer may be NULL);
+ * *n = the token count. */
+UD_API ud_status ud_streamer_emissions(ud_streamer* s, ud_streamer_id id, int32_t* tokens, int64_t* samples_seen,
+                                       double* compute_seconds, int cap, int* n);
+/* Wall seconds of each step the stream took part in (NemotronStreamer.wallTimes, :24-25, 63); *n = count. */
+UD_API ud_status ud_streamer_step_times(ud_streamer* s, ud_streamer_id id, double* out, int cap, int* n);
 /* Forgets a stream (closing its engine slot if it has not finished); its id may be reused. */
 UD_API ud_status ud_streamer_release(ud_streamer* s, ud_streamer_id id);
 

@@ -8,7 +8,9 @@
   * a short final tail is zero-extended and masked (end padding, the default) or dropped (end padding off);
   * audio streams (NemotronStreamer.push(samples:) / flush()): the GPU mel frontend feeds the chunk walk; tokens
     equal the oracle pipeline (oracle mel, drainChunks, encoder, greedy), and audio pushed in random sizes gives
-    exactly the tokens of the whole utterance pushed at once.
+    exactly the tokens of the whole utterance pushed at once;
+  * emission records (Emission: token, samples seen, compute seconds) and per-stream step wall times: one record
+    per token, samples seen = the input received before the emitting step, one wall time per chunk run.
 The model is 2 layers with subsampling and a 1-layer prediction net (fp32 engine, 1e-4 tolerance class); the
 joint is sharpened so that token choices are decided by clear logit margins."""
 
@@ -86,7 +88,13 @@ def _run(eng, mels, live: bool, seed: int = 0, end_padding: bool = True) -> list
                 toks, fin = s.tokens(sid)
                 assert fin == (sid in done)
                 if fin:
-                    out[active.pop(sid)] = toks
+                    i = active.pop(sid)
+                    em = s.emissions(sid)
+                    assert [t for t, _, _ in em] == toks
+                    assert all(c > 0 for _, _, c in em)
+                    if not live:   # every row was pushed before the first step
+                        assert all(ss == 160 * len(mels[i]) for _, ss, _ in em)
+                    out[i] = toks
                     s.release(sid)
         return [out[i] for i in range(len(mels))]
     finally:
@@ -157,10 +165,16 @@ def _run_audio(eng, fe, audios, sizes=None, seed=0):
             if all(s.tokens(i)[1] for i in ids):
                 break
         out = []
-        for i in ids:
+        for k, i in enumerate(ids):
             toks, fin = s.tokens(i)
             assert fin
-            out.append(toks)
+            em = s.emissions(i)
+            assert [t for t, _, _ in em] == toks
+            seen = [ss for _, ss, _ in em]
+            assert seen == sorted(seen) and all(0 < x <= len(audios[k]) for x in seen)
+            if sizes is None:   # the whole utterance was pushed before the first step
+                assert all(x == len(audios[k]) for x in seen)
+            out.append((toks, len(s.step_times(i))))
             s.release(i)
         return out
     finally:
@@ -176,8 +190,9 @@ def test_audio_streams_match_the_oracle_pipeline(model):
         got = _run_audio(eng, fe, audios)
         for i, a in enumerate(audios):
             mel, _ = mel_features(torch.from_numpy(a), fb, win)    # NeMo streaming counts every frame as valid
-            assert got[i] == _oracle_tokens(sd, dims, mel.numpy()), i
-        assert any(len(t) > 0 for t in got)
+            assert got[i][0] == _oracle_tokens(sd, dims, mel.numpy()), i
+            assert got[i][1] == len(list(live_plan(mel.shape[0], R, True))), i   # one wall time per chunk
+        assert any(len(t) > 0 for t, _ in got)
         live = _run_audio(eng, fe, audios, sizes=[1, 160, 333, 1600, 4000], seed=5)
         assert live == got
     finally:

@@ -933,13 +933,15 @@ bool parse_safetensors_header(const std::string& js, std::vector<StEntry>& out) 
         ++i;
         return true;
     };
-    auto num = [&](int64_t& v) -> bool {
+    auto num = [&](int64_t& v) -> bool {   // a non-negative integer below 2^62 (shapes and byte offsets)
         ws();
-        size_t st = i;
-        while (i < js.size() && (isdigit(static_cast<unsigned char>(js[i])) || js[i] == '-')) ++i;
-        if (st == i) return false;
-        v = std::stoll(js.substr(st, i - st));
-        return true;
+        const size_t st = i;
+        v = 0;
+        while (i < js.size() && isdigit(static_cast<unsigned char>(js[i]))) {
+            if (v > (int64_t(1) << 58)) return false;
+            v = v * 10 + (js[i++] - '0');
+        }
+        return i > st;
     };
     auto skip_value = [&]() -> bool {
         ws();
@@ -1333,17 +1335,21 @@ ud_status ud_load_safetensors(ud_engine* e, const char* path) {
         std::fclose(f);
         return fail(UD_ERR_IO, "cannot parse safetensors header");
     }
+    // Tensors of other dtypes (integer counters such as a batch norm's num_batches_tracked) are not weights the
+    // engine reads: they are skipped, and a needed tensor stored that way is reported missing.
     std::vector<std::vector<float>> data(ents.size());
-    std::vector<ud_weight> table(ents.size());
+    std::vector<ud_weight> table;
+    table.reserve(ents.size());
     const uint64_t base = 8 + hlen;
     for (size_t k = 0; k < ents.size(); ++k) {
         const StEntry& en = ents[k];
         int64_t count = 1;
         for (int64_t d : en.shape) count *= d;
         const int esz = en.dtype == "F32" ? 4 : (en.dtype == "F16" || en.dtype == "BF16") ? 2 : 0;
-        if (!esz || en.shape.size() > 4 || en.end - en.begin != static_cast<uint64_t>(count) * esz) {
+        if (!esz) continue;
+        if (en.shape.size() > 4 || en.end - en.begin != static_cast<uint64_t>(count) * esz) {
             std::fclose(f);
-            return fail(UD_ERR_IO, "unsupported tensor " + en.name + " (" + en.dtype + ")");
+            return fail(UD_ERR_IO, "bad tensor " + en.name + " (" + en.dtype + ")");
         }
         std::vector<uint8_t> raw(en.end - en.begin);
         if (std::fseek(f, static_cast<long>(base + en.begin), SEEK_SET) != 0 ||
@@ -1366,12 +1372,15 @@ ud_status ud_load_safetensors(ud_engine* e, const char* path) {
                 }
             }
         }
-        table[k].name = ents[k].name.c_str();
-        table[k].data = data[k].data();
-        table[k].ndim = static_cast<int>(en.shape.size());
-        for (size_t d = 0; d < en.shape.size(); ++d) table[k].shape[d] = en.shape[d];
+        ud_weight w{};
+        w.name = ents[k].name.c_str();
+        w.data = data[k].data();
+        w.ndim = static_cast<int>(en.shape.size());
+        for (size_t d = 0; d < en.shape.size(); ++d) w.shape[d] = en.shape[d];
+        table.push_back(w);
     }
     std::fclose(f);
+    if (table.empty()) return fail(UD_ERR_WEIGHTS, "no F32/F16/BF16 tensors in the file");
     return ud_load_weights(e, table.data(), static_cast<int>(table.size()));
 }
 

@@ -17,6 +17,7 @@
 //
 // Only the public C ABI of the engine and the mel frontend is used.
 #include <algorithm>
+#include <chrono>
 #include <cstddef>
 #include <cstring>
 #include <vector>
@@ -37,6 +38,11 @@ struct StreamRec {
     int capacity = 0, avail = 0, idx = 0;
     ud_stream_id slot = -1;
     std::vector<int32_t> tokens;
+    // per token: the input received when its step ran and that step's wall seconds (Emission); per step the
+    // stream took part in: the step's wall seconds (wallTimes)
+    int64_t samples = 0;            // audio samples pushed (audio streams)
+    std::vector<int64_t> emit_samples;
+    std::vector<double> emit_secs, step_secs;
     // audio streams: the frontend's stream and the rows kept from row `own_start` on
     int mel_id = -1;
     std::vector<float> own;
@@ -215,6 +221,7 @@ ud_status ud_streamer_push_audio(ud_streamer* s, int n, const ud_streamer_id* id
         const float* f = out.data() + static_cast<size_t>(i) * cap * bins;
         r.own.insert(r.own.end(), f, f + static_cast<size_t>(frames[i]) * bins);
         r.avail += frames[i];
+        r.samples += n_samples[i];
         if (fin[i]) r.last = true;
     }
     return UD_OK;
@@ -278,17 +285,23 @@ ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
         ++n;
     }
     if (n > 0) {
+        const auto t0 = std::chrono::steady_clock::now();
         ud_status st = ud_step_batch(s->e, n, s->ids.data(), s->mels.data(), s->rows.data(), s->valid.data(),
                                      s->keep.data(), s->decode ? nullptr : s->proj.data(), s->frames.data(),
                                      s->decode ? s->toks.data() : nullptr, s->decode ? s->ntok.data() : nullptr);
         if (st != UD_OK) return st;
+        const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         const size_t tok_stride = static_cast<size_t>(s->cfg.max_chunk_frames) * s->cfg.max_symbols;
         for (int i = 0; i < n; ++i) {
             StreamRec& r = s->recs[s->who[i]];
             if (s->decode) {
                 const int32_t* t = s->toks.data() + i * tok_stride;
                 r.tokens.insert(r.tokens.end(), t, t + s->ntok[i]);
+                const int64_t seen = r.mel_id != -1 ? r.samples : static_cast<int64_t>(r.avail) * 160;
+                r.emit_samples.insert(r.emit_samples.end(), static_cast<size_t>(s->ntok[i]), seen);
+                r.emit_secs.insert(r.emit_secs.end(), static_cast<size_t>(s->ntok[i]), dt);
             }
+            r.step_secs.push_back(dt);
             r.idx = s->next[i];
             if (s->keep[i]) {   // the final chunk
                 finish(r, s->who[i]);
@@ -322,6 +335,29 @@ ud_status ud_streamer_tokens(ud_streamer* s, ud_streamer_id id, int32_t* out, in
     if (out && cap > 0) std::memcpy(out, r->tokens.data(), sizeof(int32_t) * static_cast<size_t>(n < cap ? n : cap));
     if (n_tokens) *n_tokens = n;
     if (finished) *finished = r->finished ? 1 : 0;
+    return UD_OK;
+}
+
+ud_status ud_streamer_emissions(ud_streamer* s, ud_streamer_id id, int32_t* tokens, int64_t* samples_seen,
+                                double* compute_seconds, int cap, int* n) {
+    StreamRec* r = rec_of(s, id);
+    if (!r) return ud::host_fail(UD_ERR_NO_STREAM, "unknown streamer id");
+    if (!n) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL count");
+    const size_t k = r->tokens.size(), m = cap > 0 ? std::min(k, static_cast<size_t>(cap)) : 0;
+    if (tokens && m) std::memcpy(tokens, r->tokens.data(), sizeof(int32_t) * m);
+    if (samples_seen && m) std::memcpy(samples_seen, r->emit_samples.data(), sizeof(int64_t) * m);
+    if (compute_seconds && m) std::memcpy(compute_seconds, r->emit_secs.data(), sizeof(double) * m);
+    *n = static_cast<int>(k);
+    return UD_OK;
+}
+
+ud_status ud_streamer_step_times(ud_streamer* s, ud_streamer_id id, double* out, int cap, int* n) {
+    StreamRec* r = rec_of(s, id);
+    if (!r) return ud::host_fail(UD_ERR_NO_STREAM, "unknown streamer id");
+    if (!n) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL count");
+    const size_t k = r->step_secs.size(), m = cap > 0 ? std::min(k, static_cast<size_t>(cap)) : 0;
+    if (out && m) std::memcpy(out, r->step_secs.data(), sizeof(double) * m);
+    *n = static_cast<int>(k);
     return UD_OK;
 }
 

@@ -42,7 +42,7 @@ ABI_SYMBOLS = [
     "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
     "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
-    "ud_streamer_release", "ud_streamer_set_end_padding", "ud_streamer_open_audio", "ud_streamer_push_audio", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
+    "ud_streamer_release", "ud_streamer_emissions", "ud_streamer_step_times", "ud_streamer_set_end_padding", "ud_streamer_open_audio", "ud_streamer_push_audio", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
     "ud_mel_stream_open", "ud_mel_stream_close", "ud_mel_push_batch", "ud_detok_create", "ud_detok_create_file",
     "ud_detok_destroy", "ud_detok_size", "ud_detok_decode",
 ]
@@ -119,6 +119,8 @@ def lib() -> C.CDLL:
             "ud_streamer_step": (I, [VP, P(I), P(I)]),
             "ud_streamer_finished": (I, [VP, P(C.c_int32), I, P(I)]),
             "ud_streamer_tokens": (I, [VP, C.c_int32, P(C.c_int32), I, P(I), P(I)]),
+            "ud_streamer_emissions": (I, [VP, C.c_int32, P(C.c_int32), P(C.c_int64), P(C.c_double), I, P(I)]),
+            "ud_streamer_step_times": (I, [VP, C.c_int32, P(C.c_double), I, P(I)]),
             "ud_streamer_release": (I, [VP, C.c_int32]),
             "ud_streamer_set_end_padding": (I, [VP, I]),
             "ud_streamer_open_audio": (I, [VP, VP, P(C.c_int32)]),
@@ -491,6 +493,24 @@ class Streamer:
         out = np.zeros(max(1, n.value), np.int32)
         check(lib().ud_streamer_tokens(self.h, sid, _ptr(out, C.c_int32), n.value, C.byref(n), C.byref(fin)))
         return out[:n.value].tolist(), bool(fin.value)
+
+    def emissions(self, sid: int) -> list[tuple[int, int, float]]:
+        """ud_streamer_emissions: (token, samples_seen, compute_seconds) per token (the reference's Emission)."""
+        n = C.c_int()
+        check(lib().ud_streamer_emissions(self.h, sid, None, None, None, 0, C.byref(n)))
+        k = max(1, n.value)
+        t, ss, cs = np.zeros(k, np.int32), np.zeros(k, np.int64), np.zeros(k, np.float64)
+        check(lib().ud_streamer_emissions(self.h, sid, _ptr(t, C.c_int32), _ptr(ss, C.c_int64), _ptr(cs, C.c_double),
+                                          n.value, C.byref(n)))
+        return [(int(t[i]), int(ss[i]), float(cs[i])) for i in range(n.value)]
+
+    def step_times(self, sid: int) -> list[float]:
+        """ud_streamer_step_times: wall seconds of each step the stream took part in (wallTimes)."""
+        n = C.c_int()
+        check(lib().ud_streamer_step_times(self.h, sid, None, 0, C.byref(n)))
+        out = np.zeros(max(1, n.value), np.float64)
+        check(lib().ud_streamer_step_times(self.h, sid, _ptr(out, C.c_double), n.value, C.byref(n)))
+        return out[:n.value].tolist()
 
     def release(self, sid: int):
         check(lib().ud_streamer_release(self.h, sid))
