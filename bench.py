@@ -465,8 +465,10 @@ def run_streamer_bench(args, world, rank, local):
     200/s per GPU in audio time (a step advances every stream by one 0.56 s chunk), last U[2 s, 60 s], wait in a
     queue for a free slot, and leave when their final chunk (keepAll) has run; greedy RNN-T decoding runs on
     every kept frame with each stream's carried decoder state. Each stream's mel is a window of a seeded N(0,1)
-    host pool, all of it available at admission. Timing is the host wall clock around synchronous streamer steps
-    (host rows in, tokens out), max over ranks; value = stream-steps of all ranks per second."""
+    host pool, all of it available at admission. The streamer is pipelined (ud_streamer_set_pipelined: a step's
+    host-side chunk gathering and copies overlap the previous step's device work; `--c4-sync` for synchronous
+    steps). Timing is the host wall clock around the streamer steps (host rows in, tokens out), max over ranks;
+    value = stream-steps of all ranks per second."""
     import ud
     from ud_synthetic import NEMOTRON, make_weights
 
@@ -485,6 +487,7 @@ def run_streamer_bench(args, world, rank, local):
     sd["joint.joint_net.2.bias"][NEMOTRON.blank] += args.blank_offset
     eng.load_weights(sd)
     st = ud.Streamer(eng, R, decode=True)
+    st.set_pipelined(not args.c4_sync)
     rng = np.random.default_rng(1000 + rank)
     pool = np.random.default_rng(rank).standard_normal((64 * 60 * fps, MEL), dtype=np.float32)
     queue: list[int] = []          # lengths in rows of waiting streams
@@ -547,7 +550,8 @@ def run_streamer_bench(args, world, rank, local):
                                      "stream_steps_per_step": all_steps / max(1, args.steps) / world,
                                      "admitted": stats["admitted"], "finished": stats["finished"],
                                      "tokens": stats["tokens"], "queue": len(queue),
-                                     "timing": "host wall clock, synchronous streamer steps (host mel in, tokens out)",
+                                     "timing": "host wall clock, " + ("synchronous" if args.c4_sync else "pipelined") +
+                                               " streamer steps (host mel in, tokens out)",
                                      "parallelism": f"stream-sharded x{world}, no collectives"},
                           "gpu_launches": launches,
                           "kernel_ms_per_step": {k: round(v[0] / 3, 4) for k, v in prof.items() if v[1]},
@@ -655,6 +659,7 @@ def main():
     ap.add_argument("--mel-streams", type=int, default=512, help="mel: utterances per GPU step")
     ap.add_argument("--mel-seconds", type=float, default=10.0, help="mel: seconds of audio per utterance")
     ap.add_argument("--c4-streams", type=int, default=512, help="c4: stream slots per GPU")
+    ap.add_argument("--c4-sync", action="store_true", help="c4: synchronous streamer steps instead of pipelined")
     ap.add_argument("--blank-offset", type=float, default=1.0,
                     help="c2/c4: added to the joint's blank bias. With N(0,0.02) weights greedy decoding emits the "
                          "10-symbol maximum on every frame below about 0.5 and no symbol from 1.0 up; 1.0 (the "

@@ -296,6 +296,12 @@ UD_API ud_status ud_streamer_push_audio(ud_streamer* s, int n, const ud_streamer
 /* One batched step (at most max_batch streams, in order of id); *n_stepped streams advanced one chunk,
  * *n_finished of them ran their final chunk (or ended with nothing left to encode). */
 UD_API ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished);
+/* Pipelined steps (a decoding streamer only; off by default): each ud_streamer_step issues its batch with
+ * ud_step_batch_async from pinned staging buffers and takes in the results of the step before it, so the
+ * host's chunk gathering and the copies overlap the device's work. A step's tokens, emission records and
+ * finished streams appear one ud_streamer_step later (a step with no ready stream only completes the one in
+ * flight). Token sequences are those of the synchronous mode. Turning it off completes the step in flight. */
+UD_API ud_status ud_streamer_set_pipelined(ud_streamer* s, int on);
 /* The ids of the streams that finished in the last ud_streamer_step (up to cap copied) and their count. */
 UD_API ud_status ud_streamer_finished(ud_streamer* s, ud_streamer_id* out, int cap, int* n);
 /* Tokens so far (up to cap copied), the total count, and whether the stream has finished. */

@@ -62,11 +62,12 @@ def _oracle_tokens(sd, dims, mel: np.ndarray, end_padding: bool = True) -> list[
     return toks
 
 
-def _run(eng, mels, live: bool, seed: int = 0, end_padding: bool = True) -> list[list[int]]:
+def _run(eng, mels, live: bool, seed: int = 0, end_padding: bool = True, pipelined: bool = False) -> list[list[int]]:
     """Admits streams as slots allow (4 of them), feeds them buffered or in random increments, steps until all
     are done; returns tokens per stream in input order."""
     s = ud.Streamer(eng, R, decode=True)
     s.set_end_padding(end_padding)
+    s.set_pipelined(pipelined)
     rng = random.Random(seed)
     try:
         pending = list(range(len(mels)))
@@ -117,6 +118,45 @@ def test_live_increments_equal_buffered(model):
     assert _run(eng, mels, live=True, seed=3) == _run(eng, mels, live=False)
 
 
+@pytest.mark.parametrize("live", [False, True], ids=["buffered", "live"])
+def test_pipelined_steps_equal_synchronous(model, live):
+    """ud_streamer_set_pipelined: every stream's tokens equal the synchronous streamer's (results arrive a step
+    later; admission, live feeding and release follow them)."""
+    eng, _, _ = model
+    mels = _mels()
+    assert _run(eng, mels, live=live, seed=4, pipelined=True) == _run(eng, mels, live=live, seed=4)
+
+
+def test_pipelined_release_of_a_stream_in_flight(model):
+    """Releasing a stream whose chunk is in flight completes that step first; the other streams' tokens are
+    unchanged, and a stream finished by that completion is reported by the next step."""
+    eng, _, _ = model
+    mels = _mels()[:3]
+    ref = _run(eng, mels, live=False)
+    s = ud.Streamer(eng, R, decode=True)
+    s.set_pipelined(True)
+    try:
+        ids = [s.open(m) for m in mels]
+        for sid, m in zip(ids, mels):
+            s.push(sid, len(m), last=True)
+        s.step()                  # step 0 in flight
+        s.release(ids[1])         # in that step: it completes first
+        out, seen_done = {}, set()
+        for _ in range(200):
+            s.step()
+            seen_done |= set(s.finished())
+            for k in (0, 2):
+                toks, fin = s.tokens(ids[k])
+                if fin:
+                    out[k] = toks
+            if len(out) == 2:
+                break
+        assert out[0] == ref[0] and out[2] == ref[2]
+        assert {ids[0], ids[2]} <= seen_done
+    finally:
+        s.close()
+
+
 def test_admission_is_a_status_and_slots_are_reused(model):
     eng, _, _ = model
     s = ud.Streamer(eng, R, decode=True)
@@ -144,8 +184,9 @@ def _audio(n, seed):
                                                                                     dtype=torch.float64)).float().numpy()
 
 
-def _run_audio(eng, fe, audios, sizes=None, seed=0):
+def _run_audio(eng, fe, audios, sizes=None, seed=0, pipelined=False):
     s = ud.Streamer(eng, R, decode=True)
+    s.set_pipelined(pipelined)
     rng = random.Random(seed)
     try:
         ids = [s.open_audio(fe) for _ in audios]
@@ -195,5 +236,6 @@ def test_audio_streams_match_the_oracle_pipeline(model):
         assert any(len(t) > 0 for t, _ in got)
         live = _run_audio(eng, fe, audios, sizes=[1, 160, 333, 1600, 4000], seed=5)
         assert live == got
+        assert _run_audio(eng, fe, audios, sizes=[1, 160, 333, 1600, 4000], seed=5, pipelined=True) == got
     finally:
         fe.close()

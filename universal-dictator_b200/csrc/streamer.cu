@@ -16,6 +16,8 @@
 // flush(), :95-107), whose rows the streamer keeps only as far back as the pre-encode cache needs.
 //
 // Only the public C ABI of the engine and the mel frontend is used.
+#include <cuda_runtime.h>
+
 #include <algorithm>
 #include <chrono>
 #include <cstddef>
@@ -34,6 +36,7 @@ constexpr int kPreEncodeCache = 9;   // NemotronSchedule.swift:7-16
 
 struct StreamRec {
     bool used = false, finished = false, last = false;
+    bool final_issued = false;      // pipelined: the final chunk is in flight
     const float* mel = nullptr;     // caller-owned rows [capacity, mel_bins] (mel streams)
     int capacity = 0, avail = 0, idx = 0;
     ud_stream_id slot = -1;
@@ -67,6 +70,22 @@ struct ud_streamer {
     std::vector<float> proj;
     std::vector<int32_t> toks;
     std::vector<ud_streamer_id> just_finished;   // ids that finished in the last step
+    std::vector<ud_streamer_id> carry;           // finished by a release between steps: reported by the next step
+    // Pipelined mode (ud_streamer_set_pipelined): chunk rows staged in pinned buffers at a fixed stride, tokens
+    // copied back into pinned buffers, both double-buffered; a step's results are taken in by the next call.
+    int pipelined = 0;
+    int buf = 0;
+    size_t stage_rows = 0;
+    float* stage[2] = {};
+    int32_t* ptoks[2] = {};
+    int* pntok[2] = {};
+    struct Pending {
+        bool active = false;
+        int b = 0;
+        std::vector<int> who, keep;
+        std::vector<int64_t> seen;
+        std::chrono::steady_clock::time_point t0;
+    } pend;
 };
 
 extern "C" {
@@ -133,9 +152,15 @@ ud_status ud_streamer_set_end_padding(ud_streamer* s, int on) {
 
 ud_status ud_streamer_destroy(ud_streamer* s) {
     if (!s) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL streamer");
+    if (s->pend.active) ud_step_sync(s->e);   // the step in flight reads the pinned stage
     for (StreamRec& r : s->recs) {
         if (r.used && !r.finished && r.slot >= 0) ud_stream_close(s->e, r.slot);
         if (r.used && r.mel_id >= 0 && s->mel) ud_mel_stream_close(s->mel, r.mel_id);
+    }
+    for (int b = 0; b < 2; ++b) {
+        if (s->stage[b]) cudaFreeHost(s->stage[b]);
+        if (s->ptoks[b]) cudaFreeHost(s->ptoks[b]);
+        if (s->pntok[b]) cudaFreeHost(s->pntok[b]);
     }
     delete s;
     return UD_OK;
@@ -239,37 +264,119 @@ ud_status ud_streamer_push(ud_streamer* s, ud_streamer_id id, int n_rows, int la
     return UD_OK;
 }
 
+// Frees a finished stream's engine slot and frontend stream.
+static void finish_rec(ud_streamer* s, StreamRec& r, int id, int* done) {
+    ud_stream_close(s->e, r.slot);
+    if (r.mel_id >= 0) {
+        ud_mel_stream_close(s->mel, r.mel_id);
+        r.mel_id = -2;   // an audio stream whose frontend stream is closed
+        std::vector<float>().swap(r.own);
+    }
+    r.finished = true;
+    s->just_finished.push_back(id);
+    ++*done;
+}
+
+// Keeps only the pre-encode cache window of an audio stream's rows.
+static void trim_audio(ud_streamer* s, StreamRec& r) {
+    const size_t bins = static_cast<size_t>(s->cfg.mel_bins);
+    const int keep_from = r.idx - kPreEncodeCache;
+    if (r.mel_id >= 0 && keep_from > r.own_start) {
+        const size_t drop = std::min(r.own.size(), static_cast<size_t>(keep_from - r.own_start) * bins);
+        r.own.erase(r.own.begin(), r.own.begin() + static_cast<std::ptrdiff_t>(drop));
+        r.own_start = keep_from;
+    }
+}
+
+// Appends one completed step's tokens and records to its streams; finishes those whose final chunk it was.
+static void take_results(ud_streamer* s, int n, const int* who, const int* keep, const int64_t* seen,
+                         const int32_t* toks, const int* ntok, double dt, int* done) {
+    const size_t tok_stride = static_cast<size_t>(s->cfg.max_chunk_frames) * s->cfg.max_symbols;
+    for (int i = 0; i < n; ++i) {
+        StreamRec& r = s->recs[who[i]];
+        if (s->decode) {
+            const int32_t* t = toks + i * tok_stride;
+            r.tokens.insert(r.tokens.end(), t, t + ntok[i]);
+            r.emit_samples.insert(r.emit_samples.end(), static_cast<size_t>(ntok[i]), seen[i]);
+            r.emit_secs.insert(r.emit_secs.end(), static_cast<size_t>(ntok[i]), dt);
+        }
+        r.step_secs.push_back(dt);
+        if (keep[i]) finish_rec(s, r, who[i], done);
+    }
+}
+
+// Pipelined mode: takes in the results of the step in flight (its device work is complete).
+static void take_pending(ud_streamer* s, int* done) {
+    ud_streamer::Pending& p = s->pend;
+    if (!p.active) return;
+    const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - p.t0).count();
+    take_results(s, static_cast<int>(p.who.size()), p.who.data(), p.keep.data(), p.seen.data(), s->ptoks[p.b],
+                 s->pntok[p.b], dt, done);
+    p.active = false;
+}
+
+static ud_status pipeline_setup(ud_streamer* s) {
+    if (s->stage[0]) return UD_OK;
+    const size_t B = static_cast<size_t>(s->cfg.max_batch);
+    s->stage_rows = static_cast<size_t>(kPreEncodeCache + 8 + 8 * s->lookahead);   // the longest chunk
+    const size_t tok_n = B * s->cfg.max_chunk_frames * s->cfg.max_symbols;
+    for (int b = 0; b < 2; ++b) {
+        if (cudaMallocHost(&s->stage[b], sizeof(float) * B * s->stage_rows * s->cfg.mel_bins) != cudaSuccess ||
+            cudaMallocHost(&s->ptoks[b], sizeof(int32_t) * (tok_n > 0 ? tok_n : 1)) != cudaSuccess ||
+            cudaMallocHost(&s->pntok[b], sizeof(int) * B) != cudaSuccess) {
+            cudaGetLastError();
+            return ud::host_fail(UD_ERR_OUT_OF_MEMORY, "pinned streamer staging");
+        }
+    }
+    return UD_OK;
+}
+
+ud_status ud_streamer_set_pipelined(ud_streamer* s, int on) {
+    if (!s) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL streamer");
+    if (!on && s->pipelined) {   // complete the step in flight before leaving the mode
+        ud_status st = ud_step_sync(s->e);
+        if (st != UD_OK) return st;
+        int done = 0;
+        take_pending(s, &done);
+    }
+    if (on) {
+        if (!s->decode) return ud::host_fail(UD_ERR_UNSUPPORTED, "the pipelined streamer decodes");
+        ud_status st = pipeline_setup(s);
+        if (st != UD_OK) return st;
+    }
+    s->pipelined = on ? 1 : 0;
+    return UD_OK;
+}
+
 ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
     if (!s) return ud::host_fail(UD_ERR_INVALID_ARGUMENT, "NULL streamer");
     int n = 0, done = 0;
     const size_t bins = static_cast<size_t>(s->cfg.mel_bins);
     const size_t pad_rows = kPreEncodeCache + 8;
-    s->just_finished.clear();
-    auto finish = [&](StreamRec& r, int id) {   // frees the engine slot and the frontend stream
-        ud_stream_close(s->e, r.slot);
-        if (r.mel_id >= 0) {
-            ud_mel_stream_close(s->mel, r.mel_id);
-            r.mel_id = -2;   // an audio stream whose frontend stream is closed
-            std::vector<float>().swap(r.own);
-        }
-        r.finished = true;
-        s->just_finished.push_back(id);
-        ++done;
-    };
+    const bool pipe = s->pipelined != 0;
+    const int sb = s->buf;
+    std::vector<int64_t> seen;
+    s->just_finished.swap(s->carry);
+    s->carry.clear();
     for (int id = 0; id < static_cast<int>(s->recs.size()) && n < s->cfg.max_batch; ++id) {
         StreamRec& r = s->recs[id];
-        if (!r.used || r.finished) continue;
+        if (!r.used || r.finished || r.final_issued) continue;
         int start, rows, valid, keep, nxt;
         const int c = ud_chunk_next(s->lookahead, r.idx, r.avail, r.last ? 1 : 0, s->end_padding, &start, &rows,
                                     &valid, &keep, &nxt);
         if (c == 0) continue;
         if (c < 0) {   // nothing left, or a tail too short to encode without end padding: the stream ends here
-            finish(r, id);
+            finish_rec(s, r, id, &done);
             continue;
         }
         const float* src = r.mel_id != -1 ? r.own.data() + static_cast<size_t>(start - r.own_start) * bins
                                           : r.mel + static_cast<size_t>(start) * bins;
-        if (rows > valid) {   // a padded final tail: the valid rows, then zero rows
+        if (pipe) {   // the rows into the pinned stage at a fixed stride, a padded tail's zero rows included
+            float* dst = s->stage[sb] + static_cast<size_t>(n) * s->stage_rows * bins;
+            std::memcpy(dst, src, sizeof(float) * valid * bins);
+            if (rows > valid) std::memset(dst + static_cast<size_t>(valid) * bins, 0, sizeof(float) * (rows - valid) * bins);
+            src = dst;
+        } else if (rows > valid) {   // a padded final tail: the valid rows, then zero rows
             float* dst = s->pad.data() + static_cast<size_t>(n) * pad_rows * bins;
             std::memcpy(dst, src, sizeof(float) * valid * bins);
             std::memset(dst + static_cast<size_t>(valid) * bins, 0, sizeof(float) * (rows - valid) * bins);
@@ -282,37 +389,49 @@ ud_status ud_streamer_step(ud_streamer* s, int* n_stepped, int* n_finished) {
         s->keep[n] = keep;
         s->who[n] = id;
         s->next[n] = nxt;
+        seen.push_back(r.mel_id != -1 ? r.samples : static_cast<int64_t>(r.avail) * 160);
         ++n;
     }
-    if (n > 0) {
+    if (pipe) {
+        // Issue this step; the call returns once the step before it is complete, whose results are taken in.
+        if (n > 0) {
+            const auto t0 = std::chrono::steady_clock::now();
+            ud_status st = ud_step_batch_async(s->e, n, s->ids.data(), s->mels.data(), s->rows.data(),
+                                               s->valid.data(), s->keep.data(), nullptr, s->frames.data(),
+                                               s->ptoks[sb], s->pntok[sb]);
+            if (st != UD_OK) return st;
+            take_pending(s, &done);
+            ud_streamer::Pending& p = s->pend;
+            p.active = true;
+            p.b = sb;
+            p.who.assign(s->who.begin(), s->who.begin() + n);
+            p.keep.assign(s->keep.begin(), s->keep.begin() + n);
+            p.seen = seen;
+            p.t0 = t0;
+            s->buf ^= 1;
+            for (int i = 0; i < n; ++i) {
+                StreamRec& r = s->recs[s->who[i]];
+                r.idx = s->next[i];
+                if (s->keep[i]) r.final_issued = true;
+                else trim_audio(s, r);   // the chunk's rows are in the stage already
+            }
+        } else if (s->pend.active) {
+            ud_status st = ud_step_sync(s->e);
+            if (st != UD_OK) return st;
+            take_pending(s, &done);
+        }
+    } else if (n > 0) {
         const auto t0 = std::chrono::steady_clock::now();
         ud_status st = ud_step_batch(s->e, n, s->ids.data(), s->mels.data(), s->rows.data(), s->valid.data(),
                                      s->keep.data(), s->decode ? nullptr : s->proj.data(), s->frames.data(),
                                      s->decode ? s->toks.data() : nullptr, s->decode ? s->ntok.data() : nullptr);
         if (st != UD_OK) return st;
         const double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-        const size_t tok_stride = static_cast<size_t>(s->cfg.max_chunk_frames) * s->cfg.max_symbols;
+        for (int i = 0; i < n; ++i) s->recs[s->who[i]].idx = s->next[i];
+        take_results(s, n, s->who.data(), s->keep.data(), seen.data(), s->toks.data(), s->ntok.data(), dt, &done);
         for (int i = 0; i < n; ++i) {
             StreamRec& r = s->recs[s->who[i]];
-            if (s->decode) {
-                const int32_t* t = s->toks.data() + i * tok_stride;
-                r.tokens.insert(r.tokens.end(), t, t + s->ntok[i]);
-                const int64_t seen = r.mel_id != -1 ? r.samples : static_cast<int64_t>(r.avail) * 160;
-                r.emit_samples.insert(r.emit_samples.end(), static_cast<size_t>(s->ntok[i]), seen);
-                r.emit_secs.insert(r.emit_secs.end(), static_cast<size_t>(s->ntok[i]), dt);
-            }
-            r.step_secs.push_back(dt);
-            r.idx = s->next[i];
-            if (s->keep[i]) {   // the final chunk
-                finish(r, s->who[i]);
-            } else if (r.mel_id >= 0) {   // keep only the pre-encode cache window of an audio stream
-                const int keep_from = r.idx - kPreEncodeCache;
-                if (keep_from > r.own_start) {
-                    const size_t drop = std::min(r.own.size(), static_cast<size_t>(keep_from - r.own_start) * bins);
-                    r.own.erase(r.own.begin(), r.own.begin() + static_cast<std::ptrdiff_t>(drop));
-                    r.own_start = keep_from;
-                }
-            }
+            if (!r.finished) trim_audio(s, r);
         }
     }
     if (n_stepped) *n_stepped = n;
@@ -364,6 +483,18 @@ ud_status ud_streamer_step_times(ud_streamer* s, ud_streamer_id id, double* out,
 ud_status ud_streamer_release(ud_streamer* s, ud_streamer_id id) {
     StreamRec* r = rec_of(s, id);
     if (!r) return ud::host_fail(UD_ERR_NO_STREAM, "unknown streamer id");
+    if (s->pend.active && std::find(s->pend.who.begin(), s->pend.who.end(), id) != s->pend.who.end()) {
+        // the stream is in the step in flight: complete that step first; streams it finishes are reported by
+        // the next ud_streamer_step
+        ud_status st = ud_step_sync(s->e);
+        if (st != UD_OK) return st;
+        const size_t before = s->just_finished.size();
+        int done = 0;
+        take_pending(s, &done);
+        s->carry.insert(s->carry.end(), s->just_finished.begin() + static_cast<std::ptrdiff_t>(before),
+                        s->just_finished.end());
+        s->just_finished.resize(before);
+    }
     if (!r->finished && r->slot >= 0) ud_stream_close(s->e, r->slot);
     if (r->mel_id >= 0) ud_mel_stream_close(s->mel, r->mel_id);
     *r = StreamRec();

@@ -42,7 +42,8 @@ ABI_SYMBOLS = [
     "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
     "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
-    "ud_streamer_release", "ud_streamer_emissions", "ud_streamer_step_times", "ud_streamer_set_end_padding", "ud_streamer_open_audio", "ud_streamer_push_audio", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
+    "ud_streamer_release", "ud_streamer_emissions", "ud_streamer_step_times", "ud_streamer_set_end_padding",
+    "ud_streamer_set_pipelined", "ud_streamer_open_audio", "ud_streamer_push_audio", "ud_mel_create", "ud_mel_destroy", "ud_mel_features", "ud_mel_features_device",
     "ud_mel_stream_open", "ud_mel_stream_close", "ud_mel_push_batch", "ud_detok_create", "ud_detok_create_file",
     "ud_detok_destroy", "ud_detok_size", "ud_detok_decode",
 ]
@@ -123,6 +124,7 @@ def lib() -> C.CDLL:
             "ud_streamer_step_times": (I, [VP, C.c_int32, P(C.c_double), I, P(I)]),
             "ud_streamer_release": (I, [VP, C.c_int32]),
             "ud_streamer_set_end_padding": (I, [VP, I]),
+            "ud_streamer_set_pipelined": (I, [VP, I]),
             "ud_streamer_open_audio": (I, [VP, VP, P(C.c_int32)]),
             "ud_streamer_push_audio": (I, [VP, I, P(C.c_int32), P(P(F)), P(I), P(I)]),
             "ud_mel_create": (I, [eng, P(F), I, P(F), I, P(VP)]),
@@ -457,6 +459,11 @@ class Streamer:
 
     def set_end_padding(self, on: bool):
         check(lib().ud_streamer_set_end_padding(self.h, int(on)))
+
+    def set_pipelined(self, on: bool):
+        """ud_streamer_set_pipelined: each step's results appear one step later; the copies and the host's
+        chunk gathering overlap the device's work."""
+        check(lib().ud_streamer_set_pipelined(self.h, int(on)))
 
     def open_audio(self, frontend: "MelFrontend") -> int:
         """An audio stream whose mel comes from `frontend` (NemotronStreamer.push(samples:))."""
