@@ -589,7 +589,8 @@ def run_gemm_bench(args, local):
         A = (torch.randn(M, K, device=dev, generator=gen) * 0.5).bfloat16()
         Ws = [(torch.randn(N, K, device=dev, generator=gen) * 0.03).bfloat16() for _ in range(24)]
         R = torch.randn(M, N, device=dev, generator=gen) if res else None
-        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16 if obf else torch.float32)
+        # residual shapes in place (x += s * f(h W^T)), as the encoder runs them
+        out = R if res else torch.empty(M, N, device=dev, dtype=torch.bfloat16 if obf else torch.float32)
         torch.cuda.synchronize()
 
         def call(i):
