@@ -1,10 +1,11 @@
 #!/usr/bin/env python
 """Benchmark: stream-steps/s of the cache-aware streaming 24-layer FastConformer encoder step on B200.
 
-Workload ("C3"): per GPU, 256 synchronous streams at attention context [70,13]
-(T = 14 encoder frames per step from 121-row mel chunks, 105 rows for a stream's first chunk), bf16, the full
-step of the reference's NemotronStreamer.step: subsampling, 24 conformer layers over the paged K/V / conv caches,
-the joint encoder projection, and greedy RNN-T decoding of the kept frames with carried decoder state.
+Workload (configuration C3 of the benchmark): per GPU, 256 synchronous streams at attention context [70,13]
+(T = 14 encoder frames per step from 121-row mel chunks, 105 rows for a stream's first chunk), bf16, the encoder
+step of the reference's NemotronStreamer.step: subsampling, 24 conformer layers over the paged K/V / conv caches
+and the joint encoder projection (`--decode` adds greedy RNN-T decoding of the kept frames with carried decoder
+state).
 Synthetic data: each stream's 30 s of N(0,1) 128-bin mel (seed = stream id); weights N(0, 0.02), seed 0.
 One bench "step" = one batched step of all streams on a GPU; `value` = streams x steps x GPUs / max-over-ranks
 device time. Scaling is weak (256 streams per GPU); GPUs share nothing (no collectives on the data path).
