@@ -194,6 +194,7 @@ UD_API ud_status ud_stream_info(ud_engine* e, ud_stream_id id, int* cache_len, i
 /* Engine facts: the CUDA stream (cudaStream_t) work is issued on, free pages, element size. */
 UD_API ud_status ud_get_cuda_stream(ud_engine* e, void** stream_out);
 UD_API ud_status ud_pool_info(ud_engine* e, int* free_pages, int* total_pages, int* elem_bytes);
+/* Waits for the engine's work, pipelined steps (ud_step_batch_async) included; reports a device error. */
 UD_API ud_status ud_synchronize(ud_engine* e);
 /* Number of this library's kernels launched on the engine since init (counts graph replays' kernels). */
 UD_API ud_status ud_launch_count(ud_engine* e, int64_t* out);

@@ -1832,6 +1832,7 @@ ud_status ud_synchronize(ud_engine* e) {
     if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
     UD_CK(cudaSetDevice(e->device));
     UD_CK(cudaGetLastError());
+    UD_TRY(drain_async(e));   // pipelined steps complete too
     return check_device_error(e);
 }
 
