@@ -148,6 +148,35 @@ def test_sync_calls_after_async_ones_drain_the_pipeline(model):
         model.close_stream(sid)
 
 
+def test_async_projections_only(model):
+    """Without token buffers the pipelined step returns the projections alone, equal to ud_step_batch's."""
+    mels = _mels()[:2]
+    tm, W = model.cfg.max_chunk_frames, model.out_width
+    ids_a = [model.open(R) for _ in mels]
+    ids_b = [model.open(R) for _ in mels]
+    outs = [torch.empty(2, tm, W, pin_memory=True).numpy() for _ in range(2)]
+    plans = [list(chunk_plan(len(m), R)) for m in mels]
+    steps = min(len(p) for p in plans)
+    pending = None
+    for k in range(steps):
+        chunks = [np.ascontiguousarray(m[p[k][0]:p[k][0] + p[k][1]].numpy()) for m, p in zip(mels, plans)]
+        args = ([p[k][1] for p in plans], [p[k][2] for p in plans], [p[k][3] for p in plans])
+        projs, frames, _ = model.step_batch(ids_a, chunks, *args)
+        fr = model.step_batch_async(ids_b, chunks, *args, outs[k % 2])
+        assert fr == frames
+        if pending is not None:
+            pk, pprojs, pfr = pending
+            for j in range(2):
+                assert np.array_equal(outs[pk % 2][j, :pfr[j]], pprojs[j])
+        pending = (k, [p.copy() for p in projs], frames)
+    model.step_sync()
+    pk, pprojs, pfr = pending
+    for j in range(2):
+        assert np.array_equal(outs[pk % 2][j, :pfr[j]], pprojs[j])
+    for sid in ids_a + ids_b:
+        model.close_stream(sid)
+
+
 def test_rejected_async_call_is_a_status(model):
     tm, W = model.cfg.max_chunk_frames, model.out_width
     out = torch.empty(1, tm, W, pin_memory=True).numpy()

@@ -127,6 +127,30 @@ def test_pipelined_steps_equal_synchronous(model, live):
     assert _run(eng, mels, live=live, seed=4, pipelined=True) == _run(eng, mels, live=live, seed=4)
 
 
+def test_pipelined_mode_switched_off_mid_stream(model):
+    """Leaving the pipelined mode completes the step in flight; the tokens of streams that ran part of their
+    chunks pipelined and the rest synchronously equal the all-synchronous run."""
+    eng, _, _ = model
+    mels = _mels()[:3]
+    ref = _run(eng, mels, live=False)
+    s = ud.Streamer(eng, R, decode=True)
+    try:
+        s.set_pipelined(True)
+        ids = [s.open(m) for m in mels]
+        for sid, m in zip(ids, mels):
+            s.push(sid, len(m), last=True)
+        s.step()
+        s.step()
+        s.set_pipelined(False)
+        for _ in range(200):
+            s.step()
+            if all(s.tokens(i)[1] for i in ids):
+                break
+        assert [s.tokens(i)[0] for i in ids] == ref
+    finally:
+        s.close()
+
+
 def test_pipelined_release_of_a_stream_in_flight(model):
     """Releasing a stream whose chunk is in flight completes that step first; the other streams' tokens are
     unchanged, and a stream finished by that completion is reported by the next step."""
