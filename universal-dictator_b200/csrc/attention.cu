@@ -512,12 +512,8 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
     if constexpr (std::is_same<T, bf16>::value) {
         if (tmax_batch <= tc::TM && cg.L + tc::TM <= 128) {
             const tc::Lay lay(cg.L);
-            static size_t tc_attr = 0;
-            if (lay.total > tc_attr) {
-                cudaFuncSetAttribute(tc::attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(lay.total));
-                tc_attr = lay.total;
-            }
+            static size_t tc_attr[kMaxDevices] = {};
+            ensure_dyn_smem(tc::attn_tc_kernel, lay.total, tc_attr);
             dim3 grid(n, n_heads);
             launch_pdl(tc::attn_tc_kernel, dim3(grid), dim3(tc::kAttnThreads), lay.total, s, qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer,
                                                             out, ldo, dev_err);
@@ -525,12 +521,8 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
         }
     }
     const AttnSmem<T> lay(tmax_batch, cg.L);
-    static size_t attr_set = 0;
-    if (lay.total > 48 * 1024 && lay.total > attr_set) {
-        cudaFuncSetAttribute(relpos_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(lay.total));
-        attr_set = lay.total;
-    }
+    static size_t attr_set[kMaxDevices] = {};
+    if (lay.total > 48 * 1024) ensure_dyn_smem(relpos_attn_kernel<T>, lay.total, attr_set);
     dim3 grid(n, n_heads);
     launch_pdl(relpos_attn_kernel<T>, dim3(grid), dim3(256), lay.total, s, qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer, out,
                                                        ldo, tmax_batch, dev_err);

@@ -98,6 +98,24 @@ __device__ __forceinline__ void report_error(int* err, int code) {
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ------------------------------------------------------------------ per-device launch setup
+// A kernel's dynamic shared-memory limit is set on the current device; each device keeps its own record of the
+// largest size set so far (one process may drive engines on several GPUs).
+constexpr int kMaxDevices = 64;
+inline int current_device_index() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return (d >= 0 && d < kMaxDevices) ? d : 0;
+}
+template <typename F>
+inline void ensure_dyn_smem(F* kernel, size_t bytes, size_t (&done)[kMaxDevices]) {
+    const int d = current_device_index();
+    if (bytes > done[d]) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+        done[d] = bytes;
+    }
+}
+
 // ------------------------------------------------------------------ mbarrier (shared::cta)
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -127,12 +127,8 @@ void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, con
                  int n, int tmax_batch, const CacheGeom& cg, int layer, int K, T* out, int ldo, cudaStream_t s) {
     if (n <= 0 || K != 9) return;
     const size_t smem = sizeof(float) * static_cast<size_t>(tmax_batch) * cg.D;
-    static size_t attr_set = 0;
-    if (smem > 48 * 1024 && smem > attr_set) {
-        cudaFuncSetAttribute(conv_module_kernel<T, 9>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
-        attr_set = smem;
-    }
+    static size_t attr_set[kMaxDevices] = {};
+    if (smem > 48 * 1024) ensure_dyn_smem(conv_module_kernel<T, 9>, smem, attr_set);
     launch_pdl(conv_module_kernel<T, 9>, dim3(n), dim3(512), smem, s, pw, ld_pw, dw, ln_g, ln_b, meta, cg, layer, out, ldo);
 }
 

@@ -191,12 +191,8 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(const T* __restrict__ A
 
 template <typename T, int MR, int U>
 void launch_gemv_u(const T* A, int lda, const T* W, int M, int N, int K, const GemmEpilogue& epi, cudaStream_t s) {
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(gemv_kernel<T, MR, kSrcStaged, U>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kGemvStageSmem);
-        attr = true;
-    }
+    static size_t attr[kMaxDevices] = {};
+    ensure_dyn_smem(gemv_kernel<T, MR, kSrcStaged, U>, kGemvStageSmem, attr);
     const dim3 grid((N + kGemvWarps - 1) / kGemvWarps), block(256);
     const size_t smem = static_cast<size_t>(M) * K * sizeof(T);
     if (smem <= static_cast<size_t>(kGemvStageSmem))

@@ -184,11 +184,8 @@ template <int BN>
 void launch(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const GemmEpilogue& epi, int* err,
             int num_sms, cudaStream_t s) {
     using C = TcCfg<BN>;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        attr = true;
-    }
+    static size_t attr[kMaxDevices] = {};
+    ensure_dyn_smem(gemm_tc_kernel<BN>, C::SMEM, attr);
     const int tiles = ((M + BM - 1) / BM) * (N / BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     launch_pdl(gemm_tc_kernel<BN>, dim3(grid), dim3(kThreads), C::SMEM, s, A.map, W.map, M, N, K, epi, err);

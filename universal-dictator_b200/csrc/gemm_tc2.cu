@@ -334,16 +334,14 @@ void launch2(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, const 
              int num_sms, const TmaMatrix* out_map, cudaStream_t s) {
     using C = Tc2Cfg<BN, kEpiReg>;
     using CT = Tc2Cfg<BN, kEpiStoreBf16>;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(gemm_tc2_kernel<BN, kEpiReg>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        cudaFuncSetAttribute(gemm_tc2_kernel<BN, kEpiStoreBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
-        cudaFuncSetAttribute(gemm_tc2_kernel<BN, kEpiAddF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, CT::SMEM);
-        attr = true;
-    }
+    static size_t attr0[kMaxDevices] = {}, attr1[kMaxDevices] = {}, attr2[kMaxDevices] = {};
+    ensure_dyn_smem(gemm_tc2_kernel<BN, kEpiReg>, C::SMEM, attr0);
+    ensure_dyn_smem(gemm_tc2_kernel<BN, kEpiStoreBf16>, CT::SMEM, attr1);
+    ensure_dyn_smem(gemm_tc2_kernel<BN, kEpiAddF32>, CT::SMEM, attr2);
     // Persistent grid: no more pairs than can be resident at once (clusters are placed within GPCs).
-    static int max_pairs = -1;
-    if (max_pairs < 0) {
+    static int max_pairs_dev[kMaxDevices] = {};
+    int& max_pairs = max_pairs_dev[current_device_index()];
+    if (max_pairs <= 0) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(num_sms, 1, 1);
         cfg.blockDim = dim3(kThreads, 1, 1);

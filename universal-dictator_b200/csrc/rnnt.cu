@@ -606,12 +606,8 @@ void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, i
         if (base + per_stream <= kSmemMax) {
             gm.sb = static_cast<int>(std::min<size_t>(16, (kSmemMax - base) / per_stream));
             const size_t smem = base + per_stream * gm.sb;
-            static size_t attr_set = 0;
-            if (smem > attr_set) {
-                cudaFuncSetAttribute(rnnt_lockstep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kSmemMax));
-                attr_set = kSmemMax;
-            }
+            static size_t attr_set[kMaxDevices] = {};
+            ensure_dyn_smem(rnnt_lockstep_kernel, kSmemMax, attr_set);
             cudaMemsetAsync(scr->barrier, 0, sizeof(unsigned long long), s);
             rnnt_lockstep_kernel<<<G, kLsThreads, smem, s>>>(w, st, proj, ld_proj, meta, n, tokens, tok_stride, n_tokens,
                                                              *scr, gm, dev_err);
@@ -619,11 +615,8 @@ void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, i
         }
     }
     const size_t smem = rnnt_smem_bytes(w);
-    static size_t attr_set = 0;
-    if (smem > 48 * 1024 && smem > attr_set) {
-        cudaFuncSetAttribute(rnnt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        attr_set = smem;
-    }
+    static size_t attr_set[kMaxDevices] = {};
+    if (smem > 48 * 1024) ensure_dyn_smem(rnnt_kernel, smem, attr_set);
     launch_pdl(rnnt_kernel, dim3(n), dim3(kThreads), smem, s, w, st, proj, ld_proj, meta, tokens, tok_stride, n_tokens);
 }
 

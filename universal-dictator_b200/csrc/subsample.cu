@@ -299,12 +299,8 @@ template <typename T>
 void sub_dwconv2(const T* in, int Tin, int Fin, const BatchEntry* meta, int n, const float* w, const float* b, T* out,
                  int Tout, int Fout, int C, cudaStream_t s) {
     const size_t smem = sizeof(T) * 3 * static_cast<size_t>(Fin) * C;
-    static size_t attr_set[2] = {0, 0};
-    size_t& cur = attr_set[sizeof(T) == 4 ? 1 : 0];
-    if (smem > 48 * 1024 && smem > cur) {
-        cudaFuncSetAttribute(dwconv2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        cur = smem;
-    }
+    static size_t attr_set[kMaxDevices] = {};   // per instantiation (T) and device
+    if (smem > 48 * 1024) ensure_dyn_smem(dwconv2_kernel<T>, smem, attr_set);
     launch_pdl(dwconv2_kernel<T>, dim3(n, Tout), dim3(256), smem, s, in, Tin, Fin, meta, w, b, out, Tout, Fout, C);
 }
 
