@@ -214,10 +214,12 @@ __global__ void __launch_bounds__(256) relpos_attn_kernel(const T* __restrict__ 
 //   S[i, j] = (AC[i, j] + BDraw[i, (L + i - j) - rel_min]) / sqrt(dk), softmax over visible keys (fp32)
 //   O     = softmax [16 x nk] (bf16) . V [nk x dk]
 // One CTA (16 warps, two CTAs per SM) per (stream, head). A first pass writes each key's source row (cache
-// page or this chunk's QKV row) to a small table, so the copies of K, V and the needed P rows into shared
-// memory (cp.async) need no per-chunk page arithmetic; fragments come from ldmatrix (row stride 136 elements:
-// conflict-free, 16-byte aligned rows). The 13 AC/BD jobs of 16 columns run in one round over the warps, each
-// warp then normalises one query row, and each warp computes 8 output columns of O.
+// page or this chunk's QKV row) to a small table, so the copies of K, V, the needed P rows and the raw queries
+// into shared memory (cp.async) need no per-chunk page arithmetic; the chunk's K/V rows are appended to their
+// pages from the staged copies, so no synchronous global load sits in the CTA's chain. Fragments come from
+// ldmatrix (row stride 136 elements: conflict-free, 16-byte aligned rows). The 13 AC/BD jobs of 16 columns run
+// in one round over the warps, each warp then normalises one query row, and each warp computes 8 output
+// columns of O.
 namespace tc {
 
 constexpr int TM = 16;
@@ -298,6 +300,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
     const int rel_min = L - hi + 1;
     const int np = nk > 0 ? T_ + nk - 1 : 0;
     const int hoff = h * DKk;
+    const int na = L + T_ - lo;   // staged key rows: the visible ones and the chunk's invalid frames (appended too)
     const Lay lay(L);
 
     extern __shared__ __align__(128) uint8_t sm[];
@@ -313,10 +316,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
     const bf16** VP = reinterpret_cast<const bf16**>(sm + lay.vp);
 
     // ---- per-key source rows: cached frame f = head - L + j in its page, or this chunk's row j - L (null when
-    //      the page is not mapped, which is reported and read as zeros)
+    //      the page is not mapped, which is reported and read as zeros). Rows past the visible ones (this chunk's
+    //      invalid frames) are staged for the append; the softmax gives them probability 0.
     const bf16* kpool = reinterpret_cast<const bf16*>(cg.kpool);
     const bf16* vpool = reinterpret_cast<const bf16*>(cg.vpool);
-    for (int r = tid; r < nk; r += kAttnThreads) {
+    for (int r = tid; r < na; r += kAttnThreads) {
         const int j = lo + r;
         const bf16 *ks = nullptr, *vs = nullptr;
         if (j < L) {
@@ -338,9 +342,57 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
         VP[r] = vs;
     }
     __syncthreads();
-    // ---- append this chunk's K/V rows at frames head + t. Those pool rows are not read by this launch (the
-    //      window is frames head - cacheLen .. head - 1, and the 8 page slots hold 128 frames), so the copy is
-    //      issued first and overlaps the staging below.
+    // ---- stage K, P and the raw queries (group 0) and V (group 1) with cp.async; zero the padding rows.
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int idx = tid; idx < na * 16; idx += kAttnThreads) {
+        const int r = idx >> 4, c = (idx & 15) * 8;
+        const bf16* ks = KP[r];
+        if (ks) cp_async16(Ks + r * RSB + c, ks + c);
+        else *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
+    }
+    for (int idx = tid; idx < np * 16; idx += kAttnThreads) {
+        const int r = idx >> 4, c = (idx & 15) * 8;
+        cp_async16(Ps + r * RSB + c, ptab + static_cast<size_t>(rel_min + r + tmax - 1) * D + hoff + c);
+    }
+    for (int idx = tid; idx < TM * 16; idx += kAttnThreads) {   // raw queries into QU (biased in place below)
+        const int i = idx >> 4, c = (idx & 15) * 8;
+        if (i < T_) cp_async16(QU + i * RSB + c, qkv + static_cast<size_t>(row_off + i) * ld_qkv + hoff + c);
+        else *reinterpret_cast<uint4*>(QU + i * RSB + c) = z;
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int idx = tid; idx < na * 16; idx += kAttnThreads) {
+        const int r = idx >> 4, c = (idx & 15) * 8;
+        const bf16* vs = VP[r];
+        if (vs) cp_async16(Vs + r * RSB + c, vs + c);
+        else *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int idx = tid; idx < (lay.nkp - na) * 16; idx += kAttnThreads) {
+        const int r = na + (idx >> 4), c = (idx & 15) * 8;
+        *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
+        *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
+    }
+    for (int idx = tid; idx < (lay.npp - np) * 16; idx += kAttnThreads) {
+        const int r = np + (idx >> 4), c = (idx & 15) * 8;
+        *reinterpret_cast<uint4*>(Ps + r * RSB + c) = z;
+    }
+    asm volatile("cp.async.wait_group 1;" ::: "memory");   // K, P and the queries have landed; V may be in flight
+    __syncthreads();
+    // queries with the position biases, rounded to bf16 (rows >= T are zero), from the raw queries in QU
+    for (int idx = tid; idx < TM * 16; idx += kAttnThreads) {
+        const int i = idx >> 4, c = (idx & 15) * 8;
+        float q[8], a[8], bb[8];
+        load16<bf16>(QU + i * RSB + c, q);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            a[e] = i < T_ ? q[e] + bias_u[hoff + c + e] : 0.f;
+            bb[e] = i < T_ ? q[e] + bias_v[hoff + c + e] : 0.f;
+        }
+        store16<bf16>(QU + i * RSB + c, a);
+        store16<bf16>(QV + i * RSB + c, bb);
+    }
+    // ---- append this chunk's K rows (staged rows L - lo + t) at frames head + t. Those pool rows are not read by
+    //      this launch (the window is frames head - cacheLen .. head - 1, and the 8 page slots hold 128 frames).
     bf16* kw = reinterpret_cast<bf16*>(cg.kpool);
     bf16* vw = reinterpret_cast<bf16*>(cg.vpool);
     for (int idx = tid; idx < T_ * 16; idx += kAttnThreads) {
@@ -352,60 +404,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
             continue;
         }
         const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
-        const bf16* src = qkv + static_cast<size_t>(row_off + t) * ld_qkv + hoff + c;
-        *reinterpret_cast<uint4*>(kw + off) = *reinterpret_cast<const uint4*>(src + D);
-        *reinterpret_cast<uint4*>(vw + off) = *reinterpret_cast<const uint4*>(src + 2 * D);
+        *reinterpret_cast<uint4*>(kw + off) = *reinterpret_cast<const uint4*>(Ks + (L - lo + t) * RSB + c);
     }
-
-    // ---- stage K and P (group 0) and V (group 1) with cp.async; zero the padding rows.
-    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-    for (int idx = tid; idx < nk * 16; idx += kAttnThreads) {
-        const int r = idx >> 4, c = (idx & 15) * 8;
-        const bf16* ks = KP[r];
-        if (ks) cp_async16(Ks + r * RSB + c, ks + c);
-        else *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
-    }
-    for (int idx = tid; idx < np * 16; idx += kAttnThreads) {
-        const int r = idx >> 4, c = (idx & 15) * 8;
-        cp_async16(Ps + r * RSB + c, ptab + static_cast<size_t>(rel_min + r + tmax - 1) * D + hoff + c);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int idx = tid; idx < nk * 16; idx += kAttnThreads) {
-        const int r = idx >> 4, c = (idx & 15) * 8;
-        const bf16* vs = VP[r];
-        if (vs) cp_async16(Vs + r * RSB + c, vs + c);
-        else *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int idx = tid; idx < (lay.nkp - nk) * 16; idx += kAttnThreads) {
-        const int r = nk + (idx >> 4), c = (idx & 15) * 8;
-        *reinterpret_cast<uint4*>(Ks + r * RSB + c) = z;
-        *reinterpret_cast<uint4*>(Vs + r * RSB + c) = z;
-    }
-    for (int idx = tid; idx < (lay.npp - np) * 16; idx += kAttnThreads) {
-        const int r = np + (idx >> 4), c = (idx & 15) * 8;
-        *reinterpret_cast<uint4*>(Ps + r * RSB + c) = z;
-    }
-    // queries with the position biases, rounded to bf16 (rows >= T are zero)
-    for (int idx = tid; idx < TM * 16; idx += kAttnThreads) {
-        const int i = idx >> 4, c = (idx & 15) * 8;
-        float q[8];
-        if (i < T_) {
-            load16<bf16>(qkv + static_cast<size_t>(row_off + i) * ld_qkv + hoff + c, q);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) q[e] = 0.f;
-        }
-        float a[8], bb[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            a[e] = i < T_ ? q[e] + bias_u[hoff + c + e] : 0.f;
-            bb[e] = i < T_ ? q[e] + bias_v[hoff + c + e] : 0.f;
-        }
-        store16<bf16>(QU + i * RSB + c, a);
-        store16<bf16>(QV + i * RSB + c, bb);
-    }
-    asm volatile("cp.async.wait_group 1;" ::: "memory");   // K and P have landed; V may still be in flight
     __syncthreads();
 
     // ---- AC and BDraw: jobs of two n-tiles (16 columns), one round over the warps.
@@ -475,6 +475,15 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");   // V
     __syncthreads();
+    // the chunk's V rows to their pages, as the K rows above
+    for (int idx = tid; idx < T_ * 16; idx += kAttnThreads) {
+        const int t = idx >> 4, c = (idx & 15) * 8;
+        const int f = head + t;
+        const int page = me.pages[(f / PF) % kPageSlots];
+        if (page < 0 || page >= cg.n_pages) continue;   // reported with the K rows
+        const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
+        *reinterpret_cast<uint4*>(vw + off) = *reinterpret_cast<const uint4*>(Vs + (L - lo + t) * RSB + c);
+    }
 
     // ---- O = P . V: warp w owns output columns [8w, 8w + 8)
     {
