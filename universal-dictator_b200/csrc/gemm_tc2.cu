@@ -14,8 +14,8 @@
 // their width balanced and rounded up to a multiple of 16 (N = 1024 -> 256; N = 1040 -> 5 tiles of 208; the
 // last tile of a row may be narrower). The MMA's N, the W rows each CTA loads (tile width / 2) and the epilogue
 // width are read from the tile. Narrower tiles that would fill a partial last round of pairs measured slower
-// than the wide tiles on the encoder's shapes, so the host does not trade width for rounds: an MMA of N = 128
-// took as long as one of N = 256 (256 x 128 tiles, two per pair, doubled the MMA time of every shape).
+// than the wide tiles on the encoder's shapes, so the host does not trade width for rounds (256 x 128 tiles, two
+// per pair, doubled the time from the first stage to the last MMA on every shape).
 //
 // TMA epilogues (every tile 256 wide, host-supplied tensor map of the output): bf16 outputs without a residual,
 // and fp32 outputs whose residual is the output itself with unit scale (the encoder's x += s * f(x)). Each
