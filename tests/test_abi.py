@@ -66,3 +66,23 @@ def test_no_device_fails_loudly():
         ud.Engine(ud.default_config())
     assert ei.value.status == 2
     assert "device" in str(ei.value).lower()
+
+
+def test_null_handles_are_statuses_not_crashes():
+    """Entry points given a NULL engine / streamer / frontend / decoder return a status (no device needed)."""
+    import ctypes as C
+
+    L = ud.lib()
+    out = (C.c_float * 16)()
+    frames = (C.c_int * 1)()
+    ids = (C.c_int32 * 1)(0)
+    rows = (C.c_int * 1)(9)
+    mel = (C.POINTER(C.c_float) * 1)(C.cast(out, C.POINTER(C.c_float)))
+    assert L.ud_step_batch_async(None, 1, ids, mel, rows, rows, rows, out, frames, None, None) == 1
+    assert L.ud_step_sync(None) == 1
+    assert L.ud_synchronize(None) == 1
+    assert L.ud_streamer_set_pipelined(None, 1) == 1
+    n = C.c_int()
+    assert L.ud_streamer_emissions(None, 0, None, None, None, 0, C.byref(n)) == 4
+    assert L.ud_streamer_step_times(None, 0, None, 0, C.byref(n)) == 4
+    assert L.ud_detok_decode(None, None, 0, None, 0, C.byref(C.c_size_t())) == 1
