@@ -391,21 +391,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
         store16<bf16>(QU + i * RSB + c, a);
         store16<bf16>(QV + i * RSB + c, bb);
     }
-    // ---- append this chunk's K rows (staged rows L - lo + t) at frames head + t. Those pool rows are not read by
-    //      this launch (the window is frames head - cacheLen .. head - 1, and the 8 page slots hold 128 frames).
     bf16* kw = reinterpret_cast<bf16*>(cg.kpool);
     bf16* vw = reinterpret_cast<bf16*>(cg.vpool);
-    for (int idx = tid; idx < T_ * 16; idx += kAttnThreads) {
-        const int t = idx >> 4, c = (idx & 15) * 8;
-        const int f = head + t;
-        const int page = me.pages[(f / PF) % kPageSlots];
-        if (page < 0 || page >= cg.n_pages) {
-            report_error(err, DEV_BAD_PAGE);
-            continue;
-        }
-        const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
-        *reinterpret_cast<uint4*>(kw + off) = *reinterpret_cast<const uint4*>(Ks + (L - lo + t) * RSB + c);
-    }
     __syncthreads();
 
     // ---- AC and BDraw: jobs of two n-tiles (16 columns), one round over the warps.
@@ -475,13 +462,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");   // V
     __syncthreads();
-    // the chunk's V rows to their pages, as the K rows above
+    // ---- append this chunk's K/V rows (staged rows L - lo + t) at frames head + t, off the path to the AC/BD
+    //      phase. Those pool rows are not read by this launch (the window is frames head - cacheLen .. head - 1,
+    //      and the 8 page slots hold 128 frames).
     for (int idx = tid; idx < T_ * 16; idx += kAttnThreads) {
         const int t = idx >> 4, c = (idx & 15) * 8;
         const int f = head + t;
         const int page = me.pages[(f / PF) % kPageSlots];
-        if (page < 0 || page >= cg.n_pages) continue;   // reported with the K rows
+        if (page < 0 || page >= cg.n_pages) {
+            report_error(err, DEV_BAD_PAGE);
+            continue;
+        }
         const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + hoff + c;
+        *reinterpret_cast<uint4*>(kw + off) = *reinterpret_cast<const uint4*>(Ks + (L - lo + t) * RSB + c);
         *reinterpret_cast<uint4*>(vw + off) = *reinterpret_cast<const uint4*>(Vs + (L - lo + t) * RSB + c);
     }
 
