@@ -166,8 +166,12 @@ UD_API ud_status ud_rnnt_decode(ud_engine* e, ud_stream_id id, const float* f, i
  * joint_dim 640 and max_symbols 10); larger calls return UD_ERR_INVALID_ARGUMENT.
  * The block is shared by every engine and thread on a device: overlapping calls on one device race, and the
  * caller must serialize them. The first call on each device resolves the block's address
- * (cudaGetSymbolAddress) and must come before any stream capture on that device. Rejections return the status
- * and clear the message that ud_last_error reports. */
+ * (cudaGetSymbolAddress) and must come before any stream capture on that device. The address is forgotten when
+ * the last engine on the device shuts down, so a device reset (cudaDeviceReset) is safe only while no engine is
+ * alive on that device. A bounded device wait that expires returns UD_ERR_DEVICE_TIMEOUT (the tokens are then
+ * incomplete) and clears the device error word. The per-kernel profiler (ud_profile_enable) does not time this
+ * call: its event bookkeeping allocates. Rejections return the status and clear the message that ud_last_error
+ * reports. */
 UD_API ud_status ud_rnnt_decode_static(ud_engine* e, ud_stream_id id, const float* f, int frames,
                                        int32_t* tokens_out, int* n_tokens_out);
 
@@ -203,7 +207,7 @@ UD_API ud_status ud_launch_count(ud_engine* e, int64_t* out);
  * it clears the totals. ud_profile_read synchronises and returns the summed device time and launch count
  * of one class. Used outside timed regions to attribute a step's time to its kernels. */
 typedef enum ud_kernel_kind {
-    UD_KIND_GEMM_TC = 0,    /* tcgen05 GEMM                                    */
+    UD_KIND_GEMM_TC = 0,    /* 1-CTA tcgen05 GEMM                              */
     UD_KIND_GEMM_SIMT = 1,  /* few-row / fp32 FFMA GEMM                         */
     UD_KIND_ATTENTION = 2,  /* rel-pos attention + K/V append                   */
     UD_KIND_CONV = 3,       /* conv module (GLU, depthwise, LN, SiLU, ring)     */
@@ -212,7 +216,8 @@ typedef enum ud_kernel_kind {
     UD_KIND_RNNT = 6,       /* RNN-T greedy                                     */
     UD_KIND_CACHE = 7,      /* cache append / gather / reset                    */
     UD_KIND_OTHER = 8,
-    UD_KIND_COUNT = 9
+    UD_KIND_GEMM_TC2 = 9,   /* 2-CTA (cta_group::2) tcgen05 GEMM, M >= 256     */
+    UD_KIND_COUNT = 10
 } ud_kernel_kind;
 UD_API ud_status ud_profile_enable(ud_engine* e, int enable);
 UD_API ud_status ud_profile_read(ud_engine* e, int kind, double* ms_total, int64_t* launches);

@@ -1,6 +1,8 @@
 """ud_rnnt_decode_static (scratch in the library's static device block, no allocation in the call) against
 ud_rnnt_decode on the same engine: two streams with identical weights and inputs, one decoded through each entry
-point, two calls in a row with the decoder state carried between them; plus the size limit. Collected last so it
+point, two calls in a row with the decoder state carried between them; plus the size limit, and that a warm call
+leaves the device's free memory unchanged. Both decoder kernels are covered: the lock-step one (the default for
+small batches) and one CTA per stream (UD_RNNT_LOCKSTEP=0, read when the engine is created). Collected last so it
 also runs after every other GPU test in one process."""
 
 import numpy as np
@@ -14,7 +16,9 @@ from oracle.weights import ModelDims, make_weights, sharpen_joint
 pytestmark = pytest.mark.gpu
 
 
-def test_static_scratch_decode_matches_existing_entry_point():
+@pytest.mark.parametrize("lockstep", ["1", "0"])
+def test_static_scratch_decode_matches_existing_entry_point(lockstep, monkeypatch):
+    monkeypatch.setenv("UD_RNNT_LOCKSTEP", lockstep)
     dims = ModelDims(n_layers=0, sub_channels=0, pred_layers=2)
     sd = sharpen_joint(make_weights(dims, seed=3), dims, 77)
     e = ud.Engine(ud.default_config(n_layers=0, sub_channels=0, pred_layers=2, max_streams=8, max_batch=8,
@@ -34,5 +38,13 @@ def test_static_scratch_decode_matches_existing_entry_point():
         with pytest.raises(ud.EngineError):
             e.rnnt_decode_static(b, big)
         assert e.rnnt_decode_static(b, big[:100]) == e.rnnt_decode(a, big[:100])
+        # A warm call takes no device memory: the device's free bytes are the same before and after.
+        c = e.open(1)
+        e.rnnt_decode_static(c, f[:20])
+        torch.cuda.synchronize(e.device)
+        free0 = torch.cuda.mem_get_info(e.device)[0]
+        e.rnnt_decode_static(c, f[20:40])
+        torch.cuda.synchronize(e.device)
+        assert torch.cuda.mem_get_info(e.device)[0] == free0
     finally:
         e.close()

@@ -137,6 +137,7 @@ struct ud_engine {
     int* err_d = nullptr;
     int* err_h = nullptr;
     int64_t launches = 0;
+    bool counted = false;   // included in the per-device engine count of the static decode scratch
     std::map<std::tuple<const void*, int, int, int>, TmaMatrix> amaps;
     std::map<std::tuple<const void*, int, int, int, int>, TmaMatrix> emaps;   // bf16 GEMM output blocks
     // CUDA graphs of the steady step, keyed by batch shape; metadata lives in a fixed device buffer for them
@@ -244,7 +245,8 @@ bool tc_ok(int N, int K) { return N % 128 == 0 && K % 64 == 0; }
 ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, const GemmEpilogue& epi) {
     if (M <= 0) return UD_OK;
     const bool tc = e->bf && M > 16 && W.has_tma;
-    Launch L_(e, tc ? UD_KIND_GEMM_TC : UD_KIND_GEMM_SIMT);
+    const bool tc2 = tc && e->tc2_on && M >= 256 && W.N % 16 == 0;
+    Launch L_(e, tc2 ? UD_KIND_GEMM_TC2 : tc ? UD_KIND_GEMM_TC : UD_KIND_GEMM_SIMT);
     if (e->bf) {
         if (!tc) {
             gemm_simt<bf16, bf16>(static_cast<const bf16*>(A), lda, static_cast<const bf16*>(W.p), M, W.N, W.K, epi,
@@ -258,7 +260,7 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
                     return fail(UD_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
                 it = e->amaps.emplace(key, t).first;
             }
-            if (e->tc2_on && M >= 256 && W.N % 16 == 0) {
+            if (tc2) {
                 // tensor map of a bf16 output for the TMA epilogue (null when a map cannot describe it)
                 auto emap = [&](const void* p, int ld, bool bf) -> const TmaMatrix* {
                     const auto k = std::make_tuple(p, M, W.N, ld, bf ? 1 : 0);
@@ -1047,6 +1049,23 @@ namespace {
 
 std::mutex g_scratch_mu;
 unsigned char* g_scratch_addr[kMaxScratchDevices];   // resolved once per device
+int g_live_engines[kMaxScratchDevices];              // engines alive per device
+
+// The resolved address belongs to the device's current context. When the last engine on a device shuts down it is
+// forgotten, so that a context the host application re-creates after that (cudaDeviceReset) is resolved afresh.
+void scratch_engine_added(int device) {
+    if (device < 0 || device >= kMaxScratchDevices) return;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    ++g_live_engines[device];
+}
+void scratch_engine_removed(int device) {
+    if (device < 0 || device >= kMaxScratchDevices) return;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (--g_live_engines[device] <= 0) {
+        g_live_engines[device] = 0;
+        g_scratch_addr[device] = nullptr;
+    }
+}
 
 // Rejections record no message: building one could allocate.
 ud_status quiet(ud_status s) {
@@ -1283,6 +1302,8 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
         if ((s = dalloc(e, &q.part_idx, parts)) != UD_OK) return cleanup(s);
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(UD_ERR_CUDA, "device synchronize failed"));
+    scratch_engine_added(device);
+    e->counted = true;
     *out = e;
     return UD_OK;
 }
@@ -1305,6 +1326,7 @@ ud_status ud_shutdown(ud_engine* e) {
     for (cudaEvent_t ev : e->prof_events) cudaEventDestroy(ev);
     for (auto& g : e->graphs) cudaGraphExecDestroy(g.second.exec);
     if (e->stream) cudaStreamDestroy(e->stream);
+    if (e->counted) scratch_engine_removed(e->device);
     delete e;
     return UD_OK;
 }
@@ -1658,7 +1680,15 @@ ud_status ud_rnnt_decode_static(ud_engine* e, ud_stream_id id, const float* f, i
     UD_CK_QUIET(cudaGetLastError());
     int nt = 0;
     UD_CK_QUIET(cudaMemcpyAsync(&nt, count, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    UD_CK_QUIET(cudaMemcpyAsync(e->err_h, e->err_d, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     UD_CK_QUIET(cudaStreamSynchronize(e->stream));
+    // A bounded device wait that expired (the lock-step decoder's grid barrier) ends the kernel early: the tokens
+    // are incomplete, so the call fails, and the error word is cleared so that the next call starts clean.
+    if (const int code = *e->err_h) {
+        UD_CK_QUIET(cudaMemsetAsync(e->err_d, 0, sizeof(int), e->stream));
+        UD_CK_QUIET(cudaStreamSynchronize(e->stream));
+        return quiet(code == DEV_BAD_PAGE ? UD_ERR_INVALID_ARGUMENT : UD_ERR_DEVICE_TIMEOUT);
+    }
     if (nt < 0 || static_cast<size_t>(nt) > tok_cap) return quiet(UD_ERR_CUDA);
     if (nt > 0) {
         UD_CK_QUIET(cudaMemcpyAsync(tokens_out, tokens, sizeof(int32_t) * nt, cudaMemcpyDeviceToHost, e->stream));

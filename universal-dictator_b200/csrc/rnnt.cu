@@ -609,8 +609,20 @@ void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, i
             static size_t attr_set[kMaxDevices] = {};
             ensure_dyn_smem(rnnt_lockstep_kernel, kSmemMax, attr_set);
             cudaMemsetAsync(scr->barrier, 0, sizeof(unsigned long long), s);
-            rnnt_lockstep_kernel<<<G, kLsThreads, smem, s>>>(w, st, proj, ld_proj, meta, n, tokens, tok_stride, n_tokens,
-                                                             *scr, gm, dev_err);
+            // A cooperative launch: the runtime refuses it unless all G CTAs can be resident at once, so the grid
+            // barriers never wait on a CTA that has not been scheduled (the bounded waits stay as a second guard).
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(G);
+            cfg.blockDim = dim3(kLsThreads);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeCooperative;
+            attr[0].val.cooperative = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaLaunchKernelEx(&cfg, rnnt_lockstep_kernel, w, st, proj, ld_proj, meta, n, tokens, tok_stride, n_tokens,
+                               *scr, gm, dev_err);
             return;
         }
     }

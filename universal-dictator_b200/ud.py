@@ -29,7 +29,7 @@ STATUS = {0: "ok", 1: "invalid argument", 2: "CUDA error", 3: "out of memory", 4
           5: "pool exhausted", 6: "weights error", 7: "not ready", 8: "device wait expired", 9: "I/O error",
           10: "unsupported"}
 DTYPE_F32, DTYPE_BF16 = 0, 1
-KINDS = ["gemm_tc", "gemm_simt", "attention", "conv", "norm", "subsample", "rnnt", "cache", "other"]
+KINDS = ["gemm_tc", "gemm_simt", "attention", "conv", "norm", "subsample", "rnnt", "cache", "other", "gemm_tc2"]
 
 # Every symbol include/ud.h declares (the test suite checks the library exports exactly these).
 ABI_SYMBOLS = [
