@@ -241,6 +241,29 @@ ud_status halloc(ud_engine* e, T** p, size_t count) {
 
 bool tc_ok(int N, int K) { return N % 128 == 0 && K % 64 == 0; }
 
+// Cached tensor maps: a bf16 activation operand [M, K] (128-row boxes), and a GEMM output [M, N] in 32-row blocks
+// for the TMA epilogues (null when a map cannot describe it).
+const TmaMatrix* act_map(ud_engine* e, const void* A, int M, int K, int lda) {
+    auto key = std::make_tuple(A, M, K, lda);
+    auto it = e->amaps.find(key);
+    if (it == e->amaps.end()) {
+        TmaMatrix t;
+        if (!make_tma_bf16(t, A, M, K, lda, 128)) return nullptr;
+        it = e->amaps.emplace(key, t).first;
+    }
+    return &it->second;
+}
+const TmaMatrix* out_map(ud_engine* e, const void* p, int M, int N, int ld, bool bf) {
+    const auto k = std::make_tuple(p, M, N, ld, bf ? 1 : 0);
+    auto jt = e->emaps.find(k);
+    if (jt == e->emaps.end()) {
+        TmaMatrix t;
+        if (!make_tma_epi(t, p, M, N, ld, bf)) return nullptr;
+        jt = e->emaps.emplace(k, t).first;
+    }
+    return &jt->second;
+}
+
 // One GEMM through the engine's dispatch: tcgen05 for bf16 with more than 16 rows, SIMT otherwise.
 ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, const GemmEpilogue& epi) {
     if (M <= 0) return UD_OK;
@@ -252,37 +275,19 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
             gemm_simt<bf16, bf16>(static_cast<const bf16*>(A), lda, static_cast<const bf16*>(W.p), M, W.N, W.K, epi,
                                   e->stream);
         } else {
-            auto key = std::make_tuple(A, M, W.K, lda);
-            auto it = e->amaps.find(key);
-            if (it == e->amaps.end()) {
-                TmaMatrix t;
-                if (!make_tma_bf16(t, A, M, W.K, lda, 128))
-                    return fail(UD_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
-                it = e->amaps.emplace(key, t).first;
-            }
+            const TmaMatrix* am = act_map(e, A, M, W.K, lda);
+            if (!am) return fail(UD_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
             if (tc2) {
-                // tensor map of a bf16 output for the TMA epilogue (null when a map cannot describe it)
-                auto emap = [&](const void* p, int ld, bool bf) -> const TmaMatrix* {
-                    const auto k = std::make_tuple(p, M, W.N, ld, bf ? 1 : 0);
-                    auto jt = e->emaps.find(k);
-                    if (jt == e->emaps.end()) {
-                        TmaMatrix t;
-                        if (!make_tma_epi(t, p, M, W.N, ld, bf)) return nullptr;
-                        jt = e->emaps.emplace(k, t).first;
-                    }
-                    return &jt->second;
-                };
                 // output maps for the TMA epilogues: bf16 stores, and fp32 reduce-adds when the residual is the output
                 const TmaMatrix* om = nullptr;
                 if (epi.out_bf16 && !epi.residual)
-                    om = emap(epi.out, epi.ldo, true);
+                    om = out_map(e, epi.out, M, W.N, epi.ldo, true);
                 else if (!epi.out_bf16 && epi.residual == epi.out && epi.ldr == epi.ldo && epi.res_scale == 1.f)
-                    om = emap(epi.out, epi.ldo, false);
-                gemm_tc2(it->second, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, om, e->stream);
+                    om = out_map(e, epi.out, M, W.N, epi.ldo, false);
+                gemm_tc2(*am, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, om, e->stream);
             } else {
                 const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;
-                gemm_tc(it->second, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms,
-                        e->stream);
+                gemm_tc(*am, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms, e->stream);
             }
         }
     } else {
@@ -490,13 +495,17 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         g.out_scale = scale;
         return g;
     };
+    // A feed-forward module: x += 1/2 * (SiLU(h W1^T) W2^T).
+    auto ff = [&](const WeightMat& w1, const WeightMat& w2) -> ud_status {
+        GemmEpilogue gs = epi_out(e->hid, e->F, true, e);
+        gs.act = ACT_SILU;
+        UD_TRY(gemm(e, e->h, D, M, w1, gs));
+        return gemm(e, e->hid, e->F, M, w2, resid(0.5f));
+    };
     if (NL > 0) ln(e->layers[0].ln_ff1_g, e->layers[0].ln_ff1_b);
     for (int l = 0; l < NL; ++l) {
         LayerW& w = e->layers[l];
-        GemmEpilogue gs = epi_out(e->hid, e->F, true, e);
-        gs.act = ACT_SILU;
-        UD_TRY(gemm(e, e->h, D, M, w.ff1_w1, gs));
-        UD_TRY(gemm(e, e->hid, e->F, M, w.ff1_w2, resid(0.5f)));
+        UD_TRY(ff(w.ff1_w1, w.ff1_w2));
         ln(w.ln_att_g, w.ln_att_b);
         UD_TRY(gemm(e, e->h, D, M, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
         {
@@ -522,8 +531,7 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         }
         UD_TRY(gemm(e, e->y, D, M, w.pw2, resid(1.0f)));
         ln(w.ln_ff2_g, w.ln_ff2_b);
-        UD_TRY(gemm(e, e->h, D, M, w.ff2_w1, gs));
-        UD_TRY(gemm(e, e->hid, e->F, M, w.ff2_w2, resid(0.5f)));
+        UD_TRY(ff(w.ff2_w1, w.ff2_w2));
         if (l + 1 < NL) {
             LayerW& nx = e->layers[l + 1];
             Launch L_(e, UD_KIND_NORM);

@@ -32,9 +32,12 @@
 #include "common.cuh"
 #include "gemm_epi.cuh"
 #include "kernels.h"
+#include "tc2_common.cuh"
 
 namespace ud {
 namespace {
+
+using namespace tc2;
 
 constexpr int BM2 = 256;  // rows per CTA pair
 constexpr int BK = 64;
@@ -57,58 +60,12 @@ struct Tc2Cfg {
     static constexpr int SMEM = EPI_OFF + EPI_BYTES + 1024;
 };
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// Address of the same shared-memory offset in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// TMA load into this CTA's shared memory whose completion is counted on the (possibly peer) barrier.
-__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
-                                                 int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-        "[%2];" ::"r"(smem_u32(smem_dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
-        : "memory");
-}
-__device__ __forceinline__ void tc2_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                             uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrives on the barrier at this offset in both CTAs of the pair once the issued MMAs complete.
-__device__ __forceinline__ void tc2_commit_both(uint64_t* bar) {
-    const uint16_t mask = 0x3;
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            smem_u32(bar)),
-        "h"(mask)
-        : "memory");
-}
-
 template <int BN, int EP>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapW,
                     const __grid_constant__ CUtensorMap mapO, int M, int N,
                     int K, int tn, const GemmEpilogue epi, int* err) {
     using C = Tc2Cfg<BN, EP>;
-    pdl_launch_dependents();
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -192,6 +149,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
             }
         producer_done:;
+            // This CTA has no more tiles to load: the next kernel may launch now. Its CTAs then take the SMs as this
+            // grid's last tiles drain, instead of sharing them with this grid's epilogues from the start.
+            pdl_launch_dependents();
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
