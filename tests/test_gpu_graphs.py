@@ -65,3 +65,17 @@ def test_graph_replay_bit_identical_at_two_cta_batch():
         assert fa == fb and ta == tb
         for x, y in zip(pa, pb):
             assert np.array_equal(x, y)
+
+
+def test_tma_attention_matches_one_cta_per_stream_head_kernel():
+    """The persistent TMA-fed attention kernel and the one-CTA-per-(stream, head) kernel stage the same bf16 rows
+    and run the same fragment arithmetic: a 2-layer engine gives the same bits with either (UD_ATTN_TMA=0 selects
+    the latter), over first, steady and short final chunks of 20 streams."""
+    dims = ModelDims(n_layers=2)
+    sd = make_weights(dims, seed=2)
+    a = _run(True, sd, dims, n=20)
+    b = _run(True, sd, dims, n=20, env={"UD_ATTN_TMA": "0"})
+    for (pa, fa, ta), (pb, fb, tb) in zip(a, b):
+        assert fa == fb and ta == tb
+        for x, y in zip(pa, pb):
+            assert np.array_equal(x, y)

@@ -504,6 +504,356 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_tc_kernel(const bf16* __
 
 }  // namespace tc
 
+// ---------------------------------------------------------------- persistent TMA-fed variant (bf16, T <= 16)
+// The same attention and append as attn_tc_kernel, restructured so that a CTA's copies cost a few instructions
+// and overlap its compute:
+//   * one CTA per SM walks a contiguous range of (head, stream) items, head-major, so consecutive items share one
+//     head; that head's slice of the projected position table (128 rows x 128 columns) is staged once per head and
+//     stays resident (the items of one CTA span at most two heads);
+//   * a producer warp stages item k + 1 while 16 compute warps work on item k (two stage buffers on mbarriers).
+//     An item is staged by about 30 TMA tensor loads: one box of 16 frames x 64 columns per cache page touched by
+//     the window and column half (the window's first and last page boxes start at the window's ends, so frames
+//     outside it arrive as zeros without being read: the first box from the window's first frame, the last one
+//     from a negative frame coordinate), one box for this chunk's new K, V and Q rows from the QKV projection;
+//   * the compute warps address staged K and V rows through a per-item key -> row table (ldmatrix takes one row
+//     address per lane), so the page boxes need not be contiguous; the staged rows keep TMA's 128-byte swizzle
+//     (16-byte chunk c of row r at position c ^ (r % 8)), which makes the ldmatrix reads conflict-free.
+// Math per item is attn_tc_kernel's: AC = (Q + u) K^T and BDraw = (Q + v) P^T with mma.sync m16n8k16, the band
+// shift and softmax in fp32, O = softmax . V, and the chunk's K and V rows appended to their pages.
+namespace tma_attn {
+
+constexpr int kTM = 16;          // query rows per item (T <= 16)
+constexpr int kKVRows = 112;     // staged K (and V) rows: 6 page boxes of 16 frames, then the chunk's rows
+constexpr int kNewRow = 96;      // first staged row of this chunk's K / V
+constexpr int kPRows = 128;      // staged position-table rows per head
+constexpr int kNKP = 96;         // padded key count (at most L + T = 86 visible keys)
+constexpr int kNPP = 112;        // padded position-row count (at most T + 86 - 1 = 101)
+constexpr int kComputeWarps = 16;
+constexpr int kThreads = (kComputeWarps + 1) * 32;
+constexpr int RSB = 136;         // padded row of the biased queries (elements): conflict-free ldmatrix
+constexpr int ACW = kNKP + 8, BDW = kNPP + 8, PSW = kNKP + 8;
+
+struct Window {
+    int T, valid_t, cl, head, row_off, lo, hi, nk, rel_min, np;
+    int f0, p_first, p_last, npg, y0, ylast;
+    int pages[kPageSlots];
+};
+
+struct Lay {
+    static constexpr uint32_t HALF_KV = kKVRows * 128;                 // one 64-column half of the staged K rows
+    static constexpr uint32_t STAGE = 4 * HALF_KV + 2 * kTM * 128;     // K0 K1 V0 V1 Q0 Q1
+    static constexpr uint32_t P = 0;                                   // position rows, two 64-column halves
+    static constexpr uint32_t S0 = 2 * kPRows * 128;
+    static constexpr uint32_t QU = S0 + 2 * STAGE;                     // queries + pos_bias_u (bf16, padded rows)
+    static constexpr uint32_t QV = QU + kTM * RSB * 2;                 // queries + pos_bias_v
+    static constexpr uint32_t AC = QV + kTM * RSB * 2;
+    static constexpr uint32_t BD = AC + kTM * ACW * 4;
+    static constexpr uint32_t PB = BD + kTM * BDW * 4;
+    static constexpr uint32_t KROW = PB + kTM * PSW * 2;               // staged row of each key
+    static constexpr uint32_t BIAS = KROW + kNKP * 4;                  // this head's pos_bias_u, pos_bias_v (fp32)
+    static constexpr uint32_t WIN = BIAS + 2 * 128 * 4;                // the item window of each stage
+    static constexpr uint32_t ZERO = (WIN + 2 * sizeof(Window) + 127) / 128 * 128;   // one zero row (256 bytes)
+    static constexpr uint32_t BAR = ZERO + 256;
+    static constexpr uint32_t TOTAL = BAR + 64;
+    static constexpr uint32_t SMEM = TOTAL + 1024;                     // room to align the base to 1024 bytes
+};
+static_assert(Lay::STAGE % 1024 == 0 && Lay::S0 % 1024 == 0 && Lay::HALF_KV % 1024 == 0, "swizzle alignment");
+static_assert(Lay::SMEM <= 232448, "shared memory of the TMA attention kernel");
+
+// Address of the 16-byte chunk c (0..15) of staged row r in a region of two 64-column halves of `rows` rows each,
+// 128-byte swizzled; r < 0 is the zero row.
+__device__ __forceinline__ const uint8_t* chunk_addr(const uint8_t* region, int rows, int r, int c, const uint8_t* zero) {
+    if (r < 0) return zero + ((c & 7) << 4);
+    return region + (c >> 3) * rows * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory"); }
+
+__device__ __forceinline__ Window window_of(const BatchEntry& me, int L) {
+    Window w;
+    w.T = me.T;
+    w.valid_t = me.valid_t;
+    w.cl = me.cache_len;
+    w.head = me.head;
+    w.row_off = me.row_off;
+    w.lo = L - w.cl;
+    w.hi = L + w.valid_t;
+    w.nk = w.hi > w.lo ? w.hi - w.lo : 0;
+    w.rel_min = L - w.hi + 1;
+    w.np = w.nk > 0 ? w.T + w.nk - 1 : 0;
+    w.f0 = w.head - w.cl;
+    if (w.cl > 0) {
+        w.p_first = w.f0 >> 4;
+        w.p_last = (w.head - 1) >> 4;
+        w.npg = w.p_last - w.p_first + 1;
+        w.y0 = w.f0 & 15;
+        w.ylast = ((w.head - 1) & 15) + 1 - 16;
+    } else {
+        w.p_first = w.p_last = w.npg = w.y0 = w.ylast = 0;
+    }
+    for (int i = 0; i < kPageSlots; ++i) w.pages[i] = me.pages[i];
+    return w;
+}
+
+// Staged row of key j (window index; keys [0, nk) visible), -1 for the padding keys.
+__device__ __forceinline__ int key_row(const Window& w, int L, int j) {
+    if (j >= w.nk) return -1;
+    const int jj = w.lo + j;
+    if (jj >= L) return kNewRow + (jj - L);
+    const int f = w.f0 + j;
+    const int pg = f >> 4, bx = pg - w.p_first;
+    const int y = bx == 0 ? w.y0 : (pg == w.p_last ? w.ylast : 0);
+    return 16 * bx + (f & 15) - y;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
+    const __grid_constant__ CUtensorMap mqkv, const __grid_constant__ CUtensorMap mk,
+    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mp, int D, int L, int ptab_row0,
+    const float* __restrict__ bias_u, const float* __restrict__ bias_v, const BatchEntry* __restrict__ meta, int n,
+    int n_heads, int ipc, int layer, int n_pages, bf16* __restrict__ kw, bf16* __restrict__ vw, bf16* __restrict__ out,
+    int ldo, int* err) {
+    constexpr int DKk = 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + Lay::BAR);
+    uint64_t* empty = full + 2;
+    uint64_t* pfull = full + 4;
+    int* abort_flag = reinterpret_cast<int*>(full + 5);
+    volatile int* abort_v = abort_flag;
+    const uint8_t* zero = sm + Lay::ZERO;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int total = n * n_heads;
+    const int first = blockIdx.x * ipc, last = min(total, first + ipc);
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(pfull, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        prefetch_tensormap(&mqkv);
+        prefetch_tensormap(&mk);
+        prefetch_tensormap(&mv);
+        prefetch_tensormap(&mp);
+    }
+    if (tid < 64) reinterpret_cast<uint32_t*>(sm + Lay::ZERO)[tid] = 0u;
+    __syncthreads();
+    pdl_wait();   // the QKV projection and the step's metadata come from earlier work on the stream
+
+    if (warp == kComputeWarps) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            int cur_h = -1;
+            for (int k = 0; first + k < last; ++k) {
+                const int item = first + k, h = item / n, b = item - h * n, s = k & 1;
+                if (h != cur_h) {
+                    // the staged position rows are rewritten once every item of the previous head is done
+                    if (cur_h >= 0 &&
+                        !mbar_wait_bounded(&empty[(k - 1) & 1], ((k - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v))
+                        break;
+                    mbar_arrive_expect_tx(pfull, 2 * kPRows * 128);
+                    tma_load_2d(sm + Lay::P, &mp, pfull, h * DKk, ptab_row0);
+                    tma_load_2d(sm + Lay::P + kPRows * 128, &mp, pfull, h * DKk + 64, ptab_row0);
+                    cur_h = h;
+                }
+                if (k >= 2 && !mbar_wait_bounded(&empty[s], ((k - 2) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v)) break;
+                Window& w = reinterpret_cast<Window*>(sm + Lay::WIN)[s];
+                w = window_of(meta[b], L);   // published to the compute warps by the arrive below
+                uint8_t* st = sm + Lay::S0 + s * Lay::STAGE;
+                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>((w.npg + 1) * 4 * 2048 + 2 * 2048));
+                for (int bx = 0; bx < w.npg; ++bx) {
+                    const int pg = w.p_first + bx;
+                    const int page = w.pages[pg % kPageSlots];
+                    int z = layer * n_pages + page;
+                    if (page < 0 || page >= n_pages) {
+                        report_error(err, DEV_BAD_PAGE);
+                        z = -1;   // a page coordinate outside the pool: the box arrives as zeros
+                    }
+                    const int y = bx == 0 ? w.y0 : (pg == w.p_last ? w.ylast : 0);
+                    for (int half = 0; half < 2; ++half) {
+                        const int x = h * DKk + half * 64;
+                        tma_load_3d(st + half * Lay::HALF_KV + bx * 16 * 128, &mk, &full[s], x, y, z);
+                        tma_load_3d(st + (2 + half) * Lay::HALF_KV + bx * 16 * 128, &mv, &full[s], x, y, z);
+                    }
+                }
+                for (int half = 0; half < 2; ++half) {
+                    const int x = h * DKk + half * 64;
+                    tma_load_2d(st + half * Lay::HALF_KV + kNewRow * 128, &mqkv, &full[s], D + x, w.row_off);
+                    tma_load_2d(st + (2 + half) * Lay::HALF_KV + kNewRow * 128, &mqkv, &full[s], 2 * D + x, w.row_off);
+                    tma_load_2d(st + 4 * Lay::HALF_KV + half * kTM * 128, &mqkv, &full[s], x, w.row_off);
+                }
+            }
+            pdl_launch_dependents();
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------------- compute warps
+    bf16* QU = reinterpret_cast<bf16*>(sm + Lay::QU);
+    bf16* QV = reinterpret_cast<bf16*>(sm + Lay::QV);
+    float* AC = reinterpret_cast<float*>(sm + Lay::AC);
+    float* BD = reinterpret_cast<float*>(sm + Lay::BD);
+    bf16* Pb = reinterpret_cast<bf16*>(sm + Lay::PB);
+    int* krow = reinterpret_cast<int*>(sm + Lay::KROW);
+    float* bias = reinterpret_cast<float*>(sm + Lay::BIAS);   // [0, 128): pos_bias_u, [128, 256): pos_bias_v
+    const uint8_t* Ps = sm + Lay::P;
+    const float scale = rsqrtf(static_cast<float>(DKk));
+    const int g = lane >> 2, t4 = lane & 3;
+    volatile int* go = abort_flag + 1;
+    int cur_h = -1, nph = 0;
+    for (int k = 0; first + k < last; ++k) {
+        const int item = first + k, h = item / n, s = k & 1;
+        const int hoff = h * DKk;
+        const bool new_head = h != cur_h;
+        // One thread makes the bounded waits and the whole group follows its verdict, so that no warp leaves while
+        // the others wait at a group barrier; then every thread observes the completed phases (at once).
+        if (tid == 0) {
+            bool ok = !new_head || mbar_wait_bounded(pfull, nph & 1, err, DEV_TIMEOUT_ATTN, abort_v);
+            ok = ok && mbar_wait_bounded(&full[s], (k >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v);
+            *go = ok ? 1 : 0;
+        }
+        if (new_head && tid < 2 * DKk) bias[tid] = (tid < DKk ? bias_u : bias_v)[hoff + (tid & (DKk - 1))];
+        compute_sync();
+        if (!*go) break;
+        if (new_head) {
+            mbar_wait_bounded(pfull, nph & 1, err, DEV_TIMEOUT_ATTN, abort_v);
+            ++nph;
+            cur_h = h;
+        }
+        mbar_wait_bounded(&full[s], (k >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v);
+        const Window& ws = reinterpret_cast<const Window*>(sm + Lay::WIN)[s];
+        const uint8_t* st = sm + Lay::S0 + s * Lay::STAGE;
+        const uint8_t* Ks = st;
+        const uint8_t* Vs = st + 2 * Lay::HALF_KV;
+        const uint8_t* Qs = st + 4 * Lay::HALF_KV;
+
+        // ---- key -> staged row table; queries plus the position biases, rounded to bf16 (rows >= T zero)
+        for (int j = tid; j < kNKP; j += kComputeWarps * 32) krow[j] = key_row(ws, L, j);
+        const int T_ = ws.T;
+        for (int idx = tid; idx < kTM * 16; idx += kComputeWarps * 32) {
+            const int i = idx >> 4, c = idx & 15;
+            float q[8], a[8], bb[8];
+            load16<bf16>(reinterpret_cast<const bf16*>(chunk_addr(Qs, kTM, i, c, zero)), q);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                a[e] = i < T_ ? q[e] + bias[c * 8 + e] : 0.f;
+                bb[e] = i < T_ ? q[e] + bias[DKk + c * 8 + e] : 0.f;
+            }
+            store16<bf16>(QU + i * RSB + c * 8, a);
+            store16<bf16>(QV + i * RSB + c * 8, bb);
+        }
+        const int nk = ws.nk, np = ws.np, rel_min = ws.rel_min, row_off = ws.row_off, head = ws.head;
+        compute_sync();
+
+        // ---- AC = (Q + u) K^T and BDraw = (Q + v) P^T: jobs of two n-tiles (16 columns), one round over the warps
+        {
+            const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+            const int n_ac = (nk + 15) / 16, n_bd = (np + 15) / 16;
+            const int brow = (lane & 7) + ((lane >> 4) << 3), bsel = (lane >> 3) & 1;
+            for (int job = warp; job < n_ac + n_bd; job += kComputeWarps) {
+                const bool is_ac = job < n_ac;
+                const int n0 = (is_ac ? job : job - n_ac) * 16;
+                const bf16* As = is_ac ? QU : QV;
+                // this lane's B row: a key's staged K row, or a position-table row (rel_min + r -> row rel + 15)
+                const int r = n0 + brow;
+                const int brow_s = is_ac ? krow[r] : (rel_min + r + 15);
+                const uint8_t* breg = is_ac ? Ks : Ps;
+                const int brows = is_ac ? kKVRows : kPRows;
+                float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    uint32_t a[4], bfr[4];
+                    tc::ldsm_x4(a, As + arow * RSB + ks * 16 + acol);
+                    tc::ldsm_x4(bfr, chunk_addr(breg, brows, brow_s, 2 * ks + bsel, zero));
+                    tc::mma16816(c0, a, bfr[0], bfr[1]);
+                    tc::mma16816(c1, a, bfr[2], bfr[3]);
+                }
+                float* dst = is_ac ? AC : BD;
+                const int wd = is_ac ? ACW : BDW;
+                *reinterpret_cast<float2*>(dst + g * wd + n0 + 2 * t4) = make_float2(c0[0], c0[1]);
+                *reinterpret_cast<float2*>(dst + (g + 8) * wd + n0 + 2 * t4) = make_float2(c0[2], c0[3]);
+                *reinterpret_cast<float2*>(dst + g * wd + n0 + 8 + 2 * t4) = make_float2(c1[0], c1[1]);
+                *reinterpret_cast<float2*>(dst + (g + 8) * wd + n0 + 8 + 2 * t4) = make_float2(c1[2], c1[3]);
+            }
+        }
+        compute_sync();
+
+        // ---- softmax rows (fp32), probabilities to bf16: one query row per warp
+        for (int i = warp; i < kTM; i += kComputeWarps) {
+            bf16* prow = Pb + i * PSW;
+            if (i >= T_ || nk == 0) {
+                for (int jj = lane; jj < kNKP; jj += 32) prow[jj] = __float2bfloat16_rn(0.f);
+                continue;
+            }
+            const float* acr = AC + i * ACW;
+            const float* bdr = BD + i * BDW + i + nk - 1;   // BDraw column for key jj is (i + nk - 1 - jj)
+            constexpr int kPer = kNKP / 32;
+            float sv[kPer];
+            float m = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+                const int jj = lane + 32 * u;
+                sv[u] = jj < nk ? (acr[jj] + bdr[-jj]) * scale : -INFINITY;
+                m = fmaxf(m, sv[u]);
+            }
+            m = warp_max(m);
+            float sum = 0.f;
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) {
+                const int jj = lane + 32 * u;
+                sv[u] = jj < nk ? __expf(sv[u] - m) : 0.f;
+                sum += sv[u];
+            }
+            sum = warp_sum(sum);
+            const float inv = 1.f / sum;
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) prow[lane + 32 * u] = __float2bfloat16_rn(sv[u] * inv);
+        }
+        compute_sync();
+
+        // ---- append this chunk's K/V rows (staged rows kNewRow + t) at frames head + t
+        for (int idx = tid; idx < T_ * 32; idx += kComputeWarps * 32) {
+            const int t = idx >> 5, isv = (idx >> 4) & 1, c = idx & 15;
+            const int f = head + t;
+            const int page = ws.pages[(f >> 4) % kPageSlots];
+            if (page < 0 || page >= n_pages) {
+                report_error(err, DEV_BAD_PAGE);
+                continue;
+            }
+            const size_t off = ((static_cast<size_t>(layer) * n_pages + page) * 16 + (f & 15)) * D + hoff + c * 8;
+            const uint4 v = *reinterpret_cast<const uint4*>(chunk_addr(isv ? Vs : Ks, kKVRows, kNewRow + t, c, zero));
+            *reinterpret_cast<uint4*>((isv ? vw : kw) + off) = v;
+        }
+
+        // ---- O = P . V: warp w owns output columns [8 w, 8 w + 8)
+        {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+            const int ksteps = (nk + 15) / 16;
+            for (int ks = 0; ks < ksteps; ++ks) {
+                uint32_t a[4], bfr[2];
+                tc::ldsm_x4(a, Pb + arow * PSW + ks * 16 + acol);
+                tc::ldsm_x2_t(bfr, chunk_addr(Vs, kKVRows, krow[ks * 16 + (lane & 15)], warp, zero));
+                tc::mma16816(acc, a, bfr[0], bfr[1]);
+            }
+            const int col = hoff + warp * 8 + 2 * t4;
+            if (g < T_)
+                *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g) * ldo + col) =
+                    __floats2bfloat162_rn(acc[0], acc[1]);
+            if (g + 8 < T_)
+                *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g + 8) * ldo + col) =
+                    __floats2bfloat162_rn(acc[2], acc[3]);
+        }
+        compute_sync();   // every read of this stage, the window and the scores is done
+        if (tid == 0) mbar_arrive(&empty[s]);
+    }
+    if (*abort_v) __nanosleep(100000);   // after a failed wait: let copies already issued into this CTA land
+}
+
+}  // namespace tma_attn
+
 }  // namespace
 
 template <typename T>
@@ -528,6 +878,25 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
     dim3 grid(n, n_heads);
     launch_pdl(relpos_attn_kernel<T>, dim3(grid), dim3(256), lay.total, s, qkv, ld_qkv, ptab, tmax, bias_u, bias_v, meta, cg, layer, out,
                                                        ldo, tmax_batch, dev_err);
+}
+
+bool relpos_attention_tma(const TmaMatrix& qkv, const TmaMatrix& kpool, const TmaMatrix& vpool, const TmaMatrix& ptab,
+                          int ptab_row0, const float* bias_u, const float* bias_v, const BatchEntry* meta, int n,
+                          int tmax_batch, const CacheGeom& cg, int layer, bf16* out, int ldo, int n_heads, int num_sms,
+                          int* dev_err, cudaStream_t s) {
+    using namespace tma_attn;
+    if (n <= 0) return true;
+    if (tmax_batch > kTM || cg.page_frames != 16 || cg.L + kTM - 1 + 15 >= kPRows || cg.L + kTM > kNKP) return false;
+    const int total = n * n_heads;
+    int ipc = (total + num_sms - 1) / num_sms;
+    if (ipc > n) ipc = n;   // a CTA's items then span at most two heads
+    const int grid = (total + ipc - 1) / ipc;
+    static size_t attr[kMaxDevices] = {};
+    ensure_dyn_smem(attn_tma_kernel, Lay::SMEM, attr);
+    launch_pdl(attn_tma_kernel, dim3(grid), dim3(kThreads), Lay::SMEM, s, qkv.map, kpool.map, vpool.map, ptab.map, cg.D,
+               cg.L, ptab_row0, bias_u, bias_v, meta, n, n_heads, ipc, layer, cg.n_pages,
+               reinterpret_cast<bf16*>(cg.kpool), reinterpret_cast<bf16*>(cg.vpool), out, ldo, dev_err);
+    return true;
 }
 
 size_t relpos_attention_smem_bytes(int tmax_batch, int L, int elem_bytes) {

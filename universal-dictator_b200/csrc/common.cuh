@@ -21,6 +21,7 @@ enum DeviceError : int {
     DEV_BAD_PAGE = 5,           // cache: a page slot needed by a kernel is unmapped
     DEV_TIMEOUT_TEST = 6,       // the failure-detection test wait
     DEV_TIMEOUT_GRID = 7,       // RNN-T: waiting at a grid barrier of the lock-step decoder
+    DEV_TIMEOUT_ATTN = 8,       // attention: waiting for a staged item or a free stage
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
@@ -210,6 +211,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
             smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
 

@@ -56,6 +56,8 @@ struct LayerW {
     float *ln_ff2_g, *ln_ff2_b, *ln_out_g, *ln_out_b;
     float *pos_u, *pos_v, *dw;
     void* ptab;
+    TmaMatrix pmap;        // bf16 position table, boxes of 64 columns x 128 rows (the TMA attention kernel)
+    bool has_pmap = false;
 };
 
 struct Slot {
@@ -147,6 +149,9 @@ struct ud_engine {
     };
     bool graphs_on = true;
     bool tc2_on = true;  // 2-CTA tcgen05 tiles for M >= 256, N % 256 == 0
+    bool attn_tma_on = true;            // persistent TMA-fed attention (UD_ATTN_TMA=0: one CTA per stream-head)
+    bool attn_maps = false;             // the tensor maps below exist
+    TmaMatrix attn_qkv_map, attn_k_map, attn_v_map;   // QKV rows (64 x 16 boxes), K and V page pools
     BatchEntry* meta_graph_d = nullptr;
     std::map<std::tuple<int, int, int, int, int, int>, GraphEntry> graphs;   // + staging buffer index
     std::map<std::tuple<int, int, int, int, int, int>, int> graph_seen;
@@ -311,8 +316,8 @@ ud_status device_error_status(ud_engine* e, int code) {
     UD_CK(cudaStreamSynchronize(e->stream));
     static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
                                   "GEMM TMEM drain wait", "unmapped cache page", "test wait",
-                                  "RNN-T grid barrier wait"};
-    const char* nm = (code >= 0 && code <= 7) ? names[code] : "unknown";
+                                  "RNN-T grid barrier wait", "attention stage wait"};
+    const char* nm = (code >= 0 && code <= 8) ? names[code] : "unknown";
     if (code == DEV_BAD_PAGE) return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
     return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
 }
@@ -510,7 +515,12 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         UD_TRY(gemm(e, e->h, D, M, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
         {
         Launch L_(e, UD_KIND_ATTENTION);
-        if (e->bf)
+        const bool tma_done = e->bf && e->attn_tma_on && e->attn_maps && w.has_pmap &&
+                              relpos_attention_tma(e->attn_qkv_map, e->attn_k_map, e->attn_v_map, w.pmap, e->tmax - 16,
+                                                   w.pos_u, w.pos_v, md, n, tmax_b, e->cg, l, (bf16*)e->att, D, e->H,
+                                                   e->num_sms, e->err_d, st);
+        if (tma_done) {
+        } else if (e->bf)
             relpos_attention<bf16>((bf16*)e->qkv, 3 * D, (bf16*)w.ptab, e->tmax, w.pos_u, w.pos_v, md, n, tmax_b, e->cg, l,
                                    (bf16*)e->att, D, e->H, e->err_d, st);
         else
@@ -864,7 +874,10 @@ ud_status load_weights_impl(ud_engine* e, const ud_weight* table, int n) {
         gp.ldo = D;
         gemm_simt<float, float>(pe_d, D, stg.p, n_rel, D, D, gp, e->stream);
         UD_TRY(dalloc_bytes(e, &w.ptab, static_cast<size_t>(n_rel) * D * e->esz));
-        if (e->bf) f32_to_bf16(ptab_f, static_cast<bf16*>(w.ptab), static_cast<size_t>(n_rel) * D, e->stream);
+        if (e->bf) {
+            f32_to_bf16(ptab_f, static_cast<bf16*>(w.ptab), static_cast<size_t>(n_rel) * D, e->stream);
+            w.has_pmap = make_tma_bf16(w.pmap, w.ptab, n_rel, D, D, 128);
+        }
         else UD_CK(cudaMemcpyAsync(w.ptab, ptab_f, sizeof(float) * n_rel * D, cudaMemcpyDeviceToDevice, e->stream));
         UD_CK(cudaStreamSynchronize(e->stream));
     }
@@ -1282,6 +1295,11 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
     if ((s = dalloc(e, &e->meta_graph_d, meta_n)) != UD_OK) return cleanup(s);
     if (const char* g = std::getenv("UD_GRAPHS")) e->graphs_on = std::atoi(g) != 0;
     if (const char* g = std::getenv("UD_TC2")) e->tc2_on = std::atoi(g) != 0;
+    if (const char* g = std::getenv("UD_ATTN_TMA")) e->attn_tma_on = std::atoi(g) != 0;
+    if (e->bf && c.n_layers > 0 && PF == 16)
+        e->attn_maps = make_tma_bf16(e->attn_qkv_map, e->qkv, static_cast<int>(Mc), 3 * e->D, 3 * e->D, 16) &&
+                       make_tma_pages(e->attn_k_map, cg.kpool, c.n_layers * n_pages, PF, e->D) &&
+                       make_tma_pages(e->attn_v_map, cg.vpool, c.n_layers * n_pages, PF, e->D);
     if ((s = halloc(e, &e->slots_h, meta_n)) != UD_OK) return cleanup(s);
     if ((s = dalloc(e, &e->slots_d, meta_n)) != UD_OK) return cleanup(s);
     if ((s = dalloc(e, &e->err_d, 1)) != UD_OK) return cleanup(s);

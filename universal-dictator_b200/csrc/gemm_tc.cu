@@ -236,6 +236,28 @@ bool make_tma_epi(TmaMatrix& t, const void* base, int rows, int cols, int ld, bo
     return true;
 }
 
+bool make_tma_pages(TmaMatrix& t, const void* base, int pages_total, int page_frames, int cols) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || cols % 64 != 0 || page_frames < 1 || page_frames > 256)
+        return false;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(page_frames),
+                          static_cast<cuuint64_t>(pages_total)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2, static_cast<cuuint64_t>(page_frames) * cols * 2};
+    cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(page_frames), 1u};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    CUresult r = enc(&t.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+    t.base = base;
+    t.rows = pages_total * page_frames;
+    t.cols = cols;
+    t.ld = cols;
+    t.box_rows = page_frames;
+    return true;
+}
+
 int gemm_tc_pick_bn(int M, int N, int num_sms) {
     const int num_m = (M + BM - 1) / BM;
     if (N % 256 == 0 && num_m * (N / 256) >= num_sms) return 256;

@@ -55,6 +55,10 @@ bool make_tma_bf16(TmaMatrix& t, const void* base, int rows, int cols, int ld, i
 // Epilogue blocks: 32 rows x 128 bytes (32 fp32 or 64 bf16 columns), 128-byte swizzle, for TMA stores of GEMM
 // outputs.
 bool make_tma_epi(TmaMatrix& t, const void* base, int rows, int cols, int ld, bool bf16);
+// K/V page pool [pages_total][page_frames][cols] bf16 as the 3-D tensor (column, frame, page): boxes of 64 columns x
+// page_frames frames x 1 page, 128-byte swizzle. A load may start at a negative or past-the-end frame or page
+// coordinate: those rows arrive as zeros.
+bool make_tma_pages(TmaMatrix& t, const void* base, int pages_total, int page_frames, int cols);
 int gemm_tc_pick_bn(int M, int N, int num_sms);
 void gemm_tc(const TmaMatrix& A, const TmaMatrix& W, int M, int N, int K, int bn, const GemmEpilogue& epi,
              int* dev_err, int num_sms, cudaStream_t s);
@@ -182,6 +186,14 @@ void pack_frames(const float* frames, int rows_stride, const BatchEntry* meta, i
                  cudaStream_t s);
 void scatter_rows(const float* src, const BatchEntry* meta, int n, float* dst, int tmax, int W, cudaStream_t s);
 size_t relpos_attention_smem_bytes(int tmax_batch, int L, int elem_bytes);
+// The bf16 attention as a persistent TMA-fed kernel (attention.cu): qkv [rows, 3 D] (box 64 x 16), the K and V page
+// pools (make_tma_pages, 16-frame pages) and this layer's position table (box 64 x 128, from row ptab_row0 =
+// tmax - 16). Returns false, launching nothing, when the shapes are outside its limits (chunks of more than 16
+// frames, pages of other than 16 frames, L + 15 beyond the 128 staged position rows).
+bool relpos_attention_tma(const TmaMatrix& qkv, const TmaMatrix& kpool, const TmaMatrix& vpool, const TmaMatrix& ptab,
+                          int ptab_row0, const float* bias_u, const float* bias_v, const BatchEntry* meta, int n,
+                          int tmax_batch, const CacheGeom& cg, int layer, bf16* out, int ldo, int n_heads, int num_sms,
+                          int* dev_err, cudaStream_t s);
 size_t rnnt_smem_bytes(const RnntWeights& w);
 
 // ---- misc

@@ -52,8 +52,19 @@ __device__ __forceinline__ void row_stats(const float (&v)[NV][4], int D, float&
     rstd = rsqrtf(var + 1e-5f);
 }
 
-// gamma/beta for one float4 of this lane's columns (4 KB vectors shared by every row: L1-resident).
-__device__ __forceinline__ void load_affine4(const float* __restrict__ g, const float* __restrict__ b, int c, float (&gg)[4],
+// Copies gamma and beta (D <= 1024 floats each) into shared memory: the CTA does it before it waits for the
+// previous kernel (they are weights), so the affine step after the row statistics reads shared memory instead of
+// making another round trip to L2.
+__device__ __forceinline__ void stage_affine(const float* __restrict__ g, const float* __restrict__ b, float* sg,
+                                             float* sb, int D) {
+    for (int c = threadIdx.x * 4; c < D; c += blockDim.x * 4) {
+        *reinterpret_cast<float4*>(sg + c) = *reinterpret_cast<const float4*>(g + c);
+        *reinterpret_cast<float4*>(sb + c) = *reinterpret_cast<const float4*>(b + c);
+    }
+}
+
+// gamma/beta for one float4 of this lane's columns.
+__device__ __forceinline__ void load_affine4(const float* g, const float* b, int c, float (&gg)[4],
                                              float (&bb)[4]) {
     const float4 g4 = *reinterpret_cast<const float4*>(g + c), b4 = *reinterpret_cast<const float4*>(b + c);
     gg[0] = g4.x; gg[1] = g4.y; gg[2] = g4.z; gg[3] = g4.w;
@@ -73,6 +84,9 @@ template <typename TO, int NV>
 __global__ void __launch_bounds__(256) ln_kernel(const float* x, const float* __restrict__ g,
                                                  const float* __restrict__ b, TO* y, int M, int D) {
     pdl_launch_dependents();
+    __shared__ __align__(16) float sg[1024], sb[1024];
+    stage_affine(g, b, sg, sb, D);
+    __syncthreads();
     pdl_wait();
     // x and y may alias (in-place): each warp reads its whole row before writing it.
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -86,7 +100,7 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* x, const float* __
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         float gg[4], bb[4], o[4];
-        load_affine4(g, b, (i * 32 + lane) * 4, gg, bb);
+        load_affine4(sg, sb, (i * 32 + lane) * 4, gg, bb);
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
         store4<TO>(yr + (i * 32 + lane) * 4, o);
@@ -98,6 +112,10 @@ __global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const f
                                                   const float* __restrict__ b1, const float* __restrict__ g2,
                                                   const float* __restrict__ b2, TO* __restrict__ y, int M, int D) {
     pdl_launch_dependents();
+    __shared__ __align__(16) float sg1[1024], sb1[1024], sg2[1024], sb2[1024];
+    stage_affine(g1, b1, sg1, sb1, D);
+    stage_affine(g2, b2, sg2, sb2, D);
+    __syncthreads();
     pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
@@ -110,7 +128,7 @@ __global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const f
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         float gg[4], bb[4];
-        load_affine4(g1, b1, (i * 32 + lane) * 4, gg, bb);
+        load_affine4(sg1, sb1, (i * 32 + lane) * 4, gg, bb);
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[i][j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
         *reinterpret_cast<float4*>(xr + (i * 32 + lane) * 4) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
@@ -120,7 +138,7 @@ __global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const f
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         float gg[4], bb[4], o[4];
-        load_affine4(g2, b2, (i * 32 + lane) * 4, gg, bb);
+        load_affine4(sg2, sb2, (i * 32 + lane) * 4, gg, bb);
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
         store4<TO>(yr + (i * 32 + lane) * 4, o);
