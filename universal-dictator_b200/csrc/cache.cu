@@ -3,48 +3,77 @@
 //
 // K/V: frame f of a stream lives at row f % PF of page pages[(f / PF) % kPageSlots] in the layer's pool;
 // the roll only advances `head`, so it moves no data. Conv: ring of conv_ring rows per (layer, slot),
-// frame f at row f % conv_ring. All copies are 16-byte vectors, one row per warp group, coalesced.
+// frame f at row f % conv_ring. All copies are 16-byte vectors, one row per warp, coalesced.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace ud {
 namespace {
 
-// grid (n, n_layers), 256 threads. kv_rows [n][NL][2][k][D], conv_rows [n][NL][k][D].
+// Rows are moved one warp per row: each lane copies up to kPer 16-byte chunks of the row (a bf16 row of 1024 is
+// 128 chunks, 4 per lane), all its loads issued before its stores, so a warp keeps a whole 2 KB row in flight and no
+// per-element index division is needed.
+constexpr int kPer = 8;   // chunks per lane: rows of up to 256 chunks (d_model 1024 in fp32)
+
 template <typename T>
-__global__ void append_kernel(const T* __restrict__ kv_rows, const T* __restrict__ conv_rows, int k,
+__device__ __forceinline__ void copy_row(T* __restrict__ dst, const T* __restrict__ src, int cpr, int lane) {
+    constexpr int CH = 16 / sizeof(T);
+    uint4 v[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = lane + 32 * i;
+        v[i] = (src && c < cpr) ? *reinterpret_cast<const uint4*>(src + c * CH) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int c = lane + 32 * i;
+        if (c < cpr) *reinterpret_cast<uint4*>(dst + c * CH) = v[i];
+    }
+}
+
+// Row f of a layer's K or V pool (nullptr, with the error recorded, when its page slot is unmapped).
+template <typename T>
+__device__ __forceinline__ T* pool_row(const CacheGeom& cg, int kind, int layer, const BatchEntry& me, int f, int* err) {
+    const int PF = cg.page_frames;
+    const int page = me.pages[(f / PF) % kPageSlots];
+    if (page < 0 || page >= cg.n_pages) {
+        report_error(err, DEV_BAD_PAGE);
+        return nullptr;
+    }
+    T* pool = reinterpret_cast<T*>(kind == 0 ? cg.kpool : cg.vpool);
+    return pool + ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * cg.D;
+}
+
+// One warp per appended row over the whole call (appends are a few rows per stream and layer, so a CTA per
+// (stream, layer) would leave most of its warps idle): row w of the call is (stream b, layer, r) with r in
+// [0, 2k) a K (r < k) or V row and r in [2k, 2k + kc) one of the last kc = min(k, R) conv rows.
+// kv_rows [n][NL][2][k][D], conv_rows [n][NL][k][D] (either may be null).
+template <typename T>
+__global__ void append_kernel(const T* __restrict__ kv_rows, const T* __restrict__ conv_rows, int k, int n,
                               const BatchEntry* __restrict__ meta, const CacheGeom cg, int* err) {
     constexpr int CH = 16 / sizeof(T);
-    const int b = blockIdx.x, layer = blockIdx.y;
-    const BatchEntry& me = meta[b];
-    const int D = cg.D, PF = cg.page_frames, NL = cg.n_layers, R = cg.conv_ring;
+    const int lane = threadIdx.x & 31;
+    const int D = cg.D, NL = cg.n_layers, R = cg.conv_ring;
     const int cpr = D / CH;
-    if (kv_rows) {
-        const T* src = kv_rows + (static_cast<size_t>(b) * NL + layer) * 2 * k * D;
-        for (int idx = threadIdx.x; idx < 2 * k * cpr; idx += blockDim.x) {
-            const int kind = idx / (k * cpr);
-            const int rem = idx % (k * cpr);
-            const int t = rem / cpr, c = (rem % cpr) * CH;
-            const int f = me.head + t;
-            const int page = me.pages[(f / PF) % kPageSlots];
-            if (page < 0 || page >= cg.n_pages) {
-                report_error(err, DEV_BAD_PAGE);
-                continue;
-            }
-            T* pool = reinterpret_cast<T*>(kind == 0 ? cg.kpool : cg.vpool);
-            const size_t off = ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + c;
-            *reinterpret_cast<uint4*>(pool + off) =
-                *reinterpret_cast<const uint4*>(src + (static_cast<size_t>(kind) * k + t) * D + c);
-        }
-    }
-    if (conv_rows) {
-        const T* src = conv_rows + (static_cast<size_t>(b) * NL + layer) * k * D;
-        T* ring = reinterpret_cast<T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
-        const int t0 = k > R ? k - R : 0;  // only the last R new frames survive
-        for (int idx = threadIdx.x; idx < (k - t0) * cpr; idx += blockDim.x) {
-            const int t = t0 + idx / cpr, c = (idx % cpr) * CH;
-            *reinterpret_cast<uint4*>(ring + static_cast<size_t>((me.head + t) % R) * D + c) =
-                *reinterpret_cast<const uint4*>(src + static_cast<size_t>(t) * D + c);
+    const int kc = conv_rows ? (k < R ? k : R) : 0;
+    const int kv = kv_rows ? 2 * k : 0;
+    const int per = kv + kc;   // rows per (stream, layer)
+    const long long total = static_cast<long long>(n) * NL * per;
+    for (long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < total;
+         w += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
+        const int r = static_cast<int>(w % per);
+        const long long bl = w / per;
+        const int layer = static_cast<int>(bl % NL), b = static_cast<int>(bl / NL);
+        const BatchEntry& me = meta[b];
+        if (r < kv) {
+            const int kind = r >= k ? 1 : 0, t = r - kind * k;
+            T* dst = pool_row<T>(cg, kind, layer, me, me.head + t, err);
+            if (dst) copy_row<T>(dst, kv_rows + ((static_cast<size_t>(b) * NL + layer) * 2 * k + r) * D, cpr, lane);
+        } else {
+            const int t = k - kc + (r - kv);   // only the last R new frames survive in the ring
+            T* ring = reinterpret_cast<T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
+            copy_row<T>(ring + static_cast<size_t>((me.head + t) % R) * D,
+                        conv_rows + ((static_cast<size_t>(b) * NL + layer) * k + t) * D, cpr, lane);
         }
     }
 }
@@ -55,39 +84,25 @@ __global__ void gather_kernel(T* __restrict__ kv_out, T* __restrict__ conv_out, 
                               const CacheGeom cg, int* err) {
     constexpr int CH = 16 / sizeof(T);
     const int b = blockIdx.x, layer = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const BatchEntry& me = meta[b];
-    const int D = cg.D, PF = cg.page_frames, NL = cg.n_layers, L = cg.L, R = cg.conv_ring;
+    const int D = cg.D, NL = cg.n_layers, L = cg.L, R = cg.conv_ring;
     const int cpr = D / CH;
     if (kv_out) {
         T* dst = kv_out + (static_cast<size_t>(b) * NL + layer) * 2 * L * D;
-        for (int idx = threadIdx.x; idx < 2 * L * cpr; idx += blockDim.x) {
-            const int kind = idx / (L * cpr);
-            const int rem = idx % (L * cpr);
-            const int j = rem / cpr, c = (rem % cpr) * CH;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (j >= L - me.cache_len) {
-                const int f = me.head - L + j;
-                const int page = me.pages[(f / PF) % kPageSlots];
-                if (page < 0 || page >= cg.n_pages) {
-                    report_error(err, DEV_BAD_PAGE);
-                } else {
-                    const T* pool = reinterpret_cast<const T*>(kind == 0 ? cg.kpool : cg.vpool);
-                    v = *reinterpret_cast<const uint4*>(
-                        pool + ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + (f % PF)) * D + c);
-                }
-            }
-            *reinterpret_cast<uint4*>(dst + (static_cast<size_t>(kind) * L + j) * D + c) = v;
+        const int lo = L - me.cache_len;
+        for (int row = warp; row < 2 * L; row += nw) {   // row = kind * L + j; window row j is frame head - L + j
+            const int kind = row >= L ? 1 : 0, j = row - kind * L;
+            const T* src = j >= lo ? pool_row<T>(cg, kind, layer, me, me.head - L + j, err) : nullptr;
+            copy_row<T>(dst + static_cast<size_t>(row) * D, src, cpr, lane);
         }
     }
     if (conv_out) {
         const T* ring =
             reinterpret_cast<const T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
         T* dst = conv_out + (static_cast<size_t>(b) * NL + layer) * R * D;
-        for (int idx = threadIdx.x; idx < R * cpr; idx += blockDim.x) {
-            const int i = idx / cpr, c = (idx % cpr) * CH;  // frame head - R + i
-            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(i) * D + c) =
-                *reinterpret_cast<const uint4*>(ring + static_cast<size_t>((me.head + i) % R) * D + c);
-        }
+        for (int i = warp; i < R; i += nw)   // frame head - R + i
+            copy_row<T>(dst + static_cast<size_t>(i) * D, ring + static_cast<size_t>((me.head + i) % R) * D, cpr, lane);
     }
 }
 
@@ -108,9 +123,12 @@ __global__ void conv_zero_kernel(const int* __restrict__ slots, const CacheGeom 
 template <typename T>
 void cache_append(const T* kv_rows, const T* conv_rows, int k, const BatchEntry* meta, int n, const CacheGeom& cg,
                   int* dev_err, cudaStream_t s) {
-    if (n <= 0 || k <= 0 || cg.n_layers <= 0) return;
-    dim3 grid(n, cg.n_layers);
-    append_kernel<T><<<grid, 256, 0, s>>>(kv_rows, conv_rows, k, meta, cg, dev_err);
+    if (n <= 0 || k <= 0 || cg.n_layers <= 0 || (!kv_rows && !conv_rows)) return;
+    const long long rows = static_cast<long long>(n) * cg.n_layers *
+                           ((kv_rows ? 2 * k : 0) + (conv_rows ? (k < cg.conv_ring ? k : cg.conv_ring) : 0));
+    const long long blocks = (rows + 7) / 8;   // 8 warps per block, one row each; the kernel strides beyond
+    const int grid = static_cast<int>(blocks < 65535LL * 16 ? blocks : 65535LL * 16);
+    append_kernel<T><<<grid, 256, 0, s>>>(kv_rows, conv_rows, k, n, meta, cg, dev_err);
 }
 
 template <typename T>
