@@ -184,6 +184,27 @@ def cpu_baseline(sd, R: int, budget_s: float = 12.0, max_steps: int = 40):
     return n / dt, torch.get_num_threads(), f"{n} consecutive stream-steps of one stream ({dt:.1f} s), [70,{R}], fp32, 24 layers + joint + greedy"
 
 
+def cpu_baseline_batched(sd, R: int, n: int):
+    """The batched-torch form of the same CPU step (oracle BatchEncoder: one vectorised step for all n streams,
+    fp32, all host threads): a first chunk for every stream (untimed), then one timed steady chunk of all n.
+    Returns (stream-steps/s, threads, sample text)."""
+    from oracle.stream_step import BatchEncoder, StreamState
+    from oracle.weights import NEMOTRON
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    benc = BatchEncoder(sd, NEMOTRON)
+    sts = [StreamState(NEMOTRON) for _ in range(n)]
+    first, chunk = 1 + 8 * R, 9 + 8 + 8 * R
+    mel = torch.randn(n, first + chunk, MEL, generator=torch.Generator().manual_seed(0))
+    with torch.inference_mode():
+        benc.batch_step(sts, mel[:, :first], first, first, R)
+        t0 = time.perf_counter()
+        benc.batch_step(sts, mel[:, first - 9:first - 9 + chunk], chunk, chunk, R)
+        dt = time.perf_counter() - t0
+    return n / dt, torch.get_num_threads(), (f"one steady chunk of all {n} streams in one batched step ({dt:.1f} s), "
+                                             f"[70,{R}], fp32, 24 layers + joint (oracle BatchEncoder)")
+
+
 def run_reference(args, world, rank):
     """Reference arm: rank 0 times the CPU restatement; other ranks exit without work."""
     if rank != 0:
@@ -463,7 +484,7 @@ def run_mel_bench(args, world, rank, local):
                                        "frac": gbs / hbm, "traffic": None, "kernel": "mel_kernel",
                                        "note": f"audio read once + mel written once per step / step time; peak = "
                                                f"{src} HBM copy"},
-                          "cpu_baseline": cpu, "clocks": clk.summary()}), flush=True)
+                          "cpu_baseline": cpu, "cpu_baseline_batched": cpu_b, "clocks": clk.summary()}), flush=True)
     fe.close()
     eng.close()
     if dist:
@@ -872,10 +893,13 @@ def main():
                 "note": "per-stream step time falls as the batch grows (the weights are read once per step), so "
                         "streams x budget / step time underestimates the streams one GPU keeps in real time"}
 
-    cpu = None
+    cpu = cpu_b = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_baseline(sd, R)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        if args.workload == "c3" and n <= 512:
+            v, cores, sample = cpu_baseline_batched(sd, R, n)
+            cpu_b = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
     roof_gemv = None
     if n * T <= 16:   # few rows: the projections run as GEMVs over the whole weight set (HBM-bound)
@@ -907,7 +931,7 @@ def main():
                                       "the timed region; each launch's time includes its own ramp and tail, which "
                                       "the graph overlaps with its neighbours, so roofline.achieved is a lower bound"),
                "cache_ops": cache_ops, "capacity": capacity,
-               "cpu_baseline": cpu, "clocks": clk.summary()}
+               "cpu_baseline": cpu, "cpu_baseline_batched": cpu_b, "clocks": clk.summary()}
         print(json.dumps(res), flush=True)
 
     eng.close()

@@ -232,6 +232,96 @@ class Encoder:
         return proj, keep, out, T, valid_t
 
 
+class BatchEncoder(Encoder):
+    """The same step for many streams at once, vectorised over the streams (a batched-torch form of
+    Encoder.stream_step, for the CPU baseline at the benchmark's batch). Every stream of a call must share the
+    chunk geometry: n_rows, valid_rows, the step counter (first chunk or not) and cacheLen, as the benchmark's
+    synchronous streams do. The arithmetic is stream_step's: the per-stream products become batched ones."""
+
+    def batch_step(self, sts: list[StreamState], mel: torch.Tensor, n_rows: int, valid_rows: int,
+                   lookahead: int) -> torch.Tensor:
+        """mel [B, n_rows, mel_bins] -> projections [B, keep, J]; every state advances one chunk."""
+        dims = self.dims
+        B = len(sts)
+        st0 = sts[0]
+        assert all(st.step == st0.step and st.cache_len == st0.cache_len for st in sts)
+        drop = 0 if st0.step == 0 else 2
+        T = sub_len(n_rows) - drop
+        valid_t = max(0, min(sub_len(valid_rows) - drop, T))
+        x = self.subsample_batch(mel[:, :n_rows], valid_rows)[:, drop:drop + T]
+        L, D, K = dims.left_context, dims.d_model, dims.conv_kernel
+        H, DK = dims.n_heads, dims.head_dim
+        lo, hi = L - st0.cache_len, L + valid_t
+        for li in range(dims.n_layers):
+            p = f"encoder.layers.{li}."
+            w = lambda n: self.w(p + n)  # noqa: E731
+            h = layer_norm(x, w("norm_feed_forward1.weight"), w("norm_feed_forward1.bias"))
+            x = x + 0.5 * F.linear(F.silu(F.linear(h, w("feed_forward1.linear1.weight"))), w("feed_forward1.linear2.weight"))
+            h = layer_norm(x, w("norm_self_att.weight"), w("norm_self_att.bias"))
+            q = F.linear(h, w("self_attn.linear_q.weight"))
+            k = torch.cat([torch.stack([st.k[li] for st in sts]), F.linear(h, w("self_attn.linear_k.weight"))], 1)
+            v = torch.cat([torch.stack([st.v[li] for st in sts]), F.linear(h, w("self_attn.linear_v.weight"))], 1)
+            att = torch.zeros(B, T, D)
+            if hi > lo:
+                ptab, rel_lo = self.pos_table(li, T)
+                u, vb = w("self_attn.pos_bias_u"), w("self_attn.pos_bias_v")
+                qh = q.view(B, T, H, DK).transpose(1, 2)                                 # [B, H, T, DK]
+                kh = k[:, lo:hi].reshape(B, hi - lo, H, DK).transpose(1, 2)
+                vh = v[:, lo:hi].reshape(B, hi - lo, H, DK).transpose(1, 2)
+                ac = (qh + u[None, :, None, :]) @ kh.transpose(2, 3)                     # [B, H, T, n]
+                i = torch.arange(T)[:, None]
+                j = torch.arange(lo, hi)[None, :]
+                rel = L + i - j - rel_lo
+                pg = ptab[rel].view(T, hi - lo, H, DK).permute(2, 0, 1, 3)               # [H, T, n, DK]
+                bd = torch.einsum("bhtd,htnd->bhtn", qh + vb[None, :, None, :], pg)
+                pr = torch.softmax((ac + bd) / math.sqrt(DK), dim=-1)
+                att = (pr @ vh).transpose(1, 2).reshape(B, T, D)
+            x = x + F.linear(att, w("self_attn.linear_out.weight"))
+            h = layer_norm(x, w("norm_conv.weight"), w("norm_conv.bias"))
+            g = F.glu(F.linear(h, w("conv.pointwise_conv1.weight")[:, :, 0]), dim=-1)
+            g[:, valid_t:] = 0
+            ci = torch.cat([torch.stack([st.conv[li] for st in sts]), g], 1)           # [B, K-1+T, D]
+            dw = w("conv.depthwise_conv.weight")[:, 0, :]                               # [D, K]
+            y = (ci.unfold(1, K, 1) * dw[None, None]).sum(-1)                           # [B, T, D]
+            y = F.silu(layer_norm(y, w("conv.batch_norm.weight"), w("conv.batch_norm.bias")))
+            x = x + F.linear(y, w("conv.pointwise_conv2.weight")[:, :, 0])
+            h = layer_norm(x, w("norm_feed_forward2.weight"), w("norm_feed_forward2.bias"))
+            x = x + 0.5 * F.linear(F.silu(F.linear(h, w("feed_forward2.linear1.weight"))), w("feed_forward2.linear2.weight"))
+            x = layer_norm(x, w("norm_out.weight"), w("norm_out.bias"))
+            for b, st in enumerate(sts):
+                st.k[li] = k[b, T:]
+                st.v[li] = v[b, T:]
+                st.conv[li] = ci[b, T:]
+        for st in sts:
+            st.cache_len = min(st.cache_len + T, L)
+            st.step += 1
+        keep = min(valid_t, lookahead + 1)
+        return F.linear(x[:, :keep], self.w("joint.enc.weight"), self.w("joint.enc.bias"))
+
+    def subsample_batch(self, mel: torch.Tensor, valid_rows: int) -> torch.Tensor:
+        """Encoder.subsample over a batch mel [B, Tin, mel_bins] -> [B, sub_len(Tin), D], one valid length."""
+        C = self.dims.sub_channels
+        p = "encoder.pre_encode."
+        v1 = next_len(valid_rows)
+        v2 = next_len(v1)
+        v3 = next_len(v2)
+
+        def mask(x, n):
+            x = x.clone()
+            x[:, :, max(n, 0):, :] = 0
+            return x
+
+        x = mask(mel[:, None].float(), valid_rows)
+        x = mask(F.relu(F.conv2d(F.pad(x, (2, 1, 2, 1)), self.w(p + "conv.0.weight"), self.w(p + "conv.0.bias"), stride=2)), v1)
+        x = F.conv2d(F.pad(x, (2, 1, 2, 1)), self.w(p + "conv.2.weight"), self.w(p + "conv.2.bias"), stride=2, groups=C)
+        x = mask(F.relu(F.conv2d(x, self.w(p + "conv.3.weight"), self.w(p + "conv.3.bias"))), v2)
+        x = F.conv2d(F.pad(x, (2, 1, 2, 1)), self.w(p + "conv.5.weight"), self.w(p + "conv.5.bias"), stride=2, groups=C)
+        x = mask(F.relu(F.conv2d(x, self.w(p + "conv.6.weight"), self.w(p + "conv.6.bias"))), v3)
+        b, c, t, f = x.shape
+        x = x.permute(0, 2, 1, 3).reshape(b, t, c * f)
+        return F.linear(x, self.w(p + "out.weight"), self.w(p + "out.bias"))
+
+
 def drain_next(lookahead: int, idx: int, have: int, final: bool, end_padding: bool):
     """One iteration of NemotronStreamer.drainChunks (NemotronStreamer.swift:109-154), the live chunk walk, for a
     stream that has consumed mel rows up to `idx` of the `have` it holds: returns None to wait (final False) or
