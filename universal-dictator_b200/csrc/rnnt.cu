@@ -307,6 +307,55 @@ __device__ __forceinline__ float dot2(const float* a, const float* x, const floa
     return warp_sum(acc);
 }
 
+// Y[s * ldy + r] = W[r] . X[s] for r < rows, s < ns: weight rows (row stride ldw) and vectors (stride ldx) in
+// shared memory, K a multiple of 4. A warp takes a tile of 4 rows x 8 vectors: its lanes split K in 16-byte
+// chunks, so each weight chunk loaded feeds 8 vectors and each vector chunk 4 rows (32 products per 12 loads);
+// the 32 partial sums are then reduced across the lanes by halving exchanges (31 shuffles), after which lane L
+// holds tile element L (row L / 8, vector L % 8).
+__device__ void tile_dots(const float* __restrict__ W, int ldw, int rows, const float* __restrict__ X, int ldx, int ns,
+                          int K, float* __restrict__ Y, int ldy) {
+    constexpr int TR = 4, TS = 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nrt = (rows + TR - 1) / TR, nst = (ns + TS - 1) / TS;
+    const int k4 = K / 4;
+    for (int tile = warp; tile < nrt * nst; tile += kLsWarps) {
+        const int r0 = (tile / nst) * TR, s0 = (tile % nst) * TS;
+        float v[TR * TS];
+#pragma unroll
+        for (int i = 0; i < TR * TS; ++i) v[i] = 0.f;
+        for (int c = lane; c < k4; c += 32) {
+            float4 wv[TR], xv[TS];
+#pragma unroll
+            for (int r = 0; r < TR; ++r)
+                wv[r] = r0 + r < rows ? reinterpret_cast<const float4*>(W + static_cast<size_t>(r0 + r) * ldw)[c]
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < TS; ++q)
+                xv[q] = s0 + q < ns ? reinterpret_cast<const float4*>(X + static_cast<size_t>(s0 + q) * ldx)[c]
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < TR; ++r)
+#pragma unroll
+                for (int q = 0; q < TS; ++q)
+                    v[r * TS + q] = fmaf(wv[r].x, xv[q].x, fmaf(wv[r].y, xv[q].y,
+                                    fmaf(wv[r].z, xv[q].z, fmaf(wv[r].w, xv[q].w, v[r * TS + q]))));
+        }
+        // halving exchanges: at distance o the lanes with bit o set keep the upper half of their values
+#pragma unroll
+        for (int o = 16, h = 16; o >= 1; o >>= 1, h >>= 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < h; ++i) {
+                const float send = up ? v[i] : v[i + h];
+                const float keep = up ? v[i + h] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        const int r = r0 + lane / TS, q = s0 + lane % TS;
+        if (r < rows && q < ns) Y[static_cast<size_t>(q) * ldy + r] = v[0];
+    }
+}
+
 struct LsGeom {
     int nu, nj, nv;     // hidden units, prediction rows and vocabulary rows per CTA
     int sb;             // streams per staged tile
@@ -433,19 +482,27 @@ __global__ void __launch_bounds__(kLsThreads, 1) rnnt_lockstep_kernel(
                         }
                         __syncthreads();
                         const int rows = 4 * nuk;
-                        for (int it = warp; it < rows * sb; it += kLsWarps) {
-                            const int lr = it / sb, s = it - lr * sb;
-                            const int q = lr / nuk, uu = lr - q * nuk;
-                            const float *ra, *rb;
-                            if (gm.wl_smem) {
-                                ra = Wl + (static_cast<size_t>(l * 4 + q) * gm.nu + uu) * H2;
-                                rb = ra + Hp;
-                            } else {
-                                ra = w.w_ih[l] + static_cast<size_t>(q * Hp + u0 + uu) * Hp;
-                                rb = w.w_hh[l] + static_cast<size_t>(q * Hp + u0 + uu) * Hp;
+                        if (gm.wl_smem) {
+                            // gate rows (q, uu) sit at Wl[l][q][uu] with stride nu rows per gate: one tiled pass per
+                            // gate over [w_ih ; w_hh] . [x ; h]
+                            for (int q = 0; q < 4; ++q)
+                                tile_dots(Wl + static_cast<size_t>(l * 4 + q) * gm.nu * H2, H2, nuk, X, XW, sb, H2,
+                                          Y + q * nuk, YW);
+                            __syncthreads();
+                            for (int i = tid; i < sb * rows; i += kLsThreads) {
+                                const int s = i / rows, lr = i - s * rows;
+                                const int q = lr / nuk, uu = lr - q * nuk;
+                                Y[s * YW + lr] += w.bias[l][q * Hp + u0 + uu];
                             }
-                            const float v = dot2(ra, X + s * XW, rb, X + s * XW + Hp, Hp, lane);
-                            if (lane == 0) Y[s * YW + lr] = v + w.bias[l][q * Hp + u0 + uu];
+                        } else {
+                            for (int it = warp; it < rows * sb; it += kLsWarps) {
+                                const int lr = it / sb, s = it - lr * sb;
+                                const int q = lr / nuk, uu = lr - q * nuk;
+                                const float* ra = w.w_ih[l] + static_cast<size_t>(q * Hp + u0 + uu) * Hp;
+                                const float* rb = w.w_hh[l] + static_cast<size_t>(q * Hp + u0 + uu) * Hp;
+                                const float v = dot2(ra, X + s * XW, rb, X + s * XW + Hp, Hp, lane);
+                                if (lane == 0) Y[s * YW + lr] = v + w.bias[l][q * Hp + u0 + uu];
+                            }
                         }
                         __syncthreads();
                         for (int i = tid; i < sb * nuk; i += kLsThreads) {
@@ -474,10 +531,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) rnnt_lockstep_kernel(
                         for (int c = lane; c < Hp / 4; c += 32) xr[c] = __ldcg(src + c);
                     }
                     __syncthreads();
-                    for (int it = warp; it < njk * sb; it += kLsWarps) {
-                        const int jj = it / sb, s = it - jj * sb;
-                        const float v = dot2(Wp + static_cast<size_t>(jj) * Hp, X + s * XW, nullptr, nullptr, Hp, lane);
-                        if (lane == 0) st.pend_g[static_cast<size_t>(meta[need[s0 + s]].slot) * J + j0 + jj] = v + w.pred_b[j0 + jj];
+                    tile_dots(Wp, Hp, njk, X, XW, sb, Hp, Y, YW);
+                    __syncthreads();
+                    for (int i = tid; i < sb * njk; i += kLsThreads) {
+                        const int s = i / njk, jj = i - s * njk;
+                        st.pend_g[static_cast<size_t>(meta[need[s0 + s]].slot) * J + j0 + jj] = Y[s * YW + jj] + w.pred_b[j0 + jj];
                     }
                     __syncthreads();
                 }
@@ -499,10 +557,11 @@ __global__ void __launch_bounds__(kLsThreads, 1) rnnt_lockstep_kernel(
                     }
                 }
                 __syncthreads();
-                for (int it = warp; it < nvk * sb; it += kLsWarps) {
-                    const int vv = it / sb, s = it - vv * sb;
-                    const float v = dot2(Wo + static_cast<size_t>(vv) * J, X + s * XW, nullptr, nullptr, J, lane);
-                    if (lane == 0) Y[s * YW + vv] = v + w.out_b[v0 + vv];
+                tile_dots(Wo, J, nvk, X, XW, sb, J, Y, YW);
+                __syncthreads();
+                for (int i = tid; i < sb * nvk; i += kLsThreads) {
+                    const int s = i / nvk, vv = i - s * nvk;
+                    Y[s * YW + vv] += w.out_b[v0 + vv];
                 }
                 __syncthreads();
                 for (int s = warp; s < sb; s += kLsWarps) {
