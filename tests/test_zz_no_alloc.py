@@ -1,9 +1,9 @@
 """ud_rnnt_decode_static (scratch in the library's static device block, no allocation in the call) against
 ud_rnnt_decode on the same engine: two streams with identical weights and inputs, one decoded through each entry
 point, two calls in a row with the decoder state carried between them; plus the size limit, and that a warm call
-leaves the device's free memory unchanged. Both decoder kernels are covered: the lock-step one (the default for
-small batches) and one CTA per stream (UD_RNNT_LOCKSTEP=0, read when the engine is created). Collected last so it
-also runs after every other GPU test in one process."""
+leaves the device's free memory unchanged. Every decoder kernel is covered: the tensor-core lock-step one (the
+default), the fp32 lock-step one (UD_RNNT_TC=0) and one CTA per stream (UD_RNNT_LOCKSTEP=0); the variables are read
+when the engine is created. Collected last so it also runs after every other GPU test in one process."""
 
 import numpy as np
 import pytest
@@ -16,9 +16,10 @@ from oracle.weights import ModelDims, make_weights, sharpen_joint
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("lockstep", ["1", "0"])
-def test_static_scratch_decode_matches_existing_entry_point(lockstep, monkeypatch):
+@pytest.mark.parametrize("lockstep,tc", [("1", "1"), ("1", "0"), ("0", "0")], ids=["tensor", "lockstep", "per_stream"])
+def test_static_scratch_decode_matches_existing_entry_point(lockstep, tc, monkeypatch):
     monkeypatch.setenv("UD_RNNT_LOCKSTEP", lockstep)
+    monkeypatch.setenv("UD_RNNT_TC", tc)
     dims = ModelDims(n_layers=0, sub_channels=0, pred_layers=2)
     sd = sharpen_joint(make_weights(dims, seed=3), dims, 77)
     e = ud.Engine(ud.default_config(n_layers=0, sub_channels=0, pred_layers=2, max_streams=8, max_batch=8,

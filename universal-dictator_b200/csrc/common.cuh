@@ -22,6 +22,7 @@ enum DeviceError : int {
     DEV_TIMEOUT_TEST = 6,       // the failure-detection test wait
     DEV_TIMEOUT_GRID = 7,       // RNN-T: waiting at a grid barrier of the lock-step decoder
     DEV_TIMEOUT_ATTN = 8,       // attention: waiting for a staged item or a free stage
+    DEV_RANGE_F16 = 9,          // RNN-T tensor-core decoder: an operand value beyond the fp16 range
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T v);

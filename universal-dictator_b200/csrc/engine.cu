@@ -97,6 +97,7 @@ struct ud_engine {
     RnntWeights rw{};
     RnntState rs{};
     RnntScratch rscr{};          // lock-step decoder scratch
+    RnntTc rtc{};                // tensor-core decoder operands
     bool rnnt_lockstep = true;   // UD_RNNT_LOCKSTEP=0: one CTA per stream instead
 
     CacheGeom cg{};
@@ -316,9 +317,11 @@ ud_status device_error_status(ud_engine* e, int code) {
     UD_CK(cudaStreamSynchronize(e->stream));
     static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
                                   "GEMM TMEM drain wait", "unmapped cache page", "test wait",
-                                  "RNN-T grid barrier wait", "attention stage wait"};
-    const char* nm = (code >= 0 && code <= 8) ? names[code] : "unknown";
-    if (code == DEV_BAD_PAGE) return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
+                                  "RNN-T grid barrier wait", "attention stage wait",
+                                  "RNN-T decoder input beyond the fp16 range"};
+    const char* nm = (code >= 0 && code <= 9) ? names[code] : "unknown";
+    if (code == DEV_BAD_PAGE || code == DEV_RANGE_F16)
+        return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
     return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
 }
 
@@ -910,6 +913,47 @@ ud_status load_weights_impl(ud_engine* e, const ud_weight* table, int n) {
         r.J = J;
         r.V = V;
         r.max_symbols = c.max_symbols;
+        // The tensor-core decoder's fp16 pairs of the same weights (kept off if a value is beyond the fp16 range).
+        RnntTc& tc = e->rtc;
+        tc.weights_ok = false;
+        if (e->rscr.tc) {
+            bool ok = true;
+            UD_TRY(need(t, "decoder.prediction.embed.weight", {V, Hp}, &p));
+            for (size_t i = 0; ok && i < static_cast<size_t>(V) * Hp; ++i) ok = std::fabs(p[i]) < 65504.f;
+            const size_t nl = static_cast<size_t>(4) * Hp * 2 * Hp;
+            std::vector<uint16_t> hi, lo;
+            auto up = [&](uint16_t** dst, const std::vector<uint16_t>& v) -> ud_status {
+                UD_TRY(dalloc(e, dst, v.size()));
+                UD_CK(cudaMemcpyAsync(*dst, v.data(), v.size() * 2, cudaMemcpyHostToDevice, e->stream));
+                UD_CK(cudaStreamSynchronize(e->stream));   // v is reused
+                return UD_OK;
+            };
+            for (int l = 0; ok && l < c.pred_layers; ++l) {
+                const std::string s = "decoder.prediction.dec_rnn.lstm.";
+                const std::string sl = std::to_string(l);
+                const float *wi, *wh;
+                UD_TRY(need(t, s + "weight_ih_l" + sl, {4 * Hp, Hp}, &wi));
+                UD_TRY(need(t, s + "weight_hh_l" + sl, {4 * Hp, Hp}, &wh));
+                hi.assign(nl, 0);
+                lo.assign(nl, 0);
+                ok = rnnt_tc_split_lstm(wi, wh, Hp, hi.data(), lo.data());
+                if (ok) { UD_TRY(up(&tc.wl_hi[l], hi)); UD_TRY(up(&tc.wl_lo[l], lo)); }
+            }
+            const char* names[2] = {"joint.pred.weight", "joint.joint_net.2.weight"};
+            const size_t rows[2] = {static_cast<size_t>(J), static_cast<size_t>(V)};
+            const size_t cols[2] = {static_cast<size_t>(Hp), static_cast<size_t>(J)};
+            uint16_t** his[2] = {&tc.wp_hi, &tc.wo_hi};
+            uint16_t** los[2] = {&tc.wp_lo, &tc.wo_lo};
+            for (int m = 0; ok && m < 2; ++m) {
+                UD_TRY(need(t, names[m], {static_cast<int>(rows[m]), static_cast<int>(cols[m])}, &p));
+                hi.assign(rows[m] * cols[m], 0);
+                lo.assign(rows[m] * cols[m], 0);
+                ok = rnnt_tc_split(p, hi.size(), hi.data(), lo.data());
+                if (ok) { UD_TRY(up(his[m], hi)); UD_TRY(up(los[m], lo)); }
+            }
+            tc.weights_ok = ok;
+            tc.bn_lstm = tc.bn_pred = tc.bn_joint = 0;   // weight maps are rebuilt at the next launch
+        }
     }
     UD_CK(cudaStreamSynchronize(e->stream));
     UD_CK(cudaGetLastError());
@@ -1326,6 +1370,26 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
         if ((s = dalloc(e, &q.emitted, q.max_n)) != UD_OK) return cleanup(s);
         if ((s = dalloc(e, &q.part_val, parts)) != UD_OK) return cleanup(s);
         if ((s = dalloc(e, &q.part_idx, parts)) != UD_OK) return cleanup(s);
+        // Tensor-core decoder rows (UD_RNNT_TC=0 leaves it off; UD_RNNT_TC=n takes batches of n streams and up).
+        if (const char* g = std::getenv("UD_RNNT_TC")) q.tc_min_n = std::atoi(g);
+        if (q.tc_min_n > 0 && Hp % 64 == 0 && c.joint_dim % 64 == 0 && NLp <= 4) {
+            RnntTc& tc = e->rtc;
+            tc.n_pad = (q.max_n + 127) / 128 * 128;
+            const size_t NP = tc.n_pad;
+            for (size_t l = 0; l < NLp; ++l) {
+                if ((s = dalloc(e, &tc.xl_hi[l], NP * 2 * Hp)) != UD_OK) return cleanup(s);
+                if ((s = dalloc(e, &tc.xl_lo[l], NP * 2 * Hp)) != UD_OK) return cleanup(s);
+                cudaMemsetAsync(tc.xl_hi[l], 0, NP * 2 * Hp * 2, e->stream);
+                cudaMemsetAsync(tc.xl_lo[l], 0, NP * 2 * Hp * 2, e->stream);
+            }
+            uint16_t** rows[4] = {&tc.xp_hi, &tc.xp_lo, &tc.xj_hi, &tc.xj_lo};
+            const size_t widths[4] = {Hp, Hp, static_cast<size_t>(c.joint_dim), static_cast<size_t>(c.joint_dim)};
+            for (int i = 0; i < 4; ++i) {
+                if ((s = dalloc(e, rows[i], NP * widths[i])) != UD_OK) return cleanup(s);
+                cudaMemsetAsync(*rows[i], 0, NP * widths[i] * 2, e->stream);
+            }
+            if (rnnt_tc_build_row_maps(tc, static_cast<int>(NLp), static_cast<int>(Hp), c.joint_dim)) q.tc = &tc;
+        }
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(UD_ERR_CUDA, "device synchronize failed"));
     scratch_engine_added(device);

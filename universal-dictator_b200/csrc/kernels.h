@@ -174,12 +174,46 @@ struct RnntScratch {
     int* part_idx = nullptr;                // [max_n * max_grid] their vocabulary ids
     int max_n = 0, max_grid = 0;
     int lockstep_max_n = 64;   // larger batches decode faster with one CTA per stream (grid full, weights in L2)
+    int tc_min_n = 1;          // batches of at least this many streams decode on the tensor cores; 0: never
+    struct RnntTc* tc = nullptr;   // operands of the tensor-core decoder (null: off)
 };
-// Greedy decoding of n streams. With scr, n <= scr->lockstep_max_n and weights whose slices fit in shared
-// memory the lock-step kernel runs on min(num_sms, scr->max_grid) CTAs; otherwise one CTA per stream.
+// Operands of the tensor-core decoder (rnnt_tc.cu). Each fp32 value x is carried as two fp16 values,
+// hi = fp16(x) and lo = fp16((x - hi) * 2^11), so x = hi + lo * 2^-11 to within 2^-22 |x|.
+struct RnntTc {
+    // The weights, split at load: LSTM layer l as [4Hp][2Hp], rows unit-major (row 4u + q is gate q of unit u),
+    // K = [w_ih row ; w_hh row]; joint.pred [J][Hp]; the joint output [V][J].
+    uint16_t* wl_hi[4] = {};
+    uint16_t* wl_lo[4] = {};
+    uint16_t *wp_hi = nullptr, *wp_lo = nullptr, *wo_hi = nullptr, *wo_lo = nullptr;
+    bool weights_ok = false;   // split, with every weight and embedding value inside the fp16 range
+    // Per-stream operand rows in batch order (n_pad rows, zero at allocation): the LSTM inputs [x_l ; h_l], the
+    // prediction input h_top and the joint input relu(f_t + g).
+    uint16_t* xl_hi[4] = {};
+    uint16_t* xl_lo[4] = {};
+    uint16_t *xp_hi = nullptr, *xp_lo = nullptr, *xj_hi = nullptr, *xj_lo = nullptr;
+    int n_pad = 0;
+    TmaMatrix m_xl_hi[4], m_xl_lo[4], m_xp_hi, m_xp_lo, m_xj_hi, m_xj_lo;   // boxes of 128 rows
+    bool maps_ok = false;
+    TmaMatrix m_wl_hi[4], m_wl_lo[4], m_wp_hi, m_wp_lo, m_wo_hi, m_wo_lo;   // boxes of one slice width
+    int bn_lstm = 0, bn_pred = 0, bn_joint = 0;                             // slice widths of those maps
+};
+// Host splits of weights into the decoder's pairs (hi, lo of `count` values; the LSTM as unit-major [4Hp][2Hp]
+// rows); false if a value is beyond the fp16 range.
+bool rnnt_tc_split(const float* w, size_t count, uint16_t* hi, uint16_t* lo);
+bool rnnt_tc_split_lstm(const float* w_ih, const float* w_hh, int Hp, uint16_t* hi, uint16_t* lo);
+// The tensor maps of the operand rows (after the row buffers are allocated).
+bool rnnt_tc_build_row_maps(RnntTc& tc, int layers, int Hp, int J);
+// Greedy decoding of n streams. With scr: batches of at least scr->tc_min_n streams run the tensor-core lock-step
+// decoder (rnnt_tc.cu) when its shape limits hold; else, with n <= scr->lockstep_max_n and weights whose slices fit
+// in shared memory, the fp32 lock-step kernel on min(num_sms, scr->max_grid) CTAs; otherwise one CTA per stream.
 void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, int ld_proj, const BatchEntry* meta,
                  int n, int32_t* tokens, int tok_stride, int* n_tokens, const RnntScratch* scr, int num_sms,
                  int* dev_err, cudaStream_t s);
+// The tensor-core lock-step decoder; returns false, launching nothing, outside its limits (operands split and mapped,
+// Hp and J multiples of 64, at most 4 LSTM layers, n <= scr.max_n and the row buffers, V <= 16 x grid).
+bool rnnt_greedy_tc(const RnntWeights& w, const RnntState& st, const float* proj, int ld_proj, const BatchEntry* meta,
+                    int n, int32_t* tokens, int tok_stride, int* n_tokens, const RnntScratch& scr, int num_sms,
+                    int* dev_err, cudaStream_t s);
 void rnnt_reset(const RnntState& st, const int* slots, int n, const RnntWeights& w, cudaStream_t s);
 
 void pack_frames(const float* frames, int rows_stride, const BatchEntry* meta, int n, int tmax, float* x, int D,

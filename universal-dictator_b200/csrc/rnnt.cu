@@ -10,8 +10,7 @@
 // carries across calls. argmax keeps the first maximum (RNNT.swift:138-140).
 #include <algorithm>
 
-#include "common.cuh"
-#include "kernels.h"
+#include "rnnt_common.cuh"
 
 namespace ud {
 namespace {
@@ -56,8 +55,6 @@ __device__ void matvec(const float* __restrict__ W1, const float* __restrict__ x
         }
     }
 }
-
-__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + expf(-x)); }
 
 __global__ void __launch_bounds__(kThreads) rnnt_kernel(const RnntWeights w, const RnntState st,
                                                         const float* __restrict__ proj, int ld_proj,
@@ -258,38 +255,6 @@ __global__ void rnnt_reset_kernel(const RnntState st, const int* __restrict__ sl
 // emits, commits the LSTM state and marks the stream's progress. Data written by other CTAs during the launch is
 // read through L2 (ld.global.cg).
 
-constexpr int kLsThreads = 512;
-constexpr int kLsWarps = kLsThreads / 32;
-
-__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Grid barrier: all CTAs of the launch are resident (one per SM at most, grid <= SM count). Returns false (and
-// records DEV_TIMEOUT_GRID) when the wait exceeds kWaitLimitNs; the caller then leaves the kernel.
-__device__ bool grid_sync(unsigned long long* ctr, unsigned long long& target, int* err, volatile int* s_fail) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        target += gridDim.x;
-        __threadfence();
-        atomicAdd(ctr, 1ull);
-        const uint64_t t0 = global_timer_ns();
-        while (ld_acquire_u64(ctr) < target) {
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
-                report_error(err, DEV_TIMEOUT_GRID);
-                *s_fail = 1;
-                break;
-            }
-            __nanosleep(32);
-        }
-        __threadfence();
-    }
-    __syncthreads();
-    return *s_fail == 0;
-}
-
 // Dot product of one weight row [a ; b] (len each) with [x ; y], lanes over float4 chunks; full sum in every lane.
 __device__ __forceinline__ float dot2(const float* a, const float* x, const float* b, const float* y, int len,
                                       int lane) {
@@ -361,38 +326,6 @@ struct LsGeom {
     int sb;             // streams per staged tile
     int wl_smem;        // LSTM slices in shared memory (else read from global)
 };
-
-// Appends the streams b (in order) that are still in frame t, and those of them without a pending prediction.
-__device__ void ls_lists(const BatchEntry* meta, int n, int t, const RnntState& st, const RnntScratch& scr, int* act,
-                         int* need, int* s_cnt, int* s_wa, int* s_wn) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    int na = 0, nn = 0;
-    for (int b0 = 0; b0 < n; b0 += kLsThreads) {
-        const int b = b0 + tid;
-        bool fa = false, fn = false;
-        if (b < n && t < meta[b].keep && __ldcg(scr.done_frame + b) <= t) {
-            fa = true;
-            fn = __ldcg(st.pend_valid + meta[b].slot) == 0;
-        }
-        const unsigned ba = __ballot_sync(0xffffffffu, fa), bn = __ballot_sync(0xffffffffu, fn);
-        if (lane == 0) { s_wa[warp] = __popc(ba); s_wn[warp] = __popc(bn); }
-        __syncthreads();
-        int pa = na, pn = nn, ta = 0, tn = 0;
-        for (int w = 0; w < kLsWarps; ++w) {
-            if (w < warp) { pa += s_wa[w]; pn += s_wn[w]; }
-            ta += s_wa[w];
-            tn += s_wn[w];
-        }
-        const unsigned lt = (1u << lane) - 1u;
-        if (fa) act[pa + __popc(ba & lt)] = b;
-        if (fn) need[pn + __popc(bn & lt)] = b;
-        na += ta;
-        nn += tn;
-        __syncthreads();
-    }
-    if (tid == 0) { s_cnt[0] = na; s_cnt[1] = nn; }
-    __syncthreads();
-}
 
 __global__ void __launch_bounds__(kLsThreads, 1) rnnt_lockstep_kernel(
     const RnntWeights w, const RnntState st, const float* __restrict__ proj, int ld_proj,
@@ -589,48 +522,7 @@ __global__ void __launch_bounds__(kLsThreads, 1) rnnt_lockstep_kernel(
             // ---- decide, by the owner CTA of each active stream
             for (int i = warp; i < na; i += kLsWarps) {
                 const int b = act[i];
-                if (b % G != k) continue;
-                float bv = -INFINITY;
-                int bi = 0x7fffffff;
-                for (int kk = lane; kk < G; kk += 32) {
-                    const float v = __ldcg(scr.part_val + static_cast<size_t>(b) * G + kk);
-                    const int ix = __ldcg(scr.part_idx + static_cast<size_t>(b) * G + kk);
-                    if (v > bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-                }
-                const int slot = meta[b].slot;
-                if (bi == blank) {
-                    if (lane == 0) {
-                        st.pend_valid[slot] = 1;
-                        scr.done_frame[b] = t + 1;
-                        scr.emitted[b] = 0;
-                    }
-                } else {
-                    for (int x = lane; x < NLp * Hp; x += 32) {
-                        const size_t o = static_cast<size_t>(slot) * NLp * Hp + x;
-                        st.h[o] = __ldcg(st.pend_h + o);
-                        st.c[o] = __ldcg(st.pend_c + o);
-                    }
-                    if (lane == 0) {
-                        const int nt = __ldcg(n_tokens + b);
-                        tokens[static_cast<size_t>(b) * tok_stride + nt] = bi;
-                        n_tokens[b] = nt + 1;
-                        st.last_tok[slot] = bi;
-                        st.pend_valid[slot] = 0;
-                        const int em = __ldcg(scr.emitted + b) + 1;
-                        if (em >= w.max_symbols) {
-                            scr.done_frame[b] = t + 1;
-                            scr.emitted[b] = 0;
-                        } else {
-                            scr.emitted[b] = em;
-                        }
-                    }
-                }
+                if (b % G == k) ls_decide(b, t, G, meta, st, scr, NLp, Hp, blank, w.max_symbols, tokens, tok_stride, n_tokens);
             }
             if (!grid_sync(scr.barrier, target, err, &s_fail)) return;
         }
@@ -647,6 +539,9 @@ void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, i
                  int n, int32_t* tokens, int tok_stride, int* n_tokens, const RnntScratch* scr, int num_sms,
                  int* dev_err, cudaStream_t s) {
     if (n <= 0) return;
+    if (scr && scr->tc_min_n > 0 && n >= scr->tc_min_n &&
+        rnnt_greedy_tc(w, st, proj, ld_proj, meta, n, tokens, tok_stride, n_tokens, *scr, num_sms, dev_err, s))
+        return;
     if (scr && scr->barrier && n <= scr->max_n && n <= scr->lockstep_max_n && w.Hp % 4 == 0 && w.J % 4 == 0 &&
         ld_proj % 4 == 0 && (reinterpret_cast<uintptr_t>(proj) & 15) == 0 && w.max_symbols > 0) {
         const int G = std::min(num_sms, scr->max_grid);
