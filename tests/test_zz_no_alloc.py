@@ -1,9 +1,9 @@
 """ud_rnnt_decode_static (scratch in the library's static device block, no allocation in the call) against
 ud_rnnt_decode on the same engine: two streams with identical weights and inputs, one decoded through each entry
 point, two calls in a row with the decoder state carried between them; plus the size limit, and that a warm call
-leaves the device's free memory unchanged. Every decoder kernel is covered: the tensor-core lock-step one (the
-default), the fp32 lock-step one (UD_RNNT_TC=0) and one CTA per stream (UD_RNNT_LOCKSTEP=0); the variables are read
-when the engine is created. Collected last so it also runs after every other GPU test in one process."""
+leaves the device's free memory unchanged. Every decoder kernel is covered: the tensor-core lock-step one
+(UD_RNNT_TC=1 puts every batch size on it; by default it takes batches of 20 streams and up), the fp32 lock-step one
+(UD_RNNT_TC=0) and one CTA per stream (UD_RNNT_LOCKSTEP=0); the variables are read when the engine is created. Collected last so it also runs after every other GPU test in one process."""
 
 import numpy as np
 import pytest

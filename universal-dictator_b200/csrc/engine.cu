@@ -1370,7 +1370,8 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
         if ((s = dalloc(e, &q.emitted, q.max_n)) != UD_OK) return cleanup(s);
         if ((s = dalloc(e, &q.part_val, parts)) != UD_OK) return cleanup(s);
         if ((s = dalloc(e, &q.part_idx, parts)) != UD_OK) return cleanup(s);
-        // Tensor-core decoder rows (UD_RNNT_TC=0 leaves it off; UD_RNNT_TC=n takes batches of n streams and up).
+        // Tensor-core decoder rows (UD_RNNT_TC=0 leaves it off; UD_RNNT_TC=n takes batches of n streams and up,
+        // 20 by default).
         if (const char* g = std::getenv("UD_RNNT_TC")) q.tc_min_n = std::atoi(g);
         if (q.tc_min_n > 0 && Hp % 64 == 0 && c.joint_dim % 64 == 0 && NLp <= 4) {
             RnntTc& tc = e->rtc;

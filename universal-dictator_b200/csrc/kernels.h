@@ -174,7 +174,8 @@ struct RnntScratch {
     int* part_idx = nullptr;                // [max_n * max_grid] their vocabulary ids
     int max_n = 0, max_grid = 0;
     int lockstep_max_n = 64;   // larger batches decode faster with one CTA per stream (grid full, weights in L2)
-    int tc_min_n = 1;          // batches of at least this many streams decode on the tensor cores; 0: never
+    int tc_min_n = 20;         // batches of at least this many streams decode on the tensor cores (below it the fp32
+                               // lock-step kernel is faster: the per-iteration cost of the tensor-core one is fixed)
     struct RnntTc* tc = nullptr;   // operands of the tensor-core decoder (null: off)
 };
 // Operands of the tensor-core decoder (rnnt_tc.cu). Each fp32 value x is carried as two fp16 values,
