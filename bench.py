@@ -514,9 +514,12 @@ def run_streamer_bench(args, world, rank, local):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    cfg = ud.default_config(max_streams=slots, max_batch=slots, max_chunk_frames=16)
+    cfg = ud.default_config(max_streams=slots, max_batch=slots, max_chunk_frames=16,
+                            **({"n_layers": args.layers} if args.layers else {}))
     eng = ud.Engine(cfg, device=local)
     sd = make_weights(NEMOTRON, seed=0)
+    if args.layers:   # the first args.layers encoder layers
+        sd = {k: v for k, v in sd.items() if ".layers." not in k or int(k.split(".layers.")[1].split(".")[0]) < args.layers}
     sd["joint.joint_net.2.bias"][NEMOTRON.blank] += args.blank_offset
     eng.load_weights(sd)
     st = ud.Streamer(eng, R, decode=True)
@@ -683,6 +686,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--streams", type=int, default=256)
     ap.add_argument("--lookahead", type=int, default=13)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="c4: encoder layers (0: the model's 24). Fewer layers keep a profile of the RNN-T decoder "
+                         "small on the device; not a benchmark configuration")
     ap.add_argument("--decode", action="store_true",
                     help="also run greedy RNN-T decoding in each step (configs 2 and 4; C3 is the encoder step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
