@@ -544,13 +544,11 @@ struct Lay {
     static constexpr uint32_t STAGE = 4 * HALF_KV + 2 * kTM * 128;     // K0 K1 V0 V1 Q0 Q1
     static constexpr uint32_t P = 0;                                   // position rows, two 64-column halves
     static constexpr uint32_t S0 = 2 * kPRows * 128;
-    static constexpr uint32_t QU = S0 + 2 * STAGE;                     // queries + pos_bias_u (bf16, padded rows)
-    static constexpr uint32_t QV = QU + kTM * RSB * 2;                 // queries + pos_bias_v
-    static constexpr uint32_t AC = QV + kTM * RSB * 2;
+    static constexpr uint32_t AC = S0 + 2 * STAGE;
     static constexpr uint32_t BD = AC + kTM * ACW * 4;
     static constexpr uint32_t PB = BD + kTM * BDW * 4;
-    static constexpr uint32_t KROW = PB + kTM * PSW * 2;               // staged row of each key
-    static constexpr uint32_t BIAS = KROW + kNKP * 4;                  // this head's pos_bias_u, pos_bias_v (fp32)
+    static constexpr uint32_t KROW = PB + kTM * PSW * 2;               // staged row of each key, per stage
+    static constexpr uint32_t BIAS = KROW + 2 * kNKP * 4;              // this head's pos_bias_u, pos_bias_v (fp32)
     static constexpr uint32_t WIN = BIAS + 2 * 128 * 4;                // the item window of each stage
     static constexpr uint32_t ZERO = (WIN + 2 * sizeof(Window) + 127) / 128 * 128;   // one zero row (256 bytes)
     static constexpr uint32_t BAR = ZERO + 256;
@@ -565,6 +563,14 @@ static_assert(Lay::SMEM <= 232448, "shared memory of the TMA attention kernel");
 __device__ __forceinline__ const uint8_t* chunk_addr(const uint8_t* region, int rows, int r, int c, const uint8_t* zero) {
     if (r < 0) return zero + ((c & 7) << 4);
     return region + (c >> 3) * rows * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+// Two bf16 values (a packed pair) plus two fp32 biases, rounded back to a bf16 pair.
+__device__ __forceinline__ uint32_t add_bias2(uint32_t x, float2 bv) {
+    __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&x);
+    const float2 f = __bfloat1622float2(v);
+    const __nv_bfloat162 r = __floats2bfloat162_rn(f.x + bv.x, f.y + bv.y);
+    return *reinterpret_cast<const uint32_t*>(&r);
 }
 
 __device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory"); }
@@ -643,60 +649,76 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
     pdl_wait();   // the QKV projection and the step's metadata come from earlier work on the stream
 
     if (warp == kComputeWarps) {
-        // ---------------------------------------------------------------- producer
-        if (lane == 0) {
-            int cur_h = -1;
-            for (int k = 0; first + k < last; ++k) {
-                const int item = first + k, h = item / n, b = item - h * n, s = k & 1;
+        // ---------------------------------------------------------------- producer warp
+        // Lane 0 issues the copies; the whole warp reads the next item's window (before waiting for its stage, so
+        // the metadata load overlaps the wait) and writes the stage's key -> staged-row table.
+        int cur_h = -1;
+        for (int k = 0; first + k < last; ++k) {
+            const int item = first + k, h = item / n, b = item - h * n, s = k & 1;
+            const Window wv = window_of(meta[b], L);
+            int ok = 1;
+            if (lane == 0) {
                 if (h != cur_h) {
                     // the staged position rows are rewritten once every item of the previous head is done
                     if (cur_h >= 0 &&
                         !mbar_wait_bounded(&empty[(k - 1) & 1], ((k - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v))
-                        break;
-                    mbar_arrive_expect_tx(pfull, 2 * kPRows * 128);
-                    tma_load_2d(sm + Lay::P, &mp, pfull, h * DKk, ptab_row0);
-                    tma_load_2d(sm + Lay::P + kPRows * 128, &mp, pfull, h * DKk + 64, ptab_row0);
-                    cur_h = h;
+                        ok = 0;
+                    if (ok) {
+                        mbar_arrive_expect_tx(pfull, 2 * kPRows * 128);
+                        tma_load_2d(sm + Lay::P, &mp, pfull, h * DKk, ptab_row0);
+                        tma_load_2d(sm + Lay::P + kPRows * 128, &mp, pfull, h * DKk + 64, ptab_row0);
+                    }
                 }
-                if (k >= 2 && !mbar_wait_bounded(&empty[s], ((k - 2) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v)) break;
-                Window& w = reinterpret_cast<Window*>(sm + Lay::WIN)[s];
-                w = window_of(meta[b], L);   // published to the compute warps by the arrive below
-                uint8_t* st = sm + Lay::S0 + s * Lay::STAGE;
-                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>((w.npg + 1) * 4 * 2048 + 2 * 2048));
-                for (int bx = 0; bx < w.npg; ++bx) {
-                    const int pg = w.p_first + bx;
-                    const int page = w.pages[pg % kPageSlots];
+                if (ok && k >= 2 && !mbar_wait_bounded(&empty[s], ((k - 2) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v))
+                    ok = 0;
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            cur_h = h;
+            int* kr = reinterpret_cast<int*>(sm + Lay::KROW) + s * kNKP;
+            for (int j = lane; j < kNKP; j += 32) kr[j] = key_row(wv, L, j);
+            // The window and the table are published to the compute warps by the stage's full barrier: lane 0's
+            // arrive (which also sets the expected bytes) follows them and precedes every copy.
+            if (lane == 0) {
+                reinterpret_cast<Window*>(sm + Lay::WIN)[s] = wv;
+                mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>((wv.npg + 1) * 4 * 2048 + 2 * 2048));
+            }
+            __syncwarp();
+            // The copies, spread over the warp's lanes: copy q < 4 npg is page box q / 4 (K or V, column half),
+            // then the chunk's K, V and Q rows.
+            uint8_t* st = sm + Lay::S0 + s * Lay::STAGE;
+            const int n_copies = 4 * wv.npg + 6;
+            for (int q = lane; q < n_copies; q += 32) {
+                if (q < 4 * wv.npg) {
+                    const int bx = q >> 2, half = q & 1, isv = (q >> 1) & 1;
+                    const int pg = wv.p_first + bx;
+                    const int page = wv.pages[pg % kPageSlots];
                     int z = layer * n_pages + page;
                     if (page < 0 || page >= n_pages) {
                         report_error(err, DEV_BAD_PAGE);
                         z = -1;   // a page coordinate outside the pool: the box arrives as zeros
                     }
-                    const int y = bx == 0 ? w.y0 : (pg == w.p_last ? w.ylast : 0);
-                    for (int half = 0; half < 2; ++half) {
-                        const int x = h * DKk + half * 64;
-                        tma_load_3d(st + half * Lay::HALF_KV + bx * 16 * 128, &mk, &full[s], x, y, z);
-                        tma_load_3d(st + (2 + half) * Lay::HALF_KV + bx * 16 * 128, &mv, &full[s], x, y, z);
-                    }
-                }
-                for (int half = 0; half < 2; ++half) {
-                    const int x = h * DKk + half * 64;
-                    tma_load_2d(st + half * Lay::HALF_KV + kNewRow * 128, &mqkv, &full[s], D + x, w.row_off);
-                    tma_load_2d(st + (2 + half) * Lay::HALF_KV + kNewRow * 128, &mqkv, &full[s], 2 * D + x, w.row_off);
-                    tma_load_2d(st + 4 * Lay::HALF_KV + half * kTM * 128, &mqkv, &full[s], x, w.row_off);
+                    const int y = bx == 0 ? wv.y0 : (pg == wv.p_last ? wv.ylast : 0);
+                    tma_load_3d(st + (2 * isv + half) * Lay::HALF_KV + bx * 16 * 128, isv ? &mv : &mk, &full[s],
+                                h * DKk + half * 64, y, z);
+                } else {
+                    const int r = q - 4 * wv.npg, half = r & 1, which = r >> 1;   // which: 0 K, 1 V, 2 Q
+                    uint8_t* dst = which < 2 ? st + (2 * which + half) * Lay::HALF_KV + kNewRow * 128
+                                             : st + 4 * Lay::HALF_KV + half * kTM * 128;
+                    const int xcol = (which == 0 ? D : which == 1 ? 2 * D : 0) + h * DKk + half * 64;
+                    tma_load_2d(dst, &mqkv, &full[s], xcol, wv.row_off);
                 }
             }
-            pdl_launch_dependents();
         }
+        if (lane == 0) pdl_launch_dependents();
         return;
     }
 
     // -------------------------------------------------------------------- compute warps
-    bf16* QU = reinterpret_cast<bf16*>(sm + Lay::QU);
-    bf16* QV = reinterpret_cast<bf16*>(sm + Lay::QV);
     float* AC = reinterpret_cast<float*>(sm + Lay::AC);
     float* BD = reinterpret_cast<float*>(sm + Lay::BD);
     bf16* Pb = reinterpret_cast<bf16*>(sm + Lay::PB);
-    int* krow = reinterpret_cast<int*>(sm + Lay::KROW);
+    const int* krow_all = reinterpret_cast<const int*>(sm + Lay::KROW);
     float* bias = reinterpret_cast<float*>(sm + Lay::BIAS);   // [0, 128): pos_bias_u, [128, 256): pos_bias_v
     const uint8_t* Ps = sm + Lay::P;
     const float scale = rsqrtf(static_cast<float>(DKk));
@@ -729,33 +751,23 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
         const uint8_t* Vs = st + 2 * Lay::HALF_KV;
         const uint8_t* Qs = st + 4 * Lay::HALF_KV;
 
-        // ---- key -> staged row table; queries plus the position biases, rounded to bf16 (rows >= T zero)
-        for (int j = tid; j < kNKP; j += kComputeWarps * 32) krow[j] = key_row(ws, L, j);
+        const int* krow = krow_all + s * kNKP;   // key -> staged row, written by the producer warp
         const int T_ = ws.T;
-        for (int idx = tid; idx < kTM * 16; idx += kComputeWarps * 32) {
-            const int i = idx >> 4, c = idx & 15;
-            float q[8], a[8], bb[8];
-            load16<bf16>(reinterpret_cast<const bf16*>(chunk_addr(Qs, kTM, i, c, zero)), q);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                a[e] = i < T_ ? q[e] + bias[c * 8 + e] : 0.f;
-                bb[e] = i < T_ ? q[e] + bias[DKk + c * 8 + e] : 0.f;
-            }
-            store16<bf16>(QU + i * RSB + c * 8, a);
-            store16<bf16>(QV + i * RSB + c * 8, bb);
-        }
         const int nk = ws.nk, np = ws.np, rel_min = ws.rel_min, row_off = ws.row_off, head = ws.head;
-        compute_sync();
 
         // ---- AC = (Q + u) K^T and BDraw = (Q + v) P^T: jobs of two n-tiles (16 columns), one round over the warps
         {
-            const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, acol = (lane >> 4) * 8;
+            // A: the staged query rows with the position bias added in the fragments, rounded to bf16 (rows >= T
+            // zero): a[0] / a[1] hold columns 2 t4, 2 t4 + 1 of rows g / g + 8, a[2] / a[3] columns 8 + 2 t4,
+            // 9 + 2 t4 of the same rows
+            const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, ahalf = lane >> 4;
+            const bool z0 = g >= T_, z1 = g + 8 >= T_;
             const int n_ac = (nk + 15) / 16, n_bd = (np + 15) / 16;
             const int brow = (lane & 7) + ((lane >> 4) << 3), bsel = (lane >> 3) & 1;
             for (int job = warp; job < n_ac + n_bd; job += kComputeWarps) {
                 const bool is_ac = job < n_ac;
                 const int n0 = (is_ac ? job : job - n_ac) * 16;
-                const bf16* As = is_ac ? QU : QV;
+                const float* bq = is_ac ? bias : bias + DKk;
                 // this lane's B row: a key's staged K row, or a position-table row (rel_min + r -> row rel + 15)
                 const int r = n0 + brow;
                 const int brow_s = is_ac ? krow[r] : (rel_min + r + 15);
@@ -765,7 +777,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
                     uint32_t a[4], bfr[4];
-                    tc::ldsm_x4(a, As + arow * RSB + ks * 16 + acol);
+                    tc::ldsm_x4(a, chunk_addr(Qs, kTM, arow, 2 * ks + ahalf, zero));
+                    {
+                        const float2 b0 = *reinterpret_cast<const float2*>(bq + ks * 16 + 2 * t4);
+                        const float2 b1 = *reinterpret_cast<const float2*>(bq + ks * 16 + 8 + 2 * t4);
+                        a[0] = z0 ? 0u : add_bias2(a[0], b0);
+                        a[1] = z1 ? 0u : add_bias2(a[1], b0);
+                        a[2] = z0 ? 0u : add_bias2(a[2], b1);
+                        a[3] = z1 ? 0u : add_bias2(a[3], b1);
+                    }
                     tc::ldsm_x4(bfr, chunk_addr(breg, brows, brow_s, 2 * ks + bsel, zero));
                     tc::mma16816(c0, a, bfr[0], bfr[1]);
                     tc::mma16816(c1, a, bfr[2], bfr[3]);
