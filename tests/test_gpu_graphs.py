@@ -79,3 +79,20 @@ def test_tma_attention_matches_one_cta_per_stream_head_kernel():
         assert fa == fb and ta == tb
         for x, y in zip(pa, pb):
             assert np.array_equal(x, y)
+
+
+def test_two_stream_halves_are_bit_identical_to_one_stream():
+    """Large batches run the layer stack as two halves on two streams (their LayerNorms and tail CTAs share SMs
+    with the other half's GEMMs; by default from 8192 rows, UD_SPLIT=<rows> sets the threshold). Every row's
+    arithmetic is the same as on one stream (UD_SPLIT=0): 80 streams (1,120 rows per steady chunk) with the
+    threshold at 1024 rows give the same bits, replayed from graphs and eager."""
+    dims = ModelDims(n_layers=2)
+    sd = make_weights(dims, seed=3)
+    one = _run(True, sd, dims, n=80, env={"UD_SPLIT": "0"})
+    for graphs in (True, False):
+        two = _run(graphs, sd, dims, n=80, env={"UD_SPLIT": "1024"})
+        assert len(one) == len(two)
+        for (pa, fa, ta), (pb, fb, tb) in zip(one, two):
+            assert fa == fb and ta == tb
+            for x, y in zip(pa, pb):
+                assert np.array_equal(x, y)

@@ -77,6 +77,13 @@ struct ud_engine {
     ud_config cfg{};
     int device = 0;
     cudaStream_t stream = nullptr;
+    // The layer stack of a batch of split_min_rows rows and up runs as two halves, the second on stream2, so that
+    // one half's LayerNorm and tail CTAs share SMs with the other half's GEMMs: 2 % faster at 1024 streams x 14
+    // frames, 3 % slower at 256 x 14 where the halves' GEMMs lose more to tile quantization (UD_SPLIT=<rows>,
+    // 0: one stream). gstream is the stream the engine's GEMM dispatch enqueues on (null: `stream`).
+    cudaStream_t stream2 = nullptr, gstream = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    int split_min_rows = 8192;
     int num_sms = 148;
     bool loaded = false;
     bool bf = true;
@@ -154,8 +161,9 @@ struct ud_engine {
     bool attn_maps = false;             // the tensor maps below exist
     TmaMatrix attn_qkv_map, attn_k_map, attn_v_map;   // QKV rows (64 x 16 boxes), K and V page pools
     BatchEntry* meta_graph_d = nullptr;
-    std::map<std::tuple<int, int, int, int, int, int>, GraphEntry> graphs;   // + staging buffer index
-    std::map<std::tuple<int, int, int, int, int, int>, int> graph_seen;
+    // key: n, rows_max, M, tmax_b, tokens, staging buffer, the halves' split row
+    std::map<std::tuple<int, int, int, int, int, int, int>, GraphEntry> graphs;
+    std::map<std::tuple<int, int, int, int, int, int, int>, int> graph_seen;
     // per-kernel-class timing
     bool prof = false;
     std::vector<cudaEvent_t> prof_events;
@@ -273,13 +281,14 @@ const TmaMatrix* out_map(ud_engine* e, const void* p, int M, int N, int ld, bool
 // One GEMM through the engine's dispatch: tcgen05 for bf16 with more than 16 rows, SIMT otherwise.
 ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, const GemmEpilogue& epi) {
     if (M <= 0) return UD_OK;
+    cudaStream_t const gs = e->gstream ? e->gstream : e->stream;
     const bool tc = e->bf && M > 16 && W.has_tma;
     const bool tc2 = tc && e->tc2_on && M >= 256 && W.N % 16 == 0;
     Launch L_(e, tc2 ? UD_KIND_GEMM_TC2 : tc ? UD_KIND_GEMM_TC : UD_KIND_GEMM_SIMT);
     if (e->bf) {
         if (!tc) {
             gemm_simt<bf16, bf16>(static_cast<const bf16*>(A), lda, static_cast<const bf16*>(W.p), M, W.N, W.K, epi,
-                                  e->stream);
+                                  gs);
         } else {
             const TmaMatrix* am = act_map(e, A, M, W.K, lda);
             if (!am) return fail(UD_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
@@ -290,15 +299,15 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
                     om = out_map(e, epi.out, M, W.N, epi.ldo, true);
                 else if (!epi.out_bf16 && epi.residual == epi.out && epi.ldr == epi.ldo && epi.res_scale == 1.f)
                     om = out_map(e, epi.out, M, W.N, epi.ldo, false);
-                gemm_tc2(*am, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, om, e->stream);
+                gemm_tc2(*am, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, om, gs);
             } else {
                 const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;
-                gemm_tc(*am, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms, e->stream);
+                gemm_tc(*am, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms, gs);
             }
         }
     } else {
         gemm_simt<float, float>(static_cast<const float*>(A), lda, static_cast<const float*>(W.p), M, W.N, W.K, epi,
-                                e->stream);
+                                gs);
     }
     return UD_OK;
 }
@@ -445,8 +454,10 @@ ud_status check_ids(ud_engine* e, int n, const ud_stream_id* ids) {
 
 // ---------------------------------------------------------------- the batched step
 // Enqueues every kernel of one batched step on the engine stream (also the body of a captured graph).
+// One step of n streams (metadata md, M rows) on the engine stream. With 0 < n_a < n the layer stack runs as two
+// halves: streams [0, n_a) (rows [0, m_a)) on the engine stream, the rest on stream2.
 ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tmax_b, int rows_max, const float* in_dev,
-                       int rows_stride, float* out_dev, int32_t* tokens_dev, int* ntok_dev) {
+                       int rows_stride, float* out_dev, int32_t* tokens_dev, int* ntok_dev, int n_a, int m_a) {
     const bool sub = e->cfg.sub_channels > 0;
     const int D = e->D;
     cudaStream_t st = e->stream;
@@ -489,73 +500,102 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         pack_frames(in_dev, rows_stride, md, n, tmax_b, e->x, D, st);
     }
 
-    // ---- conformer layers
+    // ---- conformer layers, over the streams md[0, nh) whose rows are [row0, row0 + Mh), on stream sh. The row
+    // kernels (LayerNorm, GEMMs) take the half's rows; the per-stream kernels (attention, conv module) take the
+    // half's metadata, whose row offsets index the whole batch's buffers.
     const int NL = e->cfg.n_layers;
-    auto ln = [&](const float* g, const float* b) {
-        Launch L_(e, UD_KIND_NORM);
-        if (e->bf) layer_norm<bf16>(e->x, g, b, (bf16*)e->h, M, D, st);
-        else layer_norm<float>(e->x, g, b, (float*)e->h, M, D, st);
-    };
-    auto resid = [&](float scale) {
-        GemmEpilogue g = epi_out(e->x, D, false, e);
-        g.residual = e->x;
-        g.ldr = D;
-        g.out_scale = scale;
-        return g;
-    };
-    // A feed-forward module: x += 1/2 * (SiLU(h W1^T) W2^T).
-    auto ff = [&](const WeightMat& w1, const WeightMat& w2) -> ud_status {
-        GemmEpilogue gs = epi_out(e->hid, e->F, true, e);
-        gs.act = ACT_SILU;
-        UD_TRY(gemm(e, e->h, D, M, w1, gs));
-        return gemm(e, e->hid, e->F, M, w2, resid(0.5f));
-    };
-    if (NL > 0) ln(e->layers[0].ln_ff1_g, e->layers[0].ln_ff1_b);
-    for (int l = 0; l < NL; ++l) {
-        LayerW& w = e->layers[l];
-        UD_TRY(ff(w.ff1_w1, w.ff1_w2));
-        ln(w.ln_att_g, w.ln_att_b);
-        UD_TRY(gemm(e, e->h, D, M, w.wqkv, epi_out(e->qkv, 3 * D, true, e)));
-        {
-        Launch L_(e, UD_KIND_ATTENTION);
-        const bool tma_done = e->bf && e->attn_tma_on && e->attn_maps && w.has_pmap &&
-                              relpos_attention_tma(e->attn_qkv_map, e->attn_k_map, e->attn_v_map, w.pmap, e->tmax - 16,
-                                                   w.pos_u, w.pos_v, md, n, tmax_b, e->cg, l, (bf16*)e->att, D, e->H,
-                                                   e->num_sms, e->err_d, st);
-        if (tma_done) {
-        } else if (e->bf)
-            relpos_attention<bf16>((bf16*)e->qkv, 3 * D, (bf16*)w.ptab, e->tmax, w.pos_u, w.pos_v, md, n, tmax_b, e->cg, l,
-                                   (bf16*)e->att, D, e->H, e->err_d, st);
-        else
-            relpos_attention<float>((float*)e->qkv, 3 * D, (float*)w.ptab, e->tmax, w.pos_u, w.pos_v, md, n, tmax_b, e->cg,
-                                    l, (float*)e->att, D, e->H, e->err_d, st);
-        }
-        UD_TRY(gemm(e, e->att, D, M, w.wo, resid(1.0f)));
-        ln(w.ln_conv_g, w.ln_conv_b);
-        UD_TRY(gemm(e, e->h, D, M, w.pw1, epi_out(e->pw, 2 * D, true, e)));
-        {
-        Launch L_(e, UD_KIND_CONV);
-        if (e->bf)
-            conv_module<bf16>((bf16*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, md, n, tmax_b, e->cg, l, e->KC, (bf16*)e->y,
-                              D, st);
-        else
-            conv_module<float>((float*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, md, n, tmax_b, e->cg, l, e->KC,
-                               (float*)e->y, D, st);
-        }
-        UD_TRY(gemm(e, e->y, D, M, w.pw2, resid(1.0f)));
-        ln(w.ln_ff2_g, w.ln_ff2_b);
-        UD_TRY(ff(w.ff2_w1, w.ff2_w2));
-        if (l + 1 < NL) {
-            LayerW& nx = e->layers[l + 1];
+    auto run_layers = [&](const BatchEntry* mdh, int nh, int row0, int Mh, cudaStream_t sh) -> ud_status {
+        e->gstream = sh;
+        const size_t es = e->esz;
+        float* x = e->x + static_cast<size_t>(row0) * D;
+        void* h = static_cast<char*>(e->h) + static_cast<size_t>(row0) * D * es;
+        void* hid = static_cast<char*>(e->hid) + static_cast<size_t>(row0) * e->F * es;
+        void* qkv = static_cast<char*>(e->qkv) + static_cast<size_t>(row0) * 3 * D * es;
+        void* att = static_cast<char*>(e->att) + static_cast<size_t>(row0) * D * es;
+        void* pw = static_cast<char*>(e->pw) + static_cast<size_t>(row0) * 2 * D * es;
+        void* y = static_cast<char*>(e->y) + static_cast<size_t>(row0) * D * es;
+        auto ln = [&](const float* g, const float* b) {
             Launch L_(e, UD_KIND_NORM);
-            if (e->bf) layer_norm2<bf16>(e->x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (bf16*)e->h, M, D, st);
-            else layer_norm2<float>(e->x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (float*)e->h, M, D, st);
-        } else if (e->cfg.joint_dim) {
-            ln(w.ln_out_g, w.ln_out_b);  // h = LN_out(x): the joint's operand
-        } else {
-            Launch L_(e, UD_KIND_NORM);
-            layer_norm<float>(e->x, w.ln_out_g, w.ln_out_b, e->x, M, D, st);
+            if (e->bf) layer_norm<bf16>(x, g, b, (bf16*)h, Mh, D, sh);
+            else layer_norm<float>(x, g, b, (float*)h, Mh, D, sh);
+        };
+        auto resid = [&](float scale) {
+            GemmEpilogue g = epi_out(x, D, false, e);
+            g.residual = x;
+            g.ldr = D;
+            g.out_scale = scale;
+            return g;
+        };
+        // A feed-forward module: x += 1/2 * (SiLU(h W1^T) W2^T).
+        auto ff = [&](const WeightMat& w1, const WeightMat& w2) -> ud_status {
+            GemmEpilogue gs = epi_out(hid, e->F, true, e);
+            gs.act = ACT_SILU;
+            UD_TRY(gemm(e, h, D, Mh, w1, gs));
+            return gemm(e, hid, e->F, Mh, w2, resid(0.5f));
+        };
+        if (NL > 0) ln(e->layers[0].ln_ff1_g, e->layers[0].ln_ff1_b);
+        for (int l = 0; l < NL; ++l) {
+            LayerW& w = e->layers[l];
+            UD_TRY(ff(w.ff1_w1, w.ff1_w2));
+            ln(w.ln_att_g, w.ln_att_b);
+            UD_TRY(gemm(e, h, D, Mh, w.wqkv, epi_out(qkv, 3 * D, true, e)));
+            {
+            Launch L_(e, UD_KIND_ATTENTION);
+            const bool tma_done = e->bf && e->attn_tma_on && e->attn_maps && w.has_pmap &&
+                                  relpos_attention_tma(e->attn_qkv_map, e->attn_k_map, e->attn_v_map, w.pmap,
+                                                       e->tmax - 16, w.pos_u, w.pos_v, mdh, nh, tmax_b, e->cg, l,
+                                                       (bf16*)e->att, D, e->H, e->num_sms, e->err_d, sh);
+            if (tma_done) {
+            } else if (e->bf)
+                relpos_attention<bf16>((bf16*)e->qkv, 3 * D, (bf16*)w.ptab, e->tmax, w.pos_u, w.pos_v, mdh, nh, tmax_b,
+                                       e->cg, l, (bf16*)e->att, D, e->H, e->err_d, sh);
+            else
+                relpos_attention<float>((float*)e->qkv, 3 * D, (float*)w.ptab, e->tmax, w.pos_u, w.pos_v, mdh, nh,
+                                        tmax_b, e->cg, l, (float*)e->att, D, e->H, e->err_d, sh);
+            }
+            UD_TRY(gemm(e, att, D, Mh, w.wo, resid(1.0f)));
+            ln(w.ln_conv_g, w.ln_conv_b);
+            UD_TRY(gemm(e, h, D, Mh, w.pw1, epi_out(pw, 2 * D, true, e)));
+            {
+            Launch L_(e, UD_KIND_CONV);
+            if (e->bf)
+                conv_module<bf16>((bf16*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, mdh, nh, tmax_b, e->cg, l, e->KC,
+                                  (bf16*)e->y, D, sh);
+            else
+                conv_module<float>((float*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, mdh, nh, tmax_b, e->cg, l, e->KC,
+                                   (float*)e->y, D, sh);
+            }
+            UD_TRY(gemm(e, y, D, Mh, w.pw2, resid(1.0f)));
+            ln(w.ln_ff2_g, w.ln_ff2_b);
+            UD_TRY(ff(w.ff2_w1, w.ff2_w2));
+            if (l + 1 < NL) {
+                LayerW& nx = e->layers[l + 1];
+                Launch L_(e, UD_KIND_NORM);
+                if (e->bf) layer_norm2<bf16>(x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (bf16*)h, Mh, D, sh);
+                else layer_norm2<float>(x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (float*)h, Mh, D, sh);
+            } else if (e->cfg.joint_dim) {
+                ln(w.ln_out_g, w.ln_out_b);  // h = LN_out(x): the joint's operand
+            } else {
+                Launch L_(e, UD_KIND_NORM);
+                layer_norm<float>(x, w.ln_out_g, w.ln_out_b, x, Mh, D, sh);
+            }
         }
+        return UD_OK;
+    };
+    if (n_a > 0 && n_a < n && NL > 0) {
+        // two halves: fork stream2 from the step's stream, join it back before the joint projection
+        UD_CK(cudaEventRecord(e->ev_fork, st));
+        UD_CK(cudaStreamWaitEvent(e->stream2, e->ev_fork, 0));
+        ud_status sa = run_layers(md, n_a, 0, m_a, st);
+        ud_status sb = sa == UD_OK ? run_layers(md + n_a, n - n_a, m_a, M - m_a, e->stream2) : sa;
+        e->gstream = nullptr;
+        UD_CK(cudaEventRecord(e->ev_join, e->stream2));   // joined even after an error, so a capture can end
+        UD_CK(cudaStreamWaitEvent(st, e->ev_join, 0));
+        UD_TRY(sb);
+    } else {
+        const ud_status sa = run_layers(md, n, 0, M, st);
+        e->gstream = nullptr;
+        UD_TRY(sa);
     }
 
     // ---- joint encoder projection, outputs, RNN-T
@@ -635,12 +675,21 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
         }
         std::memcpy(mh[i].pages, e->slots[ids[i]].pages, sizeof(mh[i].pages));
     }
-    const std::tuple<int, int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0,
-                                                       in_dev == e->in_stage ? 0 : 1};
+    // Two halves for the layer stack of a large batch, each with enough rows for the 2-CTA GEMM tiles (not while
+    // profiling: per-kind times are taken on one stream).
+    int n_a = 0, m_a = 0;
+    if (e->split_min_rows > 0 && !e->prof && n >= 2 && M >= std::max(1024, e->split_min_rows)) {
+        n_a = n / 2;
+        m_a = mh[n_a].row_off;
+        if (m_a < 512 || M - m_a < 512) n_a = m_a = 0;
+    }
+    const std::tuple<int, int, int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0,
+                                                            in_dev == e->in_stage ? 0 : 1, m_a};
     const bool use_graph = graph_ok && e->graphs_on && !e->prof;
     if (!use_graph) {
         UD_TRY(upload_meta(e, mi, n));
-        UD_TRY(enqueue_step(e, e->meta_d[mi], n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev, ntok_dev));
+        UD_TRY(enqueue_step(e, e->meta_d[mi], n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev, ntok_dev,
+                            n_a, m_a));
     } else {
         // Metadata for the graph's fixed buffer; the pinned source slot is protected by the ring's event.
         UD_CK(cudaMemcpyAsync(e->meta_graph_d, mh, sizeof(BatchEntry) * n, cudaMemcpyHostToDevice, e->stream));
@@ -655,7 +704,7 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
             const int64_t before = e->launches;
             UD_CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
             const ud_status cs = enqueue_step(e, e->meta_graph_d, n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev,
-                                              tokens_dev, ntok_dev);
+                                              tokens_dev, ntok_dev, n_a, m_a);
             cudaGraph_t graph = nullptr;
             const cudaError_t ce = cudaStreamEndCapture(e->stream, &graph);
             const int64_t kernels = e->launches - before;
@@ -677,7 +726,7 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
         } else {
             e->graph_seen[key] += 1;
             UD_TRY(enqueue_step(e, e->meta_graph_d, n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev,
-                                ntok_dev));
+                                ntok_dev, n_a, m_a));
         }
     }
     UD_CK(cudaGetLastError());
@@ -1263,8 +1312,12 @@ ud_status ud_init(const ud_config* cfg, int device, ud_engine** out) {
         g_last_error = keep;
         return s;
     };
-    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&e->stream2, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess)
         return cleanup(fail(UD_ERR_CUDA, "cudaStreamCreate failed"));
+    if (const char* g = std::getenv("UD_SPLIT")) e->split_min_rows = std::atoi(g);
 
     const bool sub = c.sub_channels > 0;
     if (sub) {
@@ -1403,6 +1456,7 @@ ud_status ud_shutdown(ud_engine* e) {
     if (!e) return UD_OK;
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    if (e->stream2) cudaStreamSynchronize(e->stream2);
     for (void* p : e->allocs) cudaFree(p);
     for (void* p : e->host_allocs) cudaFreeHost(p);
     if (e->cstream) cudaStreamSynchronize(e->cstream);
@@ -1417,6 +1471,9 @@ ud_status ud_shutdown(ud_engine* e) {
     for (cudaEvent_t ev : e->prof_events) cudaEventDestroy(ev);
     for (auto& g : e->graphs) cudaGraphExecDestroy(g.second.exec);
     if (e->stream) cudaStreamDestroy(e->stream);
+    if (e->stream2) cudaStreamDestroy(e->stream2);
+    for (cudaEvent_t ev : {e->ev_fork, e->ev_join})
+        if (ev) cudaEventDestroy(ev);
     if (e->counted) scratch_engine_removed(e->device);
     delete e;
     return UD_OK;
