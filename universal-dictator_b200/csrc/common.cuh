@@ -66,6 +66,17 @@ __device__ __forceinline__ void store16(T* p, const float* v) {
 }
 
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// The PTX tanh.approx.f32 instruction: one special-function operation, relative error about 2^-11.
+__device__ __forceinline__ float tanh_approx(float x) {
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(x));
+    return t;
+}
+// x * sigmoid(q) for results that are rounded to bf16 (relative 2^-9): x * (0.5 + 0.5 tanh(q / 2)), one
+// special-function operation where x / (1 + e^-q) takes two (exponential and reciprocal). The special-function
+// unit delivers 16 results per clock per SM, and the GLU / SiLU epilogues of a C3 step queue on it.
+__device__ __forceinline__ float x_sigmoid_bf16out(float x, float q) { return x * fmaf(0.5f, tanh_approx(0.5f * q), 0.5f); }
 __device__ __forceinline__ float sigmoid(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -32,16 +32,40 @@ template <> struct Pair<bf16> {
     }
 };
 
+// x * sigmoid(q). fp32 engine: x / (1 + e^-q) with the fast exponential and division (two special-function
+// operations). bf16 engine, whose outputs are rounded to bf16 (relative 2^-9): x * (0.5 + 0.5 tanh(q / 2)) with the
+// one-instruction tanh.approx.f32 (relative error about 2^-11). The special-function unit (16 results per clock
+// per SM) is what the GLU and SiLU of a C3 launch queue on, so one operation instead of two halves that work.
+template <typename T> __device__ __forceinline__ float x_sigmoid(float x, float q);
+template <> __device__ __forceinline__ float x_sigmoid<float>(float x, float q) { return __fdividef(x, 1.f + __expf(-q)); }
+template <> __device__ __forceinline__ float x_sigmoid<bf16>(float x, float q) { return x_sigmoid_bf16out(x, q); }
+
+template <typename T> __device__ __forceinline__ void st4(T* p, float a, float b, float c, float d);
+template <> __device__ __forceinline__ void st4<float>(float* p, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+template <> __device__ __forceinline__ void st4<bf16>(bf16* p, float a, float b, float c, float d) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&lo);
+    u.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+
 // Each thread owns a channel pair (D <= 1024 = 2 x 512 threads). One CTA's work is a short dependent chain, so
-// the kernel is built to make that chain short:
+// the kernel is built to keep that chain short:
 //   * before the grid-dependency wait (overlapping the pointwise GEMM's tail): the taps and the LayerNorm
-//     parameters go to shared memory, and the thread's 8 ring rows to registers. None of them is written by
-//     the preceding kernel: the ring of this layer only by this kernel in an earlier step, which finished
-//     before the step's input copies; weights only at load;
+//     parameters start their asynchronous copies to shared memory, and the thread's 8 ring rows load into
+//     registers. None of them is written by the preceding kernel: the ring of this layer only by this kernel in
+//     an earlier step, which finished before the step's input copies; weights only at load;
 //   * after it: the GLU inputs of up to 16 frames (8 for fp32) are loaded with one round of independent loads,
 //     kept packed until all have been issued;
-//   * the depthwise convolution runs from registers over [ring ; new] into ys, and the row LayerNorm reads ys
-//     and the staged parameters from shared memory (a warp per frame).
+//   * the depthwise convolution runs from registers over [ring ; new] into ys; the row LayerNorm (a warp per
+//     frame) holds its row in registers: one pass over shared memory, 8- or 16-byte stores.
 // Taps are stored tap-major, w[k * D + c]. Two CTAs fit on an SM (64 registers, about 100 KB of shared memory
 // at T = 14), so the 256 streams of a C3 batch run in one wave.
 template <typename T, int KW>
@@ -54,18 +78,18 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
     constexpr int R = KW - 1;
     constexpr int FB = sizeof(T) == 2 ? 16 : 8;  // frames whose GLU inputs a thread has in flight at once
     using Raw = typename Pair<T>::Raw;
-    extern __shared__ float sm[];
+    extern __shared__ __align__(16) float sm[];
     const int D = cg.D;
     float* __restrict__ ys = sm;                                    // [tmax][D] GLU output, then conv output
-    float* __restrict__ taps = sm + static_cast<size_t>(tmax) * D;  // [KW][D]
-    float* __restrict__ gs = taps + KW * D;                         // LayerNorm gain, then bias
+    float* __restrict__ taps = sm + static_cast<size_t>(tmax) * D;  // [KW][D], then gain [D], bias [D]
+    float* __restrict__ gs = taps + KW * D;
     float* __restrict__ bs = gs + D;
-    for (int i = threadIdx.x * 4; i < KW * D; i += blockDim.x * 4)
-        *reinterpret_cast<float4*>(taps + i) = __ldg(reinterpret_cast<const float4*>(dw + i));
+    for (int i = threadIdx.x * 4; i < KW * D; i += blockDim.x * 4) cp_async16(taps + i, dw + i);
     for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
-        *reinterpret_cast<float4*>(gs + i) = __ldg(reinterpret_cast<const float4*>(g + i));
-        *reinterpret_cast<float4*>(bs + i) = __ldg(reinterpret_cast<const float4*>(beta + i));
+        cp_async16(gs + i, g + i);
+        cp_async16(bs + i, beta + i);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     const BatchEntry& me = meta[blockIdx.x];
     const int T_ = me.T, vt = me.valid_t, head = me.head, row_off = me.row_off;
     T* __restrict__ ring = reinterpret_cast<T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
@@ -95,14 +119,18 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
                     float g0 = 0.f, g1 = 0.f;  // pad mask: frames from validT on enter as zero
                     if (t < vt) {
                         const float2 v = Pair<T>::cvt(val[u]), q = Pair<T>::cvt(gate[u]);
-                        g0 = __fdividef(v.x, 1.f + __expf(-q.x));  // value * sigmoid(gate)
-                        g1 = __fdividef(v.y, 1.f + __expf(-q.y));
+                        g0 = x_sigmoid<T>(v.x, q.x);  // value * sigmoid(gate)
+                        g1 = x_sigmoid<T>(v.y, q.y);
                     }
                     *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(g0, g1);
                     if (t >= T_ - R) Pair<T>::st(ring + ((head + t) % R) * D + c, g0, g1);
                 }
             }
         }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();  // taps, gain and bias have landed
+    if (own) {
         float w0[KW], w1[KW], a[KW], bq[KW];
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
@@ -117,7 +145,7 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
             bq[i] = v.y;
         }
         // Causal depthwise conv over [ring ; new], in place (ys[t] is read before it is overwritten; each
-        // thread reads and writes only its own columns, so no barrier is needed before this loop).
+        // thread reads and writes only its own columns).
         for (int t = 0; t < T_; ++t) {
             const float2 gv = *reinterpret_cast<const float2*>(ys + t * D + c);
             a[R] = gv.x;
@@ -138,28 +166,38 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    constexpr int kV = 8;  // float4 per lane: D <= 1024
     for (int t = warp; t < T_; t += nwarps) {
         const float* yr = ys + t * D;
+        float4 v[kV];
         float s = 0.f;
-        for (int c4 = lane * 4; c4 < D; c4 += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(yr + c4);
-            s += v.x + v.y + v.z + v.w;
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int c4 = lane * 4 + 128 * j;
+            v[j] = c4 < D ? *reinterpret_cast<const float4*>(yr + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
         }
         const float mean = warp_sum(s) / static_cast<float>(D);
         float q = 0.f;
-        for (int c4 = lane * 4; c4 < D; c4 += 128) {
-            const float4 v = *reinterpret_cast<const float4*>(yr + c4);
-            q += (v.x - mean) * (v.x - mean) + (v.y - mean) * (v.y - mean) + (v.z - mean) * (v.z - mean) +
-                 (v.w - mean) * (v.w - mean);
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            if (lane * 4 + 128 * j < D) {
+                const float a0 = v[j].x - mean, a1 = v[j].y - mean, a2 = v[j].z - mean, a3 = v[j].w - mean;
+                q = fmaf(a0, a0, fmaf(a1, a1, fmaf(a2, a2, fmaf(a3, a3, q))));
+            }
         }
         const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(D) + 1e-5f);
         T* orow = out + static_cast<size_t>(row_off + t) * ldo;
-        for (int c2 = lane * 2; c2 < D; c2 += 64) {
-            const float2 v = *reinterpret_cast<const float2*>(yr + c2);
-            const float2 gg = *reinterpret_cast<const float2*>(gs + c2), bb = *reinterpret_cast<const float2*>(bs + c2);
-            const float z0 = (v.x - mean) * rstd * gg.x + bb.x;
-            const float z1 = (v.y - mean) * rstd * gg.y + bb.y;
-            Pair<T>::st(orow + c2, silu(z0), silu(z1));
+#pragma unroll
+        for (int j = 0; j < kV; ++j) {
+            const int c4 = lane * 4 + 128 * j;
+            if (c4 < D) {
+                const float4 gg = *reinterpret_cast<const float4*>(gs + c4), bb = *reinterpret_cast<const float4*>(bs + c4);
+                const float z0 = (v[j].x - mean) * rstd * gg.x + bb.x, z1 = (v[j].y - mean) * rstd * gg.y + bb.y;
+                const float z2 = (v[j].z - mean) * rstd * gg.z + bb.z, z3 = (v[j].w - mean) * rstd * gg.w + bb.w;
+                st4<T>(orow + c4, x_sigmoid<T>(z0, z0), x_sigmoid<T>(z1, z1), x_sigmoid<T>(z2, z2),
+                       x_sigmoid<T>(z3, z3));
+            }
         }
     }
 }

@@ -37,6 +37,12 @@ static __device__ __forceinline__ float epi_act(int act, float x) {
     if (act == ACT_SILU) return silu(x);
     return x;
 }
+// The same for outputs stored as bf16: SiLU with one special-function operation instead of two.
+static __device__ __forceinline__ float epi_act_bf16(int act, float x) {
+    if (act == ACT_RELU) return fmaxf(x, 0.f);
+    if (act == ACT_SILU) return x_sigmoid_bf16out(x, x);
+    return x;
+}
 
 // v: this lane's row (row0 + lane), columns col .. col + 15. stg: the warp's staging buffer.
 static __device__ __forceinline__ void epi16_store(const GemmEpilogue& epi, float* stg, int row0, int M, int col,
@@ -55,7 +61,7 @@ static __device__ __forceinline__ void epi16_store(const GemmEpilogue& epi, floa
         float e[4] = {x.x, x.y, x.z, x.w};
         if (epi.bias) { e[0] += b.x; e[1] += b.y; e[2] += b.z; e[3] += b.w; }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) e[j] = epi_act(epi.act, e[j]) * epi.out_scale;
+        for (int j = 0; j < 4; ++j) e[j] = (epi.out_bf16 ? epi_act_bf16(epi.act, e[j]) : epi_act(epi.act, e[j])) * epi.out_scale;
         if (epi.residual) {
             e[0] = fmaf(epi.res_scale, r[it].x, e[0]);
             e[1] = fmaf(epi.res_scale, r[it].y, e[1]);
@@ -89,8 +95,13 @@ static __device__ __forceinline__ void epi_direct(const GemmEpilogue& epi, int r
             v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
         }
     }
+    if (epi.out_bf16) {
 #pragma unroll
-    for (int j = 0; j < NC; ++j) v[j] = epi_act(epi.act, v[j]) * epi.out_scale;
+        for (int j = 0; j < NC; ++j) v[j] = epi_act_bf16(epi.act, v[j]) * epi.out_scale;
+    } else {
+#pragma unroll
+        for (int j = 0; j < NC; ++j) v[j] = epi_act(epi.act, v[j]) * epi.out_scale;
+    }
     if (epi.residual) {
 #pragma unroll
         for (int j = 0; j < NC; ++j) v[j] = fmaf(epi.res_scale, r[j], v[j]);

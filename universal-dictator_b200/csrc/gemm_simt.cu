@@ -14,7 +14,7 @@ namespace {
 __device__ __forceinline__ float apply_epi_scalar(const GemmEpilogue& epi, float acc, int m, int n) {
     float y = acc + (epi.bias ? epi.bias[n] : 0.f);
     if (epi.act == ACT_RELU) y = fmaxf(y, 0.f);
-    else if (epi.act == ACT_SILU) y = silu(y);
+    else if (epi.act == ACT_SILU) y = epi.out_bf16 ? x_sigmoid_bf16out(y, y) : silu(y);
     y *= epi.out_scale;
     if (epi.residual) y += epi.res_scale * epi.residual[static_cast<size_t>(m) * epi.ldr + n];
     return y;

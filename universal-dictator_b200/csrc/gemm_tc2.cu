@@ -227,8 +227,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         uint32_t w[4];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            __nv_bfloat162 h = __floats2bfloat162_rn(epi_act(epi.act, e[2 * j]) * epi.out_scale,
-                                                                     epi_act(epi.act, e[2 * j + 1]) * epi.out_scale);
+                            __nv_bfloat162 h = __floats2bfloat162_rn(epi_act_bf16(epi.act, e[2 * j]) * epi.out_scale,
+                                                                     epi_act_bf16(epi.act, e[2 * j + 1]) * epi.out_scale);
                             w[j] = *reinterpret_cast<uint32_t*>(&h);
                         }
                         u = make_uint4(w[0], w[1], w[2], w[3]);
