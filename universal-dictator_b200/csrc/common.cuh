@@ -23,6 +23,7 @@ enum DeviceError : int {
     DEV_TIMEOUT_GRID = 7,       // RNN-T: waiting at a grid barrier of the lock-step decoder
     DEV_TIMEOUT_ATTN = 8,       // attention: waiting for a staged item or a free stage
     DEV_RANGE_F16 = 9,          // RNN-T tensor-core decoder: an operand value beyond the fp16 range
+    DEV_TIMEOUT_CONV = 10,      // conv module: waiting for its ring rows and LayerNorm parameters
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
@@ -189,6 +190,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
             }
         }
     }
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing `bytes` transactions on `bar` (no multicast).
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(smem_dst)),
+                 "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Untiled bulk copy this CTA's shared memory -> global, in the current bulk group (commit with tma_store_commit).
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(smem_src)),
+                 "r"(bytes)
+                 : "memory");
 }
 
 // ------------------------------------------------------------------ TMA stores (shared -> global, bulk groups)

@@ -52,54 +52,63 @@ template <> __device__ __forceinline__ void st4<bf16>(bf16* p, float a, float b,
     *reinterpret_cast<uint2*>(p) = u;
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
-}
-
 // Each thread owns a channel pair (D <= 1024 = 2 x 512 threads). One CTA's work is a short dependent chain, so
-// the kernel is built to keep that chain short:
-//   * before the grid-dependency wait (overlapping the pointwise GEMM's tail): the taps and the LayerNorm
-//     parameters start their asynchronous copies to shared memory, and the thread's 8 ring rows load into
-//     registers. None of them is written by the preceding kernel: the ring of this layer only by this kernel in
-//     an earlier step, which finished before the step's input copies; weights only at load;
+// the kernel is built to keep that chain short and its per-thread work small:
+//   * before the grid-dependency wait (overlapping the pointwise GEMM's tail), one thread starts three bulk
+//     copies into shared memory on an mbarrier: the stream's 8 ring rows (contiguous in the ring pool) and the
+//     LayerNorm gain and bias; each warp prefetches its taps into L2. None of these is written by the preceding
+//     kernel: the ring of this layer only by this kernel in an earlier step, which finished before the step's
+//     input copies; weights only at load;
 //   * after it: the GLU inputs of up to 16 frames (8 for fp32) are loaded with one round of independent loads,
-//     kept packed until all have been issued;
-//   * the depthwise convolution runs from registers over [ring ; new] into ys; the row LayerNorm (a warp per
-//     frame) holds its row in registers: one pass over shared memory, 8- or 16-byte stores.
-// Taps are stored tap-major, w[k * D + c]. Two CTAs fit on an SM (64 registers, about 100 KB of shared memory
-// at T = 14), so the 256 streams of a C3 batch run in one wave.
+//     kept packed until all have been issued, and their GLU goes to ys;
+//   * the depthwise convolution runs from registers over [ring ; new] into ys, and puts the new frames' GLU
+//     values into the shared copy of the ring as it passes them; one bulk store writes the 8 rows back (rows of
+//     frames older than the last 8 hold their old values again);
+//   * the row LayerNorm (a warp per frame) holds its row in registers: one pass over shared memory, 8- or
+//     16-byte stores.
+// Taps are stored tap-major, w[k * D + c]. Two CTAs fit on an SM (64 registers, 80 KB of shared memory at
+// T = 14), so the 256 streams of a C3 batch run in one wave.
 template <typename T, int KW>
 __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict__ pw, int ld_pw,
                                                           const float* __restrict__ dw, const float* __restrict__ g,
                                                           const float* __restrict__ beta,
                                                           const BatchEntry* __restrict__ meta, const CacheGeom cg,
-                                                          int layer, int tmax, T* __restrict__ out, int ldo) {
+                                                          int layer, int tmax, T* __restrict__ out, int ldo, int* err) {
     pdl_launch_dependents();
     constexpr int R = KW - 1;
     constexpr int FB = sizeof(T) == 2 ? 16 : 8;  // frames whose GLU inputs a thread has in flight at once
     using Raw = typename Pair<T>::Raw;
     extern __shared__ __align__(16) float sm[];
+    __shared__ uint64_t bar;
+    __shared__ int fail;
     const int D = cg.D;
     float* __restrict__ ys = sm;                                    // [tmax][D] GLU output, then conv output
-    float* __restrict__ taps = sm + static_cast<size_t>(tmax) * D;  // [KW][D], then gain [D], bias [D]
-    float* __restrict__ gs = taps + KW * D;
+    float* __restrict__ gs = sm + static_cast<size_t>(tmax) * D;    // LayerNorm gain [D], bias [D]
     float* __restrict__ bs = gs + D;
-    for (int i = threadIdx.x * 4; i < KW * D; i += blockDim.x * 4) cp_async16(taps + i, dw + i);
-    for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
-        cp_async16(gs + i, g + i);
-        cp_async16(bs + i, beta + i);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    T* __restrict__ rs = reinterpret_cast<T*>(bs + D);              // [R][D] ring rows, in ring order
     const BatchEntry& me = meta[blockIdx.x];
+    const int slot = me.slot;
+    T* __restrict__ ring = reinterpret_cast<T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + slot) * R * D;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const uint32_t ring_bytes = static_cast<uint32_t>(R * D * sizeof(T));
+    if (threadIdx.x == 0) {
+        fail = 0;
+        mbar_init(&bar, 1);
+        fence_mbarrier_init();
+        const uint32_t par_bytes = static_cast<uint32_t>(D * 4);
+        mbar_arrive_expect_tx(&bar, ring_bytes + 2 * par_bytes);
+        bulk_load(rs, ring, ring_bytes, &bar);
+        bulk_load(gs, g, par_bytes, &bar);
+        bulk_load(bs, beta, par_bytes, &bar);
+    }
+    if (warp * 64 < D && lane < 2 * KW) {  // this warp's 64 channels of tap lane / 2: two 128-byte lines
+        const float* line = dw + (lane >> 1) * D + warp * 64 + (lane & 1) * 32;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
+    }
+    __syncthreads();  // the barrier is initialised before anyone waits on it
     const int T_ = me.T, vt = me.valid_t, head = me.head, row_off = me.row_off;
-    T* __restrict__ ring = reinterpret_cast<T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
     const int c = threadIdx.x * 2;
     const bool own = c < D;
-    Raw rr[R];  // frames head - R + i, read before any ring row is rewritten
-    if (own) {
-#pragma unroll
-        for (int i = 0; i < R; ++i) rr[i] = Pair<T>::ldr(ring + ((head + i) % R) * D + c);
-    }
     pdl_wait();
     if (own) {
         for (int t0 = 0; t0 < T_; t0 += FB) {
@@ -123,33 +132,35 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
                         g1 = x_sigmoid<T>(v.y, q.y);
                     }
                     *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(g0, g1);
-                    if (t >= T_ - R) Pair<T>::st(ring + ((head + t) % R) * D + c, g0, g1);
                 }
             }
         }
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();  // taps, gain and bias have landed
+    if (!mbar_wait_bounded(&bar, 0, err, DEV_TIMEOUT_CONV, &fail)) fail = 1;
+    __syncthreads();
+    if (fail) return;
     if (own) {
         float w0[KW], w1[KW], a[KW], bq[KW];
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
-            const float2 wk = *reinterpret_cast<const float2*>(taps + k * D + c);
+            const float2 wk = __ldg(reinterpret_cast<const float2*>(dw + k * D + c));
             w0[k] = wk.x;
             w1[k] = wk.y;
         }
 #pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const float2 v = Pair<T>::cvt(rr[i]);
+        for (int i = 0; i < R; ++i) {  // frame head - R + i sits in ring row (head + i) % R
+            const float2 v = Pair<T>::ld(rs + ((head + i) % R) * D + c);
             a[i] = v.x;
             bq[i] = v.y;
         }
         // Causal depthwise conv over [ring ; new], in place (ys[t] is read before it is overwritten; each
-        // thread reads and writes only its own columns).
+        // thread reads and writes only its own columns). The last R new frames' GLU values replace, in the
+        // shared copy, the ring rows of the frames R older, which this thread has already read.
         for (int t = 0; t < T_; ++t) {
             const float2 gv = *reinterpret_cast<const float2*>(ys + t * D + c);
             a[R] = gv.x;
             bq[R] = gv.y;
+            if (t >= T_ - R) Pair<T>::st(rs + ((head + t) % R) * D + c, gv.x, gv.y);
             float y0 = 0.f, y1 = 0.f;
 #pragma unroll
             for (int k = 0; k < KW; ++k) {
@@ -164,8 +175,12 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
             }
         }
     }
+    fence_proxy_async_smem();  // the ring rows written above, before the bulk store reads them
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    if (threadIdx.x == 0) {
+        bulk_store(ring, rs, ring_bytes);
+        tma_store_commit();
+    }
     constexpr int kV = 8;  // float4 per lane: D <= 1024
     for (int t = warp; t < T_; t += nwarps) {
         const float* yr = ys + t * D;
@@ -200,24 +215,26 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
             }
         }
     }
+    if (threadIdx.x == 0) tma_store_wait_all();  // the ring rows are in global memory before the CTA exits
 }
 
 }  // namespace
 
 template <typename T>
 void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, const float* ln_b, const BatchEntry* meta,
-                 int n, int tmax_batch, const CacheGeom& cg, int layer, int K, T* out, int ldo, cudaStream_t s) {
+                 int n, int tmax_batch, const CacheGeom& cg, int layer, int K, T* out, int ldo, int* dev_err,
+                 cudaStream_t s) {
     if (n <= 0 || K != 9) return;
-    const size_t smem = sizeof(float) * (static_cast<size_t>(tmax_batch) + 9 + 2) * cg.D;
+    const size_t smem = (sizeof(float) * (static_cast<size_t>(tmax_batch) + 2) + sizeof(T) * 8) * cg.D;
     static size_t attr_set[kMaxDevices] = {};
-    if (smem > 48 * 1024) ensure_dyn_smem(conv_module_kernel<T, 9>, smem, attr_set);
+    ensure_dyn_smem(conv_module_kernel<T, 9>, smem, attr_set);  // also below 48 KB: the kernel has static shared memory too
     launch_pdl(conv_module_kernel<T, 9>, dim3(n), dim3(512), smem, s, pw, ld_pw, dw, ln_g, ln_b, meta, cg, layer,
-               tmax_batch, out, ldo);
+               tmax_batch, out, ldo, dev_err);
 }
 
 template void conv_module<float>(const float*, int, const float*, const float*, const float*, const BatchEntry*, int,
-                                 int, const CacheGeom&, int, int, float*, int, cudaStream_t);
+                                 int, const CacheGeom&, int, int, float*, int, int*, cudaStream_t);
 template void conv_module<bf16>(const bf16*, int, const float*, const float*, const float*, const BatchEntry*, int, int,
-                                const CacheGeom&, int, int, bf16*, int, cudaStream_t);
+                                const CacheGeom&, int, int, bf16*, int, int*, cudaStream_t);
 
 }  // namespace ud

@@ -327,8 +327,8 @@ ud_status device_error_status(ud_engine* e, int code) {
     static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
                                   "GEMM TMEM drain wait", "unmapped cache page", "test wait",
                                   "RNN-T grid barrier wait", "attention stage wait",
-                                  "RNN-T decoder input beyond the fp16 range"};
-    const char* nm = (code >= 0 && code <= 9) ? names[code] : "unknown";
+                                  "RNN-T decoder input beyond the fp16 range", "conv module copy wait"};
+    const char* nm = (code >= 0 && code <= 10) ? names[code] : "unknown";
     if (code == DEV_BAD_PAGE || code == DEV_RANGE_F16)
         return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
     return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
@@ -560,10 +560,10 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
             Launch L_(e, UD_KIND_CONV);
             if (e->bf)
                 conv_module<bf16>((bf16*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, mdh, nh, tmax_b, e->cg, l, e->KC,
-                                  (bf16*)e->y, D, sh);
+                                  (bf16*)e->y, D, e->err_d, sh);
             else
                 conv_module<float>((float*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, mdh, nh, tmax_b, e->cg, l, e->KC,
-                                   (float*)e->y, D, sh);
+                                   (float*)e->y, D, e->err_d, sh);
             }
             UD_TRY(gemm(e, y, D, Mh, w.pw2, resid(1.0f)));
             ln(w.ln_ff2_g, w.ln_ff2_b);

@@ -117,7 +117,7 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
 template <typename T>
 void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, const float* ln_b,
                  const BatchEntry* meta, int n, int tmax_batch, const CacheGeom& cg, int layer, int K, T* out,
-                 int ldo, cudaStream_t s);
+                 int ldo, int* dev_err, cudaStream_t s);
 
 // ---- Subsampling (causal dw-striding x8, channel-last activations [b][t][f][c]).
 // conv0 + ReLU fused with the stage-1 depthwise conv: mel [n][rows_stride][mel_bins] -> out [n][T2][F2][C].

@@ -582,7 +582,7 @@ void rnnt_greedy(const RnntWeights& w, const RnntState& st, const float* proj, i
     }
     const size_t smem = rnnt_smem_bytes(w);
     static size_t attr_set[kMaxDevices] = {};
-    if (smem > 48 * 1024) ensure_dyn_smem(rnnt_kernel, smem, attr_set);
+    ensure_dyn_smem(rnnt_kernel, smem, attr_set);  // also below 48 KB: the kernel has static shared memory too
     launch_pdl(rnnt_kernel, dim3(n), dim3(kThreads), smem, s, w, st, proj, ld_proj, meta, tokens, tok_stride, n_tokens);
 }
 
