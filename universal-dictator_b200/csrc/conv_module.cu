@@ -140,38 +140,41 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
     __syncthreads();
     if (fail) return;
     if (own) {
-        float w0[KW], w1[KW], a[KW], bq[KW];
+        float w0[KW], w1[KW], xa[KW], xb[KW];
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
             const float2 wk = __ldg(reinterpret_cast<const float2*>(dw + k * D + c));
             w0[k] = wk.x;
             w1[k] = wk.y;
         }
+        // Input j (frames -R .. T-1, negative ones from the ring) lives in register (j + KW) % KW of xa / xb, so
+        // with the frame loop unrolled KW-fold every index is a compile-time constant: nothing is shifted.
 #pragma unroll
-        for (int i = 0; i < R; ++i) {  // frame head - R + i sits in ring row (head + i) % R
+        for (int i = 0; i < R; ++i) {  // frame i - R sits in ring row (head + i) % R
             const float2 v = Pair<T>::ld(rs + ((head + i) % R) * D + c);
-            a[i] = v.x;
-            bq[i] = v.y;
+            xa[i + 1] = v.x;
+            xb[i + 1] = v.y;
         }
         // Causal depthwise conv over [ring ; new], in place (ys[t] is read before it is overwritten; each
         // thread reads and writes only its own columns). The last R new frames' GLU values replace, in the
         // shared copy, the ring rows of the frames R older, which this thread has already read.
-        for (int t = 0; t < T_; ++t) {
-            const float2 gv = *reinterpret_cast<const float2*>(ys + t * D + c);
-            a[R] = gv.x;
-            bq[R] = gv.y;
-            if (t >= T_ - R) Pair<T>::st(rs + ((head + t) % R) * D + c, gv.x, gv.y);
-            float y0 = 0.f, y1 = 0.f;
+        for (int t0 = 0; t0 < T_; t0 += KW) {
 #pragma unroll
-            for (int k = 0; k < KW; ++k) {
-                y0 = fmaf(w0[k], a[k], y0);
-                y1 = fmaf(w1[k], bq[k], y1);
-            }
-            *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(y0, y1);
+            for (int u = 0; u < KW; ++u) {
+                const int t = t0 + u;
+                if (t < T_) {
+                    const float2 gv = *reinterpret_cast<const float2*>(ys + t * D + c);
+                    xa[u] = gv.x;
+                    xb[u] = gv.y;
+                    if (t >= T_ - R) Pair<T>::st(rs + ((head + t) % R) * D + c, gv.x, gv.y);
+                    float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-            for (int k = 0; k < R; ++k) {
-                a[k] = a[k + 1];
-                bq[k] = bq[k + 1];
+                    for (int k = 0; k < KW; ++k) {  // input t - R + k
+                        y0 = fmaf(w0[k], xa[(u + 1 + k) % KW], y0);
+                        y1 = fmaf(w1[k], xb[(u + 1 + k) % KW], y1);
+                    }
+                    *reinterpret_cast<float2*>(ys + t * D + c) = make_float2(y0, y1);
+                }
             }
         }
     }
