@@ -1830,12 +1830,13 @@ ud_status ud_rnnt_decode_static(ud_engine* e, ud_stream_id id, const float* f, i
     UD_CK_QUIET(cudaMemcpyAsync(&nt, count, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     UD_CK_QUIET(cudaMemcpyAsync(e->err_h, e->err_d, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
     UD_CK_QUIET(cudaStreamSynchronize(e->stream));
-    // A bounded device wait that expired (the lock-step decoder's grid barrier) ends the kernel early: the tokens
-    // are incomplete, so the call fails, and the error word is cleared so that the next call starts clean.
+    // A bounded device wait that expired (a decoder's grid barrier) or an input the kernel rejected ends the kernel
+    // early: the tokens are incomplete, so the call fails with the status device_error_status gives the same code,
+    // and the error word is cleared so that the next call starts clean.
     if (const int code = *e->err_h) {
         UD_CK_QUIET(cudaMemsetAsync(e->err_d, 0, sizeof(int), e->stream));
         UD_CK_QUIET(cudaStreamSynchronize(e->stream));
-        return quiet(code == DEV_BAD_PAGE ? UD_ERR_INVALID_ARGUMENT : UD_ERR_DEVICE_TIMEOUT);
+        return quiet((code == DEV_BAD_PAGE || code == DEV_RANGE_F16) ? UD_ERR_INVALID_ARGUMENT : UD_ERR_DEVICE_TIMEOUT);
     }
     if (nt < 0 || static_cast<size_t>(nt) > tok_cap) return quiet(UD_ERR_CUDA);
     if (nt > 0) {
