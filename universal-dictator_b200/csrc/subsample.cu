@@ -46,6 +46,12 @@ __device__ __forceinline__ void cp_async4_zfill(float* smem, const float* gmem, 
                  : "memory");
 }
 
+// 16 bytes global -> shared, or 16 zero bytes when !ok (the source is then not read).
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(ok ? 16 : 0)
+                 : "memory");
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256, 2) conv01_kernel(const float* __restrict__ mel, int rows_stride, int mel_bins,
                                                         const BatchEntry* __restrict__ meta, int Tin,
@@ -177,37 +183,26 @@ __global__ void __launch_bounds__(256, 2) conv01_kernel(const float* __restrict_
 }
 
 // Stage-2 depthwise conv (3x3 stride 2; input rows >= v2 = nxt(nxt(valid_mel)) read as zero). One CTA per
-// (stream, output row t): the three input rows 2t-2 .. 2t are staged in shared memory with 16-byte coalesced
-// loads (masked rows as zeros); each thread owns one channel group (taps in registers) and a run of output
-// columns.
+// (stream, output row t): the three input rows 2t-2 .. 2t are staged in shared memory by 16-byte cp.async, all in
+// flight at once (masked rows zero-filled); each thread owns one channel group (taps in registers, loaded before
+// the grid-dependency wait) and a run of output columns.
 template <typename T>
 __global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, int Tin, int Fin,
                                                       const BatchEntry* __restrict__ meta, const float* __restrict__ w,
                                                       const float* __restrict__ bias, T* __restrict__ out, int Tout,
                                                       int Fout, int C) {
     pdl_launch_dependents();
-    pdl_wait();
     constexpr int VW = Vec16<T>::N;
     extern __shared__ __align__(16) unsigned char smraw[];
     T* xs = reinterpret_cast<T*>(smraw);   // [3][Fin][C]
     const int b = blockIdx.x, t = blockIdx.y;
-    const int vin = nxt(nxt(meta[b].valid_mel));
-    const int row_elems = Fin * C;
-    for (int k = 0; k < 3; ++k) {
-        const int r = 2 * t - 2 + k;
-        const bool ok = r >= 0 && r < Tin && r < vin;
-        const uint4* src = reinterpret_cast<const uint4*>(in + (static_cast<size_t>(b) * Tin + (ok ? r : 0)) * row_elems);
-        uint4* dst = reinterpret_cast<uint4*>(xs + k * row_elems);
-        for (int i = threadIdx.x; i < row_elems / VW; i += blockDim.x) dst[i] = ok ? src[i] : make_uint4(0, 0, 0, 0);
-    }
-    __syncthreads();
     const int groups = C / VW;
     const int lanes_f = blockDim.x / groups;
     const int g = threadIdx.x % groups, fl = threadIdx.x / groups;
-    if (fl >= lanes_f) return;
     const int per = (Fout + lanes_f - 1) / lanes_f;
-    const int fa = fl * per, fb = min(Fout, fa + per);
+    const int fa = fl * per, fb = fl < lanes_f ? min(Fout, fa + per) : fa;
     const int c = g * VW;
+    // Taps and bias (weights, never written by the previous kernel) before the grid-dependency wait.
     float wr[9][VW], br[VW];
 #pragma unroll
     for (int e = 0; e < VW; e += 4) {
@@ -221,6 +216,20 @@ __global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, 
             const float4 ww = *reinterpret_cast<const float4*>(w + k * C + c + e);
             wr[k][e] = ww.x; wr[k][e + 1] = ww.y; wr[k][e + 2] = ww.z; wr[k][e + 3] = ww.w;
         }
+    pdl_wait();
+    // The three input rows 2 t - 2 .. 2 t (zero where masked), every 16-byte chunk in flight at once.
+    const int vin = nxt(nxt(meta[b].valid_mel));
+    const int row_chunks = Fin * C / VW;
+    for (int i = threadIdx.x; i < 3 * row_chunks; i += blockDim.x) {
+        const int k = i / row_chunks, j = i - k * row_chunks;
+        const int r = 2 * t - 2 + k;
+        const bool ok = r >= 0 && r < Tin && r < vin;
+        const T* src = in + (static_cast<size_t>(b) * Tin + (ok ? r : 0)) * Fin * C + static_cast<size_t>(j) * VW;
+        cp_async16_zfill(xs + static_cast<size_t>(i) * VW, src, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
     for (int f = fa; f < fb; ++f) {
         float acc[VW];
 #pragma unroll
