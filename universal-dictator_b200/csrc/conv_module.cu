@@ -138,7 +138,10 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
     }
     if (!mbar_wait_bounded(&bar, 0, err, DEV_TIMEOUT_CONV, &fail)) fail = 1;
     __syncthreads();
-    if (fail) return;
+    if (fail) {   // the wait expired (error recorded): give copies already issued into this CTA time to land
+        __nanosleep(100000);
+        return;
+    }
     if (own) {
         float w0[KW], w1[KW], xa[KW], xb[KW];
 #pragma unroll
