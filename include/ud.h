@@ -222,6 +222,15 @@ typedef enum ud_kernel_kind {
 UD_API ud_status ud_profile_enable(ud_engine* e, int enable);
 UD_API ud_status ud_profile_read(ud_engine* e, int kind, double* ms_total, int64_t* launches);
 
+/* Graph-mode GEMM timers. With enable != 0, every 2-CTA tcgen05 GEMM launch of the following steps records, in
+ * global-timer nanoseconds, when its first CTA passed the grid-dependency wait and when its last CTA finished;
+ * steps run with the timers on are captured in graphs of their own, so the step's CUDA graph and programmatic
+ * dependent launch stay as in normal operation. ud_gemm_timers_read synchronises and returns, for the last step,
+ * the sum over its GEMM launches of (last finish - first start) in milliseconds and the number of launches. When
+ * the layer stack runs as two halves on two streams, the halves' launches overlap and the sum counts both. */
+UD_API ud_status ud_gemm_timers(ud_engine* e, int enable);
+UD_API ud_status ud_gemm_timers_read(ud_engine* e, double* ms, int* launches);
+
 /* Kernel-level test hook (the reference's GemmTests.swift contract, Step.gemm in Core/Kernels.swift:79-113):
  * C = out_scale * act(A . W^T + bias) + res_scale * R, device pointers, A [M,K] and W [N,K] in the
  * engine dtype, C fp32 [M,N] (or bf16 if out_bf16), act 0 none / 1 relu / 2 silu, R fp32 or NULL. */

@@ -3,6 +3,7 @@ same inputs), across shape changes (first chunk, steady chunks, a short final ch
 batched entry points."""
 
 import os
+import time
 
 import numpy as np
 import pytest
@@ -15,7 +16,7 @@ from oracle.weights import ModelDims, make_weights
 pytestmark = pytest.mark.gpu
 
 
-def _run(graphs: bool, sd, dims, n=3, env=None):
+def _run(graphs: bool, sd, dims, n=3, env=None, timers=False):
     env = dict(env or {}, UD_GRAPHS="1" if graphs else "0")
     old = {k: os.environ.get(k) for k in env}
     os.environ.update(env)
@@ -28,6 +29,9 @@ def _run(graphs: bool, sd, dims, n=3, env=None):
             else:
                 os.environ[k] = v
     e.load_weights(sd)
+    if timers:
+        e.gemm_timers(True)
+    readings = []
     ids = [e.open(13) for _ in range(n)]
     mels = [torch.randn(400, 128, generator=torch.Generator().manual_seed(20 + i)).numpy() for i in range(n)]
     plans = [list(chunk_plan(400, 13, 400 - 7 * (i % 3))) for i in range(n)]
@@ -35,11 +39,15 @@ def _run(graphs: bool, sd, dims, n=3, env=None):
     for k in range(max(len(p) for p in plans)):
         act = [i for i in range(n) if k < len(plans[i])]
         chunks = [mels[i][plans[i][k][0]:plans[i][k][0] + plans[i][k][1]] for i in act]
+        t0 = time.perf_counter()
         projs, frames, toks = e.step_batch([ids[i] for i in act], chunks, [plans[i][k][1] for i in act],
                                            [plans[i][k][2] for i in act], [plans[i][k][3] for i in act], decode=True)
+        wall_ms = (time.perf_counter() - t0) * 1e3
         outs.append(([p.copy() for p in projs], frames, toks))
+        if timers:
+            readings.append((min(plans[i][k][1] for i in act), wall_ms) + e.gemm_timers_read())
     e.close()
-    return outs
+    return (outs, readings) if timers else outs
 
 
 def test_graph_replay_is_bit_identical():
@@ -65,6 +73,27 @@ def test_graph_replay_bit_identical_at_two_cta_batch():
         assert fa == fb and ta == tb
         for x, y in zip(pa, pb):
             assert np.array_equal(x, y)
+
+
+def test_graph_mode_gemm_timers_leave_results_unchanged():
+    """The graph-mode GEMM timers (ud_gemm_timers: global-timer stamps in every 2-CTA GEMM launch, the steps captured
+    in graphs of their own) give the same bits as graph replay without them. At 20 streams x 14 frames every
+    step's 2-CTA GEMMs are timed (at least the 8 projections of each of the 2 layers), each step's summed GEMM
+    time is positive and below the step's wall time. (The short final chunks run too few rows for the 2-CTA GEMMs
+    and are left out.)"""
+    dims = ModelDims(n_layers=2)
+    sd = make_weights(dims, seed=1)
+    plain = _run(True, sd, dims, n=20)
+    timed, readings = _run(True, sd, dims, n=20, timers=True)
+    for (pa, fa, ta), (pb, fb, tb) in zip(plain, timed):
+        assert fa == fb and ta == tb
+        for x, y in zip(pa, pb):
+            assert np.array_equal(x, y)
+    full = [r for r in readings if r[0] >= 105]   # first (105 mel rows) and steady (121) chunks of all 20 streams
+    assert len(full) >= 3
+    for rows, wall_ms, gemm_ms, launches in full:
+        assert launches >= 2 * 8, launches
+        assert 0.0 < gemm_ms < wall_ms, (gemm_ms, wall_ms)
 
 
 def test_tma_attention_matches_one_cta_per_stream_head_kernel():

@@ -154,6 +154,7 @@ struct ud_engine {
     struct GraphEntry {
         cudaGraphExec_t exec;
         int64_t kernels;
+        int gemm_slots;   // timed GEMM launches (graph-mode timers on)
     };
     bool graphs_on = true;
     bool tc2_on = true;  // 2-CTA tcgen05 tiles for M >= 256, N % 256 == 0
@@ -161,9 +162,14 @@ struct ud_engine {
     bool attn_maps = false;             // the tensor maps below exist
     TmaMatrix attn_qkv_map, attn_k_map, attn_v_map;   // QKV rows (64 x 16 boxes), K and V page pools
     BatchEntry* meta_graph_d = nullptr;
-    // key: n, rows_max, M, tmax_b, tokens, staging buffer, the halves' split row
-    std::map<std::tuple<int, int, int, int, int, int, int>, GraphEntry> graphs;
-    std::map<std::tuple<int, int, int, int, int, int, int>, int> graph_seen;
+    // key: n, rows_max, M, tmax_b, tokens, staging buffer, the halves' split row, GEMM timers
+    std::map<std::tuple<int, int, int, int, int, int, int, int>, GraphEntry> graphs;
+    std::map<std::tuple<int, int, int, int, int, int, int, int>, int> graph_seen;
+    // graph-mode GEMM timers: [kGemmProfCap] first-start times, then [kGemmProfCap] last-finish times (ns)
+    bool gemm_timers = false;
+    unsigned long long* gemm_prof = nullptr;
+    int gemm_prof_n = 0;      // slots handed out while the current step is enqueued
+    int gemm_prof_last = 0;   // slots of the last step run
     // per-kernel-class timing
     bool prof = false;
     std::vector<cudaEvent_t> prof_events;
@@ -285,6 +291,8 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
     const bool tc = e->bf && M > 16 && W.has_tma;
     const bool tc2 = tc && e->tc2_on && M >= 256 && W.N % 16 == 0;
     Launch L_(e, tc2 ? UD_KIND_GEMM_TC2 : tc ? UD_KIND_GEMM_TC : UD_KIND_GEMM_SIMT);
+    GemmEpilogue ep = epi;
+    if (tc2 && e->gemm_timers && e->gemm_prof_n < kGemmProfCap) ep.prof = e->gemm_prof + e->gemm_prof_n++;
     if (e->bf) {
         if (!tc) {
             gemm_simt<bf16, bf16>(static_cast<const bf16*>(A), lda, static_cast<const bf16*>(W.p), M, W.N, W.K, epi,
@@ -299,7 +307,7 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
                     om = out_map(e, epi.out, M, W.N, epi.ldo, true);
                 else if (!epi.out_bf16 && epi.residual == epi.out && epi.ldr == epi.ldo && epi.res_scale == 1.f)
                     om = out_map(e, epi.out, M, W.N, epi.ldo, false);
-                gemm_tc2(*am, W.tma128, M, W.N, W.K, 256, epi, e->err_d, e->num_sms, om, gs);
+                gemm_tc2(*am, W.tma128, M, W.N, W.K, 256, ep, e->err_d, e->num_sms, om, gs);
             } else {
                 const int bn = W.has256 ? gemm_tc_pick_bn(M, W.N, e->num_sms) : 128;
                 gemm_tc(*am, bn == 256 ? W.tma256 : W.tma128, M, W.N, W.K, bn, epi, e->err_d, e->num_sms, gs);
@@ -683,13 +691,20 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
         m_a = mh[n_a].row_off;
         if (m_a < 512 || M - m_a < 512) n_a = m_a = 0;
     }
-    const std::tuple<int, int, int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0,
-                                                            in_dev == e->in_stage ? 0 : 1, m_a};
+    const std::tuple<int, int, int, int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0,
+                                                                 in_dev == e->in_stage ? 0 : 1, m_a,
+                                                                 e->gemm_timers ? 1 : 0};
     const bool use_graph = graph_ok && e->graphs_on && !e->prof;
+    if (e->gemm_timers) {   // every slot empty: starts at the largest value, finishes at zero
+        UD_CK(cudaMemsetAsync(e->gemm_prof, 0xff, sizeof(unsigned long long) * kGemmProfCap, e->stream));
+        UD_CK(cudaMemsetAsync(e->gemm_prof + kGemmProfCap, 0, sizeof(unsigned long long) * kGemmProfCap, e->stream));
+    }
+    e->gemm_prof_n = 0;
     if (!use_graph) {
         UD_TRY(upload_meta(e, mi, n));
         UD_TRY(enqueue_step(e, e->meta_d[mi], n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev, ntok_dev,
                             n_a, m_a));
+        e->gemm_prof_last = e->gemm_prof_n;
     } else {
         // Metadata for the graph's fixed buffer; the pinned source slot is protected by the ring's event.
         UD_CK(cudaMemcpyAsync(e->meta_graph_d, mh, sizeof(BatchEntry) * n, cudaMemcpyHostToDevice, e->stream));
@@ -718,15 +733,18 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
             const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
             if (ie != cudaSuccess) return fail(UD_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
-            it = e->graphs.emplace(key, ud_engine::GraphEntry{exec, kernels}).first;
+            it = e->graphs.emplace(key, ud_engine::GraphEntry{exec, kernels, e->gemm_prof_n}).first;
         }
         if (it != e->graphs.end()) {
             UD_CK(cudaGraphLaunch(it->second.exec, e->stream));
             e->launches += it->second.kernels;
+            e->gemm_prof_last = it->second.gemm_slots;
         } else {
             e->graph_seen[key] += 1;
+            e->gemm_prof_n = 0;
             UD_TRY(enqueue_step(e, e->meta_graph_d, n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev,
                                 ntok_dev, n_a, m_a));
+            e->gemm_prof_last = e->gemm_prof_n;
         }
     }
     UD_CK(cudaGetLastError());
@@ -2071,6 +2089,38 @@ ud_status ud_profile_enable(ud_engine* e, int enable) {
         e->prof_ms[k] = 0.0;
         e->prof_n[k] = 0;
     }
+    return UD_OK;
+}
+
+ud_status ud_gemm_timers(ud_engine* e, int enable) {
+    if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
+    UD_CK(cudaSetDevice(e->device));
+    if (enable && !e->gemm_prof) UD_TRY(dalloc(e, &e->gemm_prof, 2 * static_cast<size_t>(kGemmProfCap)));
+    e->gemm_timers = enable != 0;
+    e->gemm_prof_last = 0;
+    return UD_OK;
+}
+
+ud_status ud_gemm_timers_read(ud_engine* e, double* ms, int* launches) {
+    if (!e || !ms || !launches) return fail(UD_ERR_INVALID_ARGUMENT, "bad argument");
+    UD_CK(cudaSetDevice(e->device));
+    *ms = 0.0;
+    *launches = 0;
+    if (!e->gemm_prof || e->gemm_prof_last <= 0) return UD_OK;
+    const int n = e->gemm_prof_last;
+    std::vector<unsigned long long> h(2 * static_cast<size_t>(kGemmProfCap));
+    UD_CK(cudaStreamSynchronize(e->stream));
+    UD_CK(cudaMemcpy(h.data(), e->gemm_prof, sizeof(unsigned long long) * h.size(), cudaMemcpyDeviceToHost));
+    double ns = 0.0;
+    int counted = 0;
+    for (int i = 0; i < n; ++i) {
+        const unsigned long long t0 = h[i], t1 = h[kGemmProfCap + i];
+        if (t0 == ~0ull || t1 < t0) continue;   // a launch with no CTA past the wait (cannot happen in a step)
+        ns += static_cast<double>(t1 - t0);
+        ++counted;
+    }
+    *ms = ns * 1e-6;
+    *launches = counted;
     return UD_OK;
 }
 

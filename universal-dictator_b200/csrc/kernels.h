@@ -42,7 +42,11 @@ struct GemmEpilogue {
     void* out = nullptr;             // fp32 or bf16 [M, ldo]
     int ldo = 0;
     int out_bf16 = 0;
+    // Graph-mode timers (2-CTA GEMM only, null when off): prof[0] receives the earliest global-timer time (ns) at
+    // which a CTA passed the grid-dependency wait, prof[kGemmProfCap] the latest at which a CTA finished.
+    unsigned long long* prof = nullptr;
 };
+constexpr int kGemmProfCap = 2048;   // GEMM launches one step can time
 
 // ---- tcgen05 GEMM (bf16 x bf16 -> fp32 in TMEM), A [M, K] row-major (lda), W [N, K] row-major.
 // Requirements: K % 64 == 0, N % 128 == 0, lda/ldw multiples of 8 elements, 16-byte aligned bases.

@@ -39,7 +39,8 @@ ABI_SYMBOLS = [
     "ud_rnnt_decode_static",
     "ud_cache_append", "ud_cache_roll", "ud_cache_gather", "ud_cache_evict", "ud_cache_read", "ud_stream_info",
     "ud_get_cuda_stream", "ud_pool_info", "ud_synchronize", "ud_launch_count", "ud_debug_gemm",
-    "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_last_error",
+    "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_gemm_timers", "ud_gemm_timers_read",
+    "ud_last_error",
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
     "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
     "ud_streamer_release", "ud_streamer_emissions", "ud_streamer_step_times", "ud_streamer_set_end_padding",
@@ -109,6 +110,8 @@ def lib() -> C.CDLL:
             "ud_debug_wait_probe": (I, [eng, C.c_uint64]),
             "ud_profile_enable": (I, [eng, I]),
             "ud_profile_read": (I, [eng, I, P(C.c_double), P(C.c_int64)]),
+            "ud_gemm_timers": (I, [eng, I]),
+            "ud_gemm_timers_read": (I, [eng, P(C.c_double), P(I)]),
             "ud_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
             "ud_status_string": (C.c_char_p, [I]),
             "ud_get_config": (I, [eng, P(Config)]),
@@ -412,6 +415,16 @@ class Engine:
             check(lib().ud_profile_read(self.h, k, C.byref(ms), C.byref(n)))
             out[name] = (ms.value, n.value)
         return out
+
+    def gemm_timers(self, enable: bool):
+        """Graph-mode GEMM timers for the following steps (their graphs are captured separately)."""
+        check(lib().ud_gemm_timers(self.h, int(enable)))
+
+    def gemm_timers_read(self) -> tuple[float, int]:
+        """(summed device ms of the last step's 2-CTA GEMM launches, from first start to last finish each; launches)."""
+        ms, n = C.c_double(), C.c_int()
+        check(lib().ud_gemm_timers_read(self.h, C.byref(ms), C.byref(n)))
+        return ms.value, n.value
 
     def launch_count(self) -> int:
         v = C.c_int64()
