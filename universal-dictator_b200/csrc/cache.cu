@@ -4,6 +4,9 @@
 // K/V: frame f of a stream lives at row f % PF of page pages[(f / PF) % kPageSlots] in the layer's pool;
 // the roll only advances `head`, so it moves no data. Conv: ring of conv_ring rows per (layer, slot),
 // frame f at row f % conv_ring. All copies are 16-byte vectors, one row per warp, coalesced.
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -106,6 +109,108 @@ __global__ void gather_kernel(T* __restrict__ kv_out, T* __restrict__ conv_out, 
     }
 }
 
+// The same gather by bulk copies (TMA engine, no multicast): a window's rows are contiguous within each page, and
+// the conv ring's within each of its two wrapped parts, so one thread splits the CTA's output into runs of up to
+// kGatherBytes and moves each run global -> shared (cp.async.bulk on an mbarrier, bounded wait) -> global (bulk
+// store), two runs in flight. The window's unfilled rows are zeroed by all threads with plain stores first.
+// grid (n, n_layers), 128 threads, 2 * kGatherBytes of dynamic shared memory.
+constexpr int kGatherBytes = 32 * 1024;
+constexpr int kMaxRuns = 40;
+
+template <typename T>
+__global__ void __launch_bounds__(128) gather_bulk_kernel(T* __restrict__ kv_out, T* __restrict__ conv_out,
+                                                          const BatchEntry* __restrict__ meta, const CacheGeom cg,
+                                                          int* err) {
+    constexpr int CH = 16 / sizeof(T);
+    extern __shared__ __align__(128) unsigned char gsm[];
+    __shared__ uint64_t bar[2];
+    __shared__ int fail;
+    const int b = blockIdx.x, layer = blockIdx.y;
+    const BatchEntry& me = meta[b];
+    const int D = cg.D, NL = cg.n_layers, L = cg.L, R = cg.conv_ring, PF = cg.page_frames;
+    const uint32_t row_bytes = static_cast<uint32_t>(D * sizeof(T));
+    const int run_max = kGatherBytes / static_cast<int>(row_bytes);
+    const int lo = L - me.cache_len;   // window rows j < lo hold no frame yet: zero
+    T* kvd = kv_out ? kv_out + (static_cast<size_t>(b) * NL + layer) * 2 * L * D : nullptr;
+    if (kvd && lo > 0) {
+        const int n16 = lo * D / CH;
+        for (int kind = 0; kind < 2; ++kind)
+            for (int i = threadIdx.x; i < n16; i += blockDim.x)
+                reinterpret_cast<uint4*>(kvd + static_cast<size_t>(kind) * L * D)[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (threadIdx.x == 0) {
+        fail = 0;
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    // The runs: (source, destination, rows).
+    const T* rsrc[kMaxRuns];
+    T* rdst[kMaxRuns];
+    int rrows[kMaxRuns];
+    int nr = 0;
+    if (kvd) {
+        T* pools[2] = {reinterpret_cast<T*>(cg.kpool), reinterpret_cast<T*>(cg.vpool)};
+        for (int kind = 0; kind < 2; ++kind) {
+            for (int j = lo > 0 ? lo : 0; j < L;) {
+                const int f = me.head - L + j;
+                const int page = me.pages[(f / PF) % kPageSlots];
+                int rows = PF - f % PF;
+                rows = min(rows, L - j);
+                rows = min(rows, run_max);
+                T* dst = kvd + (static_cast<size_t>(kind) * L + j) * D;
+                if (page < 0 || page >= cg.n_pages) {   // unmapped: recorded, the rows read as zero
+                    report_error(err, DEV_BAD_PAGE);
+                    for (int i = 0; i < rows * D / CH; ++i) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0u, 0u, 0u, 0u);
+                } else if (nr < kMaxRuns) {
+                    rsrc[nr] = pools[kind] + ((static_cast<size_t>(layer) * cg.n_pages + page) * PF + f % PF) * D;
+                    rdst[nr] = dst;
+                    rrows[nr++] = rows;
+                }
+                j += rows;
+            }
+        }
+    }
+    if (conv_out) {
+        const T* ring = reinterpret_cast<const T*>(cg.conv) + (static_cast<size_t>(layer) * cg.max_streams + me.slot) * R * D;
+        T* dst = conv_out + (static_cast<size_t>(b) * NL + layer) * R * D;
+        for (int i = 0; i < R;) {   // output row i is frame head - R + i, ring row (head + i) % R
+            const int rr = (me.head + i) % R;
+            const int rows = min(min(R - rr, R - i), run_max);
+            if (nr < kMaxRuns) {
+                rsrc[nr] = ring + static_cast<size_t>(rr) * D;
+                rdst[nr] = dst + static_cast<size_t>(i) * D;
+                rrows[nr++] = rows;
+            }
+            i += rows;
+        }
+    }
+    T* buf[2] = {reinterpret_cast<T*>(gsm), reinterpret_cast<T*>(gsm + kGatherBytes)};
+    uint32_t phase[2] = {0u, 0u};
+    auto issue = [&](int r) {
+        const int s = r & 1;
+        const uint32_t bytes = static_cast<uint32_t>(rrows[r]) * row_bytes;
+        mbar_arrive_expect_tx(&bar[s], bytes);
+        bulk_load(buf[s], rsrc[r], bytes, &bar[s]);
+    };
+    if (nr > 0) issue(0);
+    for (int r = 0; r < nr; ++r) {
+        const int s = r & 1;
+        if (r + 1 < nr) {
+            if (r >= 1) tma_store_wait_read<0>();   // run r - 1's store has read the buffer run r + 1 reuses
+            issue(r + 1);
+        }
+        if (!mbar_wait_bounded(&bar[s], phase[s], err, DEV_TIMEOUT_COPY, &fail)) break;
+        phase[s] ^= 1u;
+        bulk_store(rdst[r], buf[s], static_cast<uint32_t>(rrows[r]) * row_bytes);
+        tma_store_commit();
+    }
+    tma_store_wait_all();
+    if (fail) __nanosleep(100000);   // an expired wait: give loads already issued into this CTA time to land
+}
+
 // grid (n, n_layers): zero the conv ring of each listed slot.
 template <typename T>
 __global__ void conv_zero_kernel(const int* __restrict__ slots, const CacheGeom cg) {
@@ -136,6 +241,21 @@ void cache_gather(T* kv_out, T* conv_out, const BatchEntry* meta, int n, const C
                   cudaStream_t s) {
     if (n <= 0 || cg.n_layers <= 0) return;
     dim3 grid(n, cg.n_layers);
+    static int bulk = -1;
+    if (bulk < 0) {
+        const char* v = std::getenv("UD_GATHER_BULK");
+        bulk = v ? std::atoi(v) : 1;
+    }
+    const bool aligned = (cg.D * sizeof(T)) % 16 == 0 && static_cast<int>(cg.D * sizeof(T)) <= kGatherBytes;
+    // runs: per kind at most one per page boundary or kGatherBytes of rows crossed, plus the ring's two parts
+    const int rm = aligned ? std::min(kGatherBytes / static_cast<int>(cg.D * sizeof(T)), cg.page_frames) : 1;
+    const bool fits = 2 * ((cg.L + rm - 1) / rm + 1) + 2 <= kMaxRuns;
+    if (bulk && aligned && fits) {
+        static size_t attr[kMaxDevices] = {};
+        ensure_dyn_smem(gather_bulk_kernel<T>, 2 * kGatherBytes, attr);
+        gather_bulk_kernel<T><<<grid, 128, 2 * kGatherBytes, s>>>(kv_out, conv_out, meta, cg, dev_err);
+        return;
+    }
     gather_kernel<T><<<grid, 256, 0, s>>>(kv_out, conv_out, meta, cg, dev_err);
 }
 

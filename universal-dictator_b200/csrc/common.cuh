@@ -24,6 +24,7 @@ enum DeviceError : int {
     DEV_TIMEOUT_ATTN = 8,       // attention: waiting for a staged item or a free stage
     DEV_RANGE_F16 = 9,          // RNN-T tensor-core decoder: an operand value beyond the fp16 range
     DEV_TIMEOUT_CONV = 10,      // conv module: waiting for its ring rows and LayerNorm parameters
+    DEV_TIMEOUT_COPY = 11,      // cache gather: waiting for a staged run of rows
 };
 
 template <typename T> __device__ __forceinline__ float to_f(T v);

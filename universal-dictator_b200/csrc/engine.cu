@@ -335,8 +335,9 @@ ud_status device_error_status(ud_engine* e, int code) {
     static const char* names[] = {"ok", "GEMM TMA stage wait", "GEMM free-stage wait", "GEMM accumulator wait",
                                   "GEMM TMEM drain wait", "unmapped cache page", "test wait",
                                   "RNN-T grid barrier wait", "attention stage wait",
-                                  "RNN-T decoder input beyond the fp16 range", "conv module copy wait"};
-    const char* nm = (code >= 0 && code <= 10) ? names[code] : "unknown";
+                                  "RNN-T decoder input beyond the fp16 range", "conv module copy wait",
+                                  "cache gather copy wait"};
+    const char* nm = (code >= 0 && code <= 11) ? names[code] : "unknown";
     if (code == DEV_BAD_PAGE || code == DEV_RANGE_F16)
         return fail(UD_ERR_INVALID_ARGUMENT, std::string("device reported: ") + nm);
     return fail(UD_ERR_DEVICE_TIMEOUT, std::string("device wait expired: ") + nm);
