@@ -815,24 +815,25 @@ def main():
     tc_launches = (prof["gemm_tc"][1] + prof["gemm_tc2"][1]) / 2
     flops = gemm_flops_per_step(n, T, R, cfg)
     achieved = flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else None
-    # The same GEMMs inside the graph-replayed step (outside the timed region): each 2-CTA GEMM launch stamps the
-    # global timer when its first CTA passes the grid-dependency wait and when its last CTA finishes; the step's
-    # graph and programmatic dependent launch are as in the timed region. Five steps: the first runs eagerly, the
-    # second captures the timer graph, the last three replay it and are averaged.
-    graph_mode = None
-    eng.gemm_timers(True)
+    # The same kernels inside the graph-replayed step (outside the timed region): each 2-CTA GEMM, TMA attention,
+    # LayerNorm and conv-module launch stamps the global timer when its first CTA passes the grid-dependency wait
+    # and when its last CTA's work ends; the step's graph and programmatic dependent launch are as in the timed
+    # region. Five steps: the first runs eagerly, the second captures the timer graph, the last three replay it and
+    # are averaged.
+    graph_mode, kernel_graph = None, None
+    eng.graph_timers(True)
     g_runs = []
     for i in range(5):
         step()
-        g_ms, g_n = eng.gemm_timers_read()
-        if i >= 2 and g_n > 0:
-            g_runs.append((g_ms, g_n))
-    eng.gemm_timers(False)
-    if g_runs:
-        g_ms = sum(r[0] for r in g_runs) / len(g_runs)
+        if i >= 2:
+            g_runs.append(eng.graph_timers_read())
+    eng.graph_timers(False)
+    if g_runs and g_runs[-1]["gemm_tc2"][1] > 0:
+        kernel_graph = {k: round(sum(r[k][0] for r in g_runs) / len(g_runs), 4) for k in g_runs[-1] if g_runs[-1][k][1]}
+        g_ms = kernel_graph["gemm_tc2"]
         g_ach = flops / (g_ms / 1e3) / 1e12
         graph_mode = {"achieved": g_ach, "frac": g_ach / bf16_sus, "gemm_ms_per_step": g_ms,
-                      "launches_per_step": g_runs[-1][1],
+                      "launches_per_step": g_runs[-1]["gemm_tc2"][1],
                       "note": "algorithmic GEMM FLOPs per step / summed (last CTA finish - first CTA past the "
                               "grid-dependency wait) of the 2-CTA GEMM launches, global-timer stamps in the "
                               "graph-replayed step, mean of 3 steps outside the timed region"
@@ -954,6 +955,11 @@ def main():
                                     f"{src} sustained bf16",
                             "graph_mode": graph_mode},
                "kernel_ms_per_step": {k: round(v[0] / 2, 4) for k, v in prof.items() if v[1]},
+               "kernel_ms_per_step_graph": kernel_graph,
+               "kernel_attribution_graph": ("the same kinds in the graph-replayed step, as in the timed region: per "
+                                            "launch, last CTA end - first CTA past the grid-dependency wait "
+                                            "(global-timer stamps), summed per kind, mean of 3 steps outside the "
+                                            "timed region; subsampling and the joint projection are not stamped"),
                "kernel_attribution": ("two extra steps outside the timed region, launched eagerly (no CUDA graph, no "
                                       "programmatic dependent launch) with CUDA events around every launch: "
                                       f"{sum(v[0] for v in prof.values()) / 2:.3f} ms per step summed over the "

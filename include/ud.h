@@ -222,14 +222,16 @@ typedef enum ud_kernel_kind {
 UD_API ud_status ud_profile_enable(ud_engine* e, int enable);
 UD_API ud_status ud_profile_read(ud_engine* e, int kind, double* ms_total, int64_t* launches);
 
-/* Graph-mode GEMM timers. With enable != 0, every 2-CTA tcgen05 GEMM launch of the following steps records, in
- * global-timer nanoseconds, when its first CTA passed the grid-dependency wait and when its last CTA finished;
- * steps run with the timers on are captured in graphs of their own, so the step's CUDA graph and programmatic
- * dependent launch stay as in normal operation. ud_gemm_timers_read synchronises and returns, for the last step,
- * the sum over its GEMM launches of (last finish - first start) in milliseconds and the number of launches. When
- * the layer stack runs as two halves on two streams, the halves' launches overlap and the sum counts both. */
-UD_API ud_status ud_gemm_timers(ud_engine* e, int enable);
-UD_API ud_status ud_gemm_timers_read(ud_engine* e, double* ms, int* launches);
+/* Graph-mode kernel timers. With enable != 0, the following steps' 2-CTA tcgen05 GEMM, TMA attention, LayerNorm
+ * and conv-module launches each record, in global-timer nanoseconds, when their first CTA passed the
+ * grid-dependency wait and when their last CTA's work ended; steps run with the timers on are captured in graphs
+ * of their own, so the step's CUDA graph and programmatic dependent launch stay as in normal operation.
+ * ud_graph_timers_read synchronises and returns, for the last step and one ud_kernel_kind (UD_KIND_GEMM_TC2,
+ * UD_KIND_ATTENTION, UD_KIND_NORM or UD_KIND_CONV), the sum over its launches of (last end - first start) in
+ * milliseconds and the number of launches. When the layer stack runs as two halves on two streams, the halves'
+ * launches overlap and the sum counts both. */
+UD_API ud_status ud_graph_timers(ud_engine* e, int enable);
+UD_API ud_status ud_graph_timers_read(ud_engine* e, int kind, double* ms, int* launches);
 
 /* Kernel-level test hook (the reference's GemmTests.swift contract, Step.gemm in Core/Kernels.swift:79-113):
  * C = out_scale * act(A . W^T + bias) + res_scale * R, device pointers, A [M,K] and W [N,K] in the

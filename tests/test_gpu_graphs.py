@@ -30,7 +30,7 @@ def _run(graphs: bool, sd, dims, n=3, env=None, timers=False):
                 os.environ[k] = v
     e.load_weights(sd)
     if timers:
-        e.gemm_timers(True)
+        e.graph_timers(True)
     readings = []
     ids = [e.open(13) for _ in range(n)]
     mels = [torch.randn(400, 128, generator=torch.Generator().manual_seed(20 + i)).numpy() for i in range(n)]
@@ -45,7 +45,7 @@ def _run(graphs: bool, sd, dims, n=3, env=None, timers=False):
         wall_ms = (time.perf_counter() - t0) * 1e3
         outs.append(([p.copy() for p in projs], frames, toks))
         if timers:
-            readings.append((min(plans[i][k][1] for i in act), wall_ms) + e.gemm_timers_read())
+            readings.append((min(plans[i][k][1] for i in act), wall_ms, e.graph_timers_read()))
     e.close()
     return (outs, readings) if timers else outs
 
@@ -75,12 +75,12 @@ def test_graph_replay_bit_identical_at_two_cta_batch():
             assert np.array_equal(x, y)
 
 
-def test_graph_mode_gemm_timers_leave_results_unchanged():
-    """The graph-mode GEMM timers (ud_gemm_timers: global-timer stamps in every 2-CTA GEMM launch, the steps captured
-    in graphs of their own) give the same bits as graph replay without them. At 20 streams x 14 frames every
-    step's 2-CTA GEMMs are timed (at least the 8 projections of each of the 2 layers), each step's summed GEMM
-    time is positive and below the step's wall time. (The short final chunks run too few rows for the 2-CTA GEMMs
-    and are left out.)"""
+def test_graph_mode_timers_leave_results_unchanged():
+    """The graph-mode kernel timers (ud_graph_timers: global-timer stamps in every 2-CTA GEMM, TMA attention,
+    LayerNorm and conv-module launch, the steps captured in graphs of their own) give the same bits as graph replay
+    without them. At 20 streams x 14 frames every step's launches of those kinds are timed (per layer 8 projections,
+    one attention, one conv module, 4 LayerNorms) and the summed time of all of them is positive and below the
+    step's wall time. (The short final chunks run too few rows for the 2-CTA GEMMs and are left out.)"""
     dims = ModelDims(n_layers=2)
     sd = make_weights(dims, seed=1)
     plain = _run(True, sd, dims, n=20)
@@ -91,9 +91,12 @@ def test_graph_mode_gemm_timers_leave_results_unchanged():
             assert np.array_equal(x, y)
     full = [r for r in readings if r[0] >= 105]   # first (105 mel rows) and steady (121) chunks of all 20 streams
     assert len(full) >= 3
-    for rows, wall_ms, gemm_ms, launches in full:
-        assert launches >= 2 * 8, launches
-        assert 0.0 < gemm_ms < wall_ms, (gemm_ms, wall_ms)
+    for rows, wall_ms, kinds in full:
+        assert kinds["gemm_tc2"][1] >= 2 * 8, kinds
+        assert kinds["attention"][1] == 2 and kinds["conv"][1] == 2, kinds
+        assert kinds["norm"][1] >= 2 * 4, kinds
+        assert all(ms > 0.0 for ms, _ in kinds.values()), kinds
+        assert sum(ms for ms, _ in kinds.values()) < wall_ms, (kinds, wall_ms)
 
 
 def test_tma_attention_matches_one_cta_per_stream_head_kernel():

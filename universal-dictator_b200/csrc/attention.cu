@@ -617,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
     const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mp, int D, int L, int ptab_row0,
     const float* __restrict__ bias_u, const float* __restrict__ bias_v, const BatchEntry* __restrict__ meta, int n,
     int n_heads, int ipc, int layer, int n_pages, bf16* __restrict__ kw, bf16* __restrict__ vw, bf16* __restrict__ out,
-    int ldo, int* err) {
+    int ldo, int* err, unsigned long long* timer) {
     constexpr int DKk = 128;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -647,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
     if (tid < 64) reinterpret_cast<uint32_t*>(sm + Lay::ZERO)[tid] = 0u;
     __syncthreads();
     pdl_wait();   // the QKV projection and the step's metadata come from earlier work on the stream
+    if (tid == 0) timer_start(timer);
 
     if (warp == kComputeWarps) {
         // ---------------------------------------------------------------- producer warp
@@ -869,6 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
         compute_sync();   // every read of this stage, the window and the scores is done
         if (tid == 0) mbar_arrive(&empty[s]);
     }
+    if (tid == 0) timer_end(timer);   // after the last item's group barrier: every compute warp is done
     if (*abort_v) __nanosleep(100000);   // after a failed wait: let copies already issued into this CTA land
 }
 
@@ -903,7 +905,7 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
 bool relpos_attention_tma(const TmaMatrix& qkv, const TmaMatrix& kpool, const TmaMatrix& vpool, const TmaMatrix& ptab,
                           int ptab_row0, const float* bias_u, const float* bias_v, const BatchEntry* meta, int n,
                           int tmax_batch, const CacheGeom& cg, int layer, bf16* out, int ldo, int n_heads, int num_sms,
-                          int* dev_err, cudaStream_t s) {
+                          int* dev_err, cudaStream_t s, unsigned long long* timer) {
     using namespace tma_attn;
     if (n <= 0) return true;
     if (tmax_batch > kTM || cg.page_frames != 16 || cg.L + kTM - 1 + 15 >= kPRows || cg.L + kTM > kNKP) return false;
@@ -915,7 +917,7 @@ bool relpos_attention_tma(const TmaMatrix& qkv, const TmaMatrix& kpool, const Tm
     ensure_dyn_smem(attn_tma_kernel, Lay::SMEM, attr);
     launch_pdl(attn_tma_kernel, dim3(grid), dim3(kThreads), Lay::SMEM, s, qkv.map, kpool.map, vpool.map, ptab.map, cg.D,
                cg.L, ptab_row0, bias_u, bias_v, meta, n, n_heads, ipc, layer, cg.n_pages,
-               reinterpret_cast<bf16*>(cg.kpool), reinterpret_cast<bf16*>(cg.vpool), out, ldo, dev_err);
+               reinterpret_cast<bf16*>(cg.kpool), reinterpret_cast<bf16*>(cg.vpool), out, ldo, dev_err, timer);
     return true;
 }
 

@@ -98,6 +98,17 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
+// Graph-mode kernel timers (off unless the engine hands a kernel a slot): slot p receives in p[0] the earliest
+// global-timer time (ns) at which a CTA passed the grid-dependency wait, in p[kTimerSlots] the latest at which a
+// CTA's work ended. Slots start at (max, 0) before each timed step.
+constexpr int kTimerSlots = 2048;
+__device__ __forceinline__ void timer_start(unsigned long long* p) {
+    if (p) atomicMin(p, static_cast<unsigned long long>(global_timer_ns()));
+}
+__device__ __forceinline__ void timer_end(unsigned long long* p) {
+    if (p) atomicMax(p + kTimerSlots, static_cast<unsigned long long>(global_timer_ns()));
+}
+
 // Upper bound of any single wait inside a kernel. A healthy kernel never waits this long on one
 // barrier; reaching it means a protocol bug, and the kernel reports instead of hanging.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s

@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
                                                           const float* __restrict__ dw, const float* __restrict__ g,
                                                           const float* __restrict__ beta,
                                                           const BatchEntry* __restrict__ meta, const CacheGeom cg,
-                                                          int layer, int tmax, T* __restrict__ out, int ldo, int* err) {
+                                                          int layer, int tmax, T* __restrict__ out, int ldo, int* err,
+                                                          unsigned long long* timer) {
     pdl_launch_dependents();
     constexpr int R = KW - 1;
     constexpr int FB = sizeof(T) == 2 ? 16 : 8;  // frames whose GLU inputs a thread has in flight at once
@@ -110,6 +111,7 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
     const int c = threadIdx.x * 2;
     const bool own = c < D;
     pdl_wait();
+    if (threadIdx.x == 0) timer_start(timer);
     if (own) {
         for (int t0 = 0; t0 < T_; t0 += FB) {
             Raw val[FB], gate[FB];
@@ -222,6 +224,7 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
         }
     }
     if (threadIdx.x == 0) tma_store_wait_all();  // the ring rows are in global memory before the CTA exits
+    if (lane == 0) timer_end(timer);
 }
 
 }  // namespace
@@ -229,18 +232,19 @@ __global__ void __launch_bounds__(512, 2) conv_module_kernel(const T* __restrict
 template <typename T>
 void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, const float* ln_b, const BatchEntry* meta,
                  int n, int tmax_batch, const CacheGeom& cg, int layer, int K, T* out, int ldo, int* dev_err,
-                 cudaStream_t s) {
+                 cudaStream_t s, unsigned long long* timer) {
     if (n <= 0 || K != 9) return;
     const size_t smem = (sizeof(float) * (static_cast<size_t>(tmax_batch) + 2) + sizeof(T) * 8) * cg.D;
     static size_t attr_set[kMaxDevices] = {};
     ensure_dyn_smem(conv_module_kernel<T, 9>, smem, attr_set);  // also below 48 KB: the kernel has static shared memory too
     launch_pdl(conv_module_kernel<T, 9>, dim3(n), dim3(512), smem, s, pw, ld_pw, dw, ln_g, ln_b, meta, cg, layer,
-               tmax_batch, out, ldo, dev_err);
+               tmax_batch, out, ldo, dev_err, timer);
 }
 
 template void conv_module<float>(const float*, int, const float*, const float*, const float*, const BatchEntry*, int,
-                                 int, const CacheGeom&, int, int, float*, int, int*, cudaStream_t);
+                                 int, const CacheGeom&, int, int, float*, int, int*, cudaStream_t,
+                                 unsigned long long*);
 template void conv_module<bf16>(const bf16*, int, const float*, const float*, const float*, const BatchEntry*, int, int,
-                                const CacheGeom&, int, int, bf16*, int, int*, cudaStream_t);
+                                const CacheGeom&, int, int, bf16*, int, int*, cudaStream_t, unsigned long long*);
 
 }  // namespace ud

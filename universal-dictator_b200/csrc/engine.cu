@@ -154,7 +154,7 @@ struct ud_engine {
     struct GraphEntry {
         cudaGraphExec_t exec;
         int64_t kernels;
-        int gemm_slots;   // timed GEMM launches (graph-mode timers on)
+        std::vector<int> timer_kinds;   // kind of each timer slot its launches stamp (graph-mode timers on)
     };
     bool graphs_on = true;
     bool tc2_on = true;  // 2-CTA tcgen05 tiles for M >= 256, N % 256 == 0
@@ -162,14 +162,14 @@ struct ud_engine {
     bool attn_maps = false;             // the tensor maps below exist
     TmaMatrix attn_qkv_map, attn_k_map, attn_v_map;   // QKV rows (64 x 16 boxes), K and V page pools
     BatchEntry* meta_graph_d = nullptr;
-    // key: n, rows_max, M, tmax_b, tokens, staging buffer, the halves' split row, GEMM timers
+    // key: n, rows_max, M, tmax_b, tokens, staging buffer, the halves' split row, graph-mode timers
     std::map<std::tuple<int, int, int, int, int, int, int, int>, GraphEntry> graphs;
     std::map<std::tuple<int, int, int, int, int, int, int, int>, int> graph_seen;
-    // graph-mode GEMM timers: [kGemmProfCap] first-start times, then [kGemmProfCap] last-finish times (ns)
-    bool gemm_timers = false;
-    unsigned long long* gemm_prof = nullptr;
-    int gemm_prof_n = 0;      // slots handed out while the current step is enqueued
-    int gemm_prof_last = 0;   // slots of the last step run
+    // graph-mode kernel timers: [kTimerSlots] first-start times, then [kTimerSlots] last-finish times (ns)
+    bool timers = false;
+    unsigned long long* timer_buf = nullptr;
+    std::vector<int> timer_kinds;        // kind of each slot handed out while the current step is enqueued
+    std::vector<int> timer_last_kinds;   // the slots of the last step run
     // per-kernel-class timing
     bool prof = false;
     std::vector<cudaEvent_t> prof_events;
@@ -285,6 +285,13 @@ const TmaMatrix* out_map(ud_engine* e, const void* p, int M, int N, int ld, bool
 }
 
 // One GEMM through the engine's dispatch: tcgen05 for bf16 with more than 16 rows, SIMT otherwise.
+// A graph-mode timer slot for the next launch of this kind, or null (timers off, or every slot handed out).
+unsigned long long* timer_slot(ud_engine* e, int kind) {
+    if (!e->timers || static_cast<int>(e->timer_kinds.size()) >= kTimerSlots) return nullptr;
+    e->timer_kinds.push_back(kind);
+    return e->timer_buf + (e->timer_kinds.size() - 1);
+}
+
 ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, const GemmEpilogue& epi) {
     if (M <= 0) return UD_OK;
     cudaStream_t const gs = e->gstream ? e->gstream : e->stream;
@@ -292,7 +299,7 @@ ud_status gemm(ud_engine* e, const void* A, int lda, int M, const WeightMat& W, 
     const bool tc2 = tc && e->tc2_on && M >= 256 && W.N % 16 == 0;
     Launch L_(e, tc2 ? UD_KIND_GEMM_TC2 : tc ? UD_KIND_GEMM_TC : UD_KIND_GEMM_SIMT);
     GemmEpilogue ep = epi;
-    if (tc2 && e->gemm_timers && e->gemm_prof_n < kGemmProfCap) ep.prof = e->gemm_prof + e->gemm_prof_n++;
+    if (tc2) ep.prof = timer_slot(e, UD_KIND_GEMM_TC2);
     if (e->bf) {
         if (!tc) {
             gemm_simt<bf16, bf16>(static_cast<const bf16*>(A), lda, static_cast<const bf16*>(W.p), M, W.N, W.K, epi,
@@ -525,8 +532,8 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
         void* y = static_cast<char*>(e->y) + static_cast<size_t>(row0) * D * es;
         auto ln = [&](const float* g, const float* b) {
             Launch L_(e, UD_KIND_NORM);
-            if (e->bf) layer_norm<bf16>(x, g, b, (bf16*)h, Mh, D, sh);
-            else layer_norm<float>(x, g, b, (float*)h, Mh, D, sh);
+            if (e->bf) layer_norm<bf16>(x, g, b, (bf16*)h, Mh, D, sh, timer_slot(e, UD_KIND_NORM));
+            else layer_norm<float>(x, g, b, (float*)h, Mh, D, sh, timer_slot(e, UD_KIND_NORM));
         };
         auto resid = [&](float scale) {
             GemmEpilogue g = epi_out(x, D, false, e);
@@ -553,7 +560,8 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
             const bool tma_done = e->bf && e->attn_tma_on && e->attn_maps && w.has_pmap &&
                                   relpos_attention_tma(e->attn_qkv_map, e->attn_k_map, e->attn_v_map, w.pmap,
                                                        e->tmax - 16, w.pos_u, w.pos_v, mdh, nh, tmax_b, e->cg, l,
-                                                       (bf16*)e->att, D, e->H, e->num_sms, e->err_d, sh);
+                                                       (bf16*)e->att, D, e->H, e->num_sms, e->err_d, sh,
+                                                       timer_slot(e, UD_KIND_ATTENTION));
             if (tma_done) {
             } else if (e->bf)
                 relpos_attention<bf16>((bf16*)e->qkv, 3 * D, (bf16*)w.ptab, e->tmax, w.pos_u, w.pos_v, mdh, nh, tmax_b,
@@ -569,10 +577,10 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
             Launch L_(e, UD_KIND_CONV);
             if (e->bf)
                 conv_module<bf16>((bf16*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, mdh, nh, tmax_b, e->cg, l, e->KC,
-                                  (bf16*)e->y, D, e->err_d, sh);
+                                  (bf16*)e->y, D, e->err_d, sh, timer_slot(e, UD_KIND_CONV));
             else
                 conv_module<float>((float*)e->pw, 2 * D, w.dw, w.ln_cbn_g, w.ln_cbn_b, mdh, nh, tmax_b, e->cg, l, e->KC,
-                                   (float*)e->y, D, e->err_d, sh);
+                                   (float*)e->y, D, e->err_d, sh, timer_slot(e, UD_KIND_CONV));
             }
             UD_TRY(gemm(e, y, D, Mh, w.pw2, resid(1.0f)));
             ln(w.ln_ff2_g, w.ln_ff2_b);
@@ -580,13 +588,17 @@ ud_status enqueue_step(ud_engine* e, const BatchEntry* md, int n, int M, int tma
             if (l + 1 < NL) {
                 LayerW& nx = e->layers[l + 1];
                 Launch L_(e, UD_KIND_NORM);
-                if (e->bf) layer_norm2<bf16>(x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (bf16*)h, Mh, D, sh);
-                else layer_norm2<float>(x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (float*)h, Mh, D, sh);
+                if (e->bf)
+                    layer_norm2<bf16>(x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (bf16*)h, Mh, D, sh,
+                                      timer_slot(e, UD_KIND_NORM));
+                else
+                    layer_norm2<float>(x, w.ln_out_g, w.ln_out_b, nx.ln_ff1_g, nx.ln_ff1_b, (float*)h, Mh, D, sh,
+                                       timer_slot(e, UD_KIND_NORM));
             } else if (e->cfg.joint_dim) {
                 ln(w.ln_out_g, w.ln_out_b);  // h = LN_out(x): the joint's operand
             } else {
                 Launch L_(e, UD_KIND_NORM);
-                layer_norm<float>(x, w.ln_out_g, w.ln_out_b, x, Mh, D, sh);
+                layer_norm<float>(x, w.ln_out_g, w.ln_out_b, x, Mh, D, sh, timer_slot(e, UD_KIND_NORM));
             }
         }
         return UD_OK;
@@ -694,18 +706,18 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
     }
     const std::tuple<int, int, int, int, int, int, int, int> key{n, rows_max, M, tmax_b, tokens_dev ? 1 : 0,
                                                                  in_dev == e->in_stage ? 0 : 1, m_a,
-                                                                 e->gemm_timers ? 1 : 0};
+                                                                 e->timers ? 1 : 0};
     const bool use_graph = graph_ok && e->graphs_on && !e->prof;
-    if (e->gemm_timers) {   // every slot empty: starts at the largest value, finishes at zero
-        UD_CK(cudaMemsetAsync(e->gemm_prof, 0xff, sizeof(unsigned long long) * kGemmProfCap, e->stream));
-        UD_CK(cudaMemsetAsync(e->gemm_prof + kGemmProfCap, 0, sizeof(unsigned long long) * kGemmProfCap, e->stream));
+    if (e->timers) {   // every slot empty: starts at the largest value, finishes at zero
+        UD_CK(cudaMemsetAsync(e->timer_buf, 0xff, sizeof(unsigned long long) * kTimerSlots, e->stream));
+        UD_CK(cudaMemsetAsync(e->timer_buf + kTimerSlots, 0, sizeof(unsigned long long) * kTimerSlots, e->stream));
     }
-    e->gemm_prof_n = 0;
+    e->timer_kinds.clear();
     if (!use_graph) {
         UD_TRY(upload_meta(e, mi, n));
         UD_TRY(enqueue_step(e, e->meta_d[mi], n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev, ntok_dev,
                             n_a, m_a));
-        e->gemm_prof_last = e->gemm_prof_n;
+        e->timer_last_kinds = e->timer_kinds;
     } else {
         // Metadata for the graph's fixed buffer; the pinned source slot is protected by the ring's event.
         UD_CK(cudaMemcpyAsync(e->meta_graph_d, mh, sizeof(BatchEntry) * n, cudaMemcpyHostToDevice, e->stream));
@@ -734,18 +746,18 @@ ud_status run_batch(ud_engine* e, int n, const ud_stream_id* ids, const float* i
             const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
             if (ie != cudaSuccess) return fail(UD_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
-            it = e->graphs.emplace(key, ud_engine::GraphEntry{exec, kernels, e->gemm_prof_n}).first;
+            it = e->graphs.emplace(key, ud_engine::GraphEntry{exec, kernels, e->timer_kinds}).first;
         }
         if (it != e->graphs.end()) {
             UD_CK(cudaGraphLaunch(it->second.exec, e->stream));
             e->launches += it->second.kernels;
-            e->gemm_prof_last = it->second.gemm_slots;
+            e->timer_last_kinds = it->second.timer_kinds;
         } else {
             e->graph_seen[key] += 1;
-            e->gemm_prof_n = 0;
+            e->timer_kinds.clear();
             UD_TRY(enqueue_step(e, e->meta_graph_d, n, M, tmax_b, rows_max, in_dev, rows_stride, out_dev, tokens_dev,
                                 ntok_dev, n_a, m_a));
-            e->gemm_prof_last = e->gemm_prof_n;
+            e->timer_last_kinds = e->timer_kinds;
         }
     }
     UD_CK(cudaGetLastError());
@@ -2093,30 +2105,31 @@ ud_status ud_profile_enable(ud_engine* e, int enable) {
     return UD_OK;
 }
 
-ud_status ud_gemm_timers(ud_engine* e, int enable) {
+ud_status ud_graph_timers(ud_engine* e, int enable) {
     if (!e) return fail(UD_ERR_INVALID_ARGUMENT, "NULL engine");
     UD_CK(cudaSetDevice(e->device));
-    if (enable && !e->gemm_prof) UD_TRY(dalloc(e, &e->gemm_prof, 2 * static_cast<size_t>(kGemmProfCap)));
-    e->gemm_timers = enable != 0;
-    e->gemm_prof_last = 0;
+    if (enable && !e->timer_buf) UD_TRY(dalloc(e, &e->timer_buf, 2 * static_cast<size_t>(kTimerSlots)));
+    e->timers = enable != 0;
+    e->timer_last_kinds.clear();
     return UD_OK;
 }
 
-ud_status ud_gemm_timers_read(ud_engine* e, double* ms, int* launches) {
-    if (!e || !ms || !launches) return fail(UD_ERR_INVALID_ARGUMENT, "bad argument");
+ud_status ud_graph_timers_read(ud_engine* e, int kind, double* ms, int* launches) {
+    if (!e || !ms || !launches || kind < 0 || kind >= UD_KIND_COUNT) return fail(UD_ERR_INVALID_ARGUMENT, "bad argument");
     UD_CK(cudaSetDevice(e->device));
     *ms = 0.0;
     *launches = 0;
-    if (!e->gemm_prof || e->gemm_prof_last <= 0) return UD_OK;
-    const int n = e->gemm_prof_last;
-    std::vector<unsigned long long> h(2 * static_cast<size_t>(kGemmProfCap));
+    if (!e->timer_buf || e->timer_last_kinds.empty()) return UD_OK;
+    const int n = static_cast<int>(e->timer_last_kinds.size());
+    std::vector<unsigned long long> h(2 * static_cast<size_t>(kTimerSlots));
     UD_CK(cudaStreamSynchronize(e->stream));
-    UD_CK(cudaMemcpy(h.data(), e->gemm_prof, sizeof(unsigned long long) * h.size(), cudaMemcpyDeviceToHost));
+    UD_CK(cudaMemcpy(h.data(), e->timer_buf, sizeof(unsigned long long) * h.size(), cudaMemcpyDeviceToHost));
     double ns = 0.0;
     int counted = 0;
     for (int i = 0; i < n; ++i) {
-        const unsigned long long t0 = h[i], t1 = h[kGemmProfCap + i];
-        if (t0 == ~0ull || t1 < t0) continue;   // a launch with no CTA past the wait (cannot happen in a step)
+        if (e->timer_last_kinds[i] != kind) continue;
+        const unsigned long long t0 = h[i], t1 = h[kTimerSlots + i];
+        if (t0 == ~0ull || t1 < t0) continue;   // a slot its kernel did not use (another path ran)
         ns += static_cast<double>(t1 - t0);
         ++counted;
     }

@@ -128,7 +128,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     }
     pdl_wait();  // the prologue above overlaps the previous kernel; its outputs are read only from here on
-    if (epi.prof && threadIdx.x == 0) atomicMin(epi.prof, static_cast<unsigned long long>(global_timer_ns()));
+    if (threadIdx.x == 0) timer_start(epi.prof);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -282,8 +282,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     cluster_sync();  // no CTA frees TMEM while its peer's MMAs or epilogue may still touch the pair's state
-    if (epi.prof && threadIdx.x == 0)
-        atomicMax(epi.prof + kGemmProfCap, static_cast<unsigned long long>(global_timer_ns()));
+    if (threadIdx.x == 0) timer_end(epi.prof);
     if (*abort_v) __nanosleep(100000);
     if (warp == 1) {
         tc_fence_after();

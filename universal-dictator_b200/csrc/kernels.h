@@ -42,11 +42,9 @@ struct GemmEpilogue {
     void* out = nullptr;             // fp32 or bf16 [M, ldo]
     int ldo = 0;
     int out_bf16 = 0;
-    // Graph-mode timers (2-CTA GEMM only, null when off): prof[0] receives the earliest global-timer time (ns) at
-    // which a CTA passed the grid-dependency wait, prof[kGemmProfCap] the latest at which a CTA finished.
+    // Graph-mode timer slot (2-CTA GEMM only, null when off; timer_start / timer_end in common.cuh).
     unsigned long long* prof = nullptr;
 };
-constexpr int kGemmProfCap = 2048;   // GEMM launches one step can time
 
 // ---- tcgen05 GEMM (bf16 x bf16 -> fp32 in TMEM), A [M, K] row-major (lda), W [N, K] row-major.
 // Requirements: K % 64 == 0, N % 128 == 0, lda/ldw multiples of 8 elements, 16-byte aligned bases.
@@ -80,11 +78,12 @@ void gemm_simt(const TA* A, int lda, const TW* W, int M, int N, int K, const Gem
 
 // ---- LayerNorm over rows of width D (eps 1e-5). x fp32 [M, D] -> y (TO) [M, D].
 template <typename TO>
-void layer_norm(const float* x, const float* g, const float* b, TO* y, int M, int D, cudaStream_t s);
+void layer_norm(const float* x, const float* g, const float* b, TO* y, int M, int D, cudaStream_t s,
+                unsigned long long* timer = nullptr);
 // x <- LN1(x) (fp32, in place), y <- LN2(x) in TO: a layer's norm_out fused with the next layer's norm_ff1.
 template <typename TO>
 void layer_norm2(float* x, const float* g1, const float* b1, const float* g2, const float* b2, TO* y, int M, int D,
-                 cudaStream_t s);
+                 cudaStream_t s, unsigned long long* timer = nullptr);
 
 // ---- Per-stream step metadata, uploaded once per batched step.
 constexpr int kPageSlots = 8;     // page-table slots per stream (ring of pages)
@@ -121,7 +120,7 @@ void relpos_attention(const T* qkv, int ld_qkv, const T* ptab, int tmax, const f
 template <typename T>
 void conv_module(const T* pw, int ld_pw, const float* dw, const float* ln_g, const float* ln_b,
                  const BatchEntry* meta, int n, int tmax_batch, const CacheGeom& cg, int layer, int K, T* out,
-                 int ldo, int* dev_err, cudaStream_t s);
+                 int ldo, int* dev_err, cudaStream_t s, unsigned long long* timer = nullptr);
 
 // ---- Subsampling (causal dw-striding x8, channel-last activations [b][t][f][c]).
 // conv0 + ReLU fused with the stage-1 depthwise conv: mel [n][rows_stride][mel_bins] -> out [n][T2][F2][C].
@@ -232,7 +231,7 @@ size_t relpos_attention_smem_bytes(int tmax_batch, int L, int elem_bytes);
 bool relpos_attention_tma(const TmaMatrix& qkv, const TmaMatrix& kpool, const TmaMatrix& vpool, const TmaMatrix& ptab,
                           int ptab_row0, const float* bias_u, const float* bias_v, const BatchEntry* meta, int n,
                           int tmax_batch, const CacheGeom& cg, int layer, bf16* out, int ldo, int n_heads, int num_sms,
-                          int* dev_err, cudaStream_t s);
+                          int* dev_err, cudaStream_t s, unsigned long long* timer = nullptr);
 size_t rnnt_smem_bytes(const RnntWeights& w);
 
 // ---- misc

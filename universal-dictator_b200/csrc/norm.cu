@@ -82,12 +82,14 @@ __device__ __forceinline__ void load_row(const float* xr, int lane, float (&v)[N
 
 template <typename TO, int NV>
 __global__ void __launch_bounds__(256) ln_kernel(const float* x, const float* __restrict__ g,
-                                                 const float* __restrict__ b, TO* y, int M, int D) {
+                                                 const float* __restrict__ b, TO* y, int M, int D,
+                                                 unsigned long long* timer) {
     pdl_launch_dependents();
     __shared__ __align__(16) float sg[1024], sb[1024];
     stage_affine(g, b, sg, sb, D);
     __syncthreads();
     pdl_wait();
+    if (threadIdx.x == 0) timer_start(timer);
     // x and y may alias (in-place): each warp reads its whole row before writing it.
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
@@ -105,18 +107,21 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* x, const float* __
         for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
         store4<TO>(yr + (i * 32 + lane) * 4, o);
     }
+    if (lane == 0) timer_end(timer);
 }
 
 template <typename TO, int NV>
 __global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const float* __restrict__ g1,
                                                   const float* __restrict__ b1, const float* __restrict__ g2,
-                                                  const float* __restrict__ b2, TO* __restrict__ y, int M, int D) {
+                                                  const float* __restrict__ b2, TO* __restrict__ y, int M, int D,
+                                                  unsigned long long* timer) {
     pdl_launch_dependents();
     __shared__ __align__(16) float sg1[1024], sb1[1024], sg2[1024], sb2[1024];
     stage_affine(g1, b1, sg1, sb1, D);
     stage_affine(g2, b2, sg2, sb2, D);
     __syncthreads();
     pdl_wait();
+    if (threadIdx.x == 0) timer_start(timer);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + warp;
     if (row >= M) return;
@@ -143,28 +148,32 @@ __global__ void __launch_bounds__(256) ln2_kernel(float* __restrict__ x, const f
         for (int j = 0; j < 4; ++j) o[j] = (v[i][j] - mean) * rstd * gg[j] + bb[j];
         store4<TO>(yr + (i * 32 + lane) * 4, o);
     }
+    if (lane == 0) timer_end(timer);
 }
 
 }  // namespace
 
 template <typename TO>
-void layer_norm(const float* x, const float* g, const float* b, TO* y, int M, int D, cudaStream_t s) {
+void layer_norm(const float* x, const float* g, const float* b, TO* y, int M, int D, cudaStream_t s,
+                unsigned long long* timer) {
     if (M <= 0) return;
-    UD_LN_DISPATCH(ln_kernel, x, g, b, y, M, D);
+    UD_LN_DISPATCH(ln_kernel, x, g, b, y, M, D, timer);
 }
 
 template <typename TO>
 void layer_norm2(float* x, const float* g1, const float* b1, const float* g2, const float* b2, TO* y, int M, int D,
-                 cudaStream_t s) {
+                 cudaStream_t s, unsigned long long* timer) {
     if (M <= 0) return;
-    UD_LN_DISPATCH(ln2_kernel, x, g1, b1, g2, b2, y, M, D);
+    UD_LN_DISPATCH(ln2_kernel, x, g1, b1, g2, b2, y, M, D, timer);
 }
 
-template void layer_norm<float>(const float*, const float*, const float*, float*, int, int, cudaStream_t);
-template void layer_norm<bf16>(const float*, const float*, const float*, bf16*, int, int, cudaStream_t);
+template void layer_norm<float>(const float*, const float*, const float*, float*, int, int, cudaStream_t,
+                                unsigned long long*);
+template void layer_norm<bf16>(const float*, const float*, const float*, bf16*, int, int, cudaStream_t,
+                               unsigned long long*);
 template void layer_norm2<float>(float*, const float*, const float*, const float*, const float*, float*, int, int,
-                                 cudaStream_t);
+                                 cudaStream_t, unsigned long long*);
 template void layer_norm2<bf16>(float*, const float*, const float*, const float*, const float*, bf16*, int, int,
-                                cudaStream_t);
+                                cudaStream_t, unsigned long long*);
 
 }  // namespace ud

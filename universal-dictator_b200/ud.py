@@ -39,7 +39,7 @@ ABI_SYMBOLS = [
     "ud_rnnt_decode_static",
     "ud_cache_append", "ud_cache_roll", "ud_cache_gather", "ud_cache_evict", "ud_cache_read", "ud_stream_info",
     "ud_get_cuda_stream", "ud_pool_info", "ud_synchronize", "ud_launch_count", "ud_debug_gemm",
-    "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_gemm_timers", "ud_gemm_timers_read",
+    "ud_debug_wait_probe", "ud_profile_enable", "ud_profile_read", "ud_graph_timers", "ud_graph_timers_read",
     "ud_last_error",
     "ud_status_string", "ud_get_config", "ud_chunk_next", "ud_streamer_create", "ud_streamer_destroy",
     "ud_streamer_open", "ud_streamer_push", "ud_streamer_step", "ud_streamer_finished", "ud_streamer_tokens",
@@ -110,8 +110,8 @@ def lib() -> C.CDLL:
             "ud_debug_wait_probe": (I, [eng, C.c_uint64]),
             "ud_profile_enable": (I, [eng, I]),
             "ud_profile_read": (I, [eng, I, P(C.c_double), P(C.c_int64)]),
-            "ud_gemm_timers": (I, [eng, I]),
-            "ud_gemm_timers_read": (I, [eng, P(C.c_double), P(I)]),
+            "ud_graph_timers": (I, [eng, I]),
+            "ud_graph_timers_read": (I, [eng, I, P(C.c_double), P(I)]),
             "ud_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
             "ud_status_string": (C.c_char_p, [I]),
             "ud_get_config": (I, [eng, P(Config)]),
@@ -416,15 +416,19 @@ class Engine:
             out[name] = (ms.value, n.value)
         return out
 
-    def gemm_timers(self, enable: bool):
-        """Graph-mode GEMM timers for the following steps (their graphs are captured separately)."""
-        check(lib().ud_gemm_timers(self.h, int(enable)))
+    def graph_timers(self, enable: bool):
+        """Graph-mode kernel timers for the following steps (their graphs are captured separately)."""
+        check(lib().ud_graph_timers(self.h, int(enable)))
 
-    def gemm_timers_read(self) -> tuple[float, int]:
-        """(summed device ms of the last step's 2-CTA GEMM launches, from first start to last finish each; launches)."""
-        ms, n = C.c_double(), C.c_int()
-        check(lib().ud_gemm_timers_read(self.h, C.byref(ms), C.byref(n)))
-        return ms.value, n.value
+    def graph_timers_read(self) -> dict[str, tuple[float, int]]:
+        """{kind: (summed device ms of the last step's launches of that kind, each from its first CTA past the
+        grid-dependency wait to its last CTA's end; launches)} for the timed kinds."""
+        out = {}
+        for name in ("gemm_tc2", "attention", "norm", "conv"):
+            ms, n = C.c_double(), C.c_int()
+            check(lib().ud_graph_timers_read(self.h, KINDS.index(name), C.byref(ms), C.byref(n)))
+            out[name] = (ms.value, n.value)
+        return out
 
     def launch_count(self) -> int:
         v = C.c_int64()
