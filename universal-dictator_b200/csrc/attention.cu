@@ -634,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
+            mbar_init(&empty[i], kComputeWarps);   // every compute warp releases the stage when done with it
         }
         mbar_init(pfull, 1);
         *abort_flag = 0;
@@ -867,9 +867,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
                 *reinterpret_cast<__nv_bfloat162*>(out + static_cast<size_t>(row_off + g + 8) * ldo + col) =
                     __floats2bfloat162_rn(acc[2], acc[3]);
         }
-        compute_sync();   // every read of this stage, the window and the scores is done
-        if (tid == 0) mbar_arrive(&empty[s]);
+        // This warp's reads of the stage and the window are done: it releases them (the scores are rewritten only
+        // after the next item's group barrier, which every warp reaches after this point).
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
+    compute_sync();   // every compute warp has finished its last item
     if (tid == 0) timer_end(timer);   // after the last item's group barrier: every compute warp is done
     if (*abort_v) __nanosleep(100000);   // after a failed wait: let copies already issued into this CTA land
 }
