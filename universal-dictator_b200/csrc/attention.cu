@@ -646,13 +646,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
     }
     if (tid < 64) reinterpret_cast<uint32_t*>(sm + Lay::ZERO)[tid] = 0u;
     __syncthreads();
-    pdl_wait();   // the QKV projection and the step's metadata come from earlier work on the stream
-    if (tid == 0) timer_start(timer);
 
     if (warp == kComputeWarps) {
         // ---------------------------------------------------------------- producer warp
         // Lane 0 issues the copies; the whole warp reads the next item's window (before waiting for its stage, so
-        // the metadata load overlaps the wait) and writes the stage's key -> staged-row table.
+        // the metadata load overlaps the wait) and writes the stage's key -> staged-row table. The first item's
+        // position rows and cached page boxes are issued before the grid-dependency wait: none of them comes from
+        // the previous kernel (the pages of this layer were written by this kernel in an earlier step, the
+        // position table is a weight, the metadata is copied in before the step), so they overlap its tail; the
+        // chunk's new K, V and Q rows, from the QKV projection, only after it.
         int cur_h = -1;
         for (int k = 0; first + k < last; ++k) {
             const int item = first + k, h = item / n, b = item - h * n, s = k & 1;
@@ -690,6 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
             uint8_t* st = sm + Lay::S0 + s * Lay::STAGE;
             const int n_copies = 4 * wv.npg + 6;
             for (int q = lane; q < n_copies; q += 32) {
+                if (k == 0 && q >= 4 * wv.npg) continue;   // the first item's new rows: after the wait below
                 if (q < 4 * wv.npg) {
                     const int bx = q >> 2, half = q & 1, isv = (q >> 1) & 1;
                     const int pg = wv.p_first + bx;
@@ -710,10 +713,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
                     tma_load_2d(dst, &mqkv, &full[s], xcol, wv.row_off);
                 }
             }
+            if (k == 0) {
+                pdl_wait();   // the QKV projection's outputs are read only from here on
+                for (int r = lane; r < 6; r += 32) {
+                    const int half = r & 1, which = r >> 1;   // which: 0 K, 1 V, 2 Q
+                    uint8_t* dst = which < 2 ? st + (2 * which + half) * Lay::HALF_KV + kNewRow * 128
+                                             : st + 4 * Lay::HALF_KV + half * kTM * 128;
+                    const int xcol = (which == 0 ? D : which == 1 ? 2 * D : 0) + h * DKk + half * 64;
+                    tma_load_2d(dst, &mqkv, &full[s], xcol, wv.row_off);
+                }
+            }
         }
         if (lane == 0) pdl_launch_dependents();
         return;
     }
+    pdl_wait();   // compute warps: the previous kernel's grid has completed (its outputs reach them by the copies)
+    if (tid == 0) timer_start(timer);
 
     // -------------------------------------------------------------------- compute warps
     float* AC = reinterpret_cast<float*>(sm + Lay::AC);
