@@ -542,8 +542,9 @@ struct Window {
 struct Lay {
     static constexpr uint32_t HALF_KV = kKVRows * 128;                 // one 64-column half of the staged K rows
     static constexpr uint32_t STAGE = 4 * HALF_KV + 2 * kTM * 128;     // K0 K1 V0 V1 Q0 Q1
-    static constexpr uint32_t P = 0;                                   // position rows, two 64-column halves
-    static constexpr uint32_t S0 = 2 * kPRows * 128;
+    static constexpr uint32_t PBUF = 2 * kPRows * 128;                 // one head's position rows: two column halves
+    static constexpr uint32_t P = 0;                                   // a CTA's (at most two) heads' position rows
+    static constexpr uint32_t S0 = 2 * PBUF;
     static constexpr uint32_t AC = S0 + 2 * STAGE;
     static constexpr uint32_t BD = AC + kTM * ACW * 4;
     static constexpr uint32_t PB = BD + kTM * BDW * 4;
@@ -623,8 +624,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
     uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + Lay::BAR);
     uint64_t* empty = full + 2;
-    uint64_t* pfull = full + 4;
-    int* abort_flag = reinterpret_cast<int*>(full + 5);
+    uint64_t* pfull = full + 4;   // per head of the CTA: its position rows have landed
+    int* abort_flag = reinterpret_cast<int*>(full + 6);
     volatile int* abort_v = abort_flag;
     const uint8_t* zero = sm + Lay::ZERO;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -636,7 +637,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], kComputeWarps);   // every compute warp releases the stage when done with it
         }
-        mbar_init(pfull, 1);
+        mbar_init(&pfull[0], 1);
+        mbar_init(&pfull[1], 1);
         *abort_flag = 0;
         fence_mbarrier_init();
         prefetch_tensormap(&mqkv);
@@ -655,29 +657,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
         // the previous kernel (the pages of this layer were written by this kernel in an earlier step, the
         // position table is a weight, the metadata is copied in before the step), so they overlap its tail; the
         // chunk's new K, V and Q rows, from the QKV projection, only after it.
-        int cur_h = -1;
+        // The position rows of the CTA's heads (at most two: a CTA holds at most n items), each in its own buffer.
+        if (lane == 0 && first < last) {
+            const int h0 = first / n, h1 = (last - 1) / n;
+            for (int hh = h0; hh <= h1 && hh <= h0 + 1; ++hh) {
+                uint8_t* pbuf = sm + Lay::P + (hh - h0) * Lay::PBUF;
+                mbar_arrive_expect_tx(&pfull[hh - h0], Lay::PBUF);
+                tma_load_2d(pbuf, &mp, &pfull[hh - h0], hh * DKk, ptab_row0);
+                tma_load_2d(pbuf + kPRows * 128, &mp, &pfull[hh - h0], hh * DKk + 64, ptab_row0);
+            }
+        }
         for (int k = 0; first + k < last; ++k) {
             const int item = first + k, h = item / n, b = item - h * n, s = k & 1;
             const Window wv = window_of(meta[b], L);
             int ok = 1;
-            if (lane == 0) {
-                if (h != cur_h) {
-                    // the staged position rows are rewritten once every item of the previous head is done
-                    if (cur_h >= 0 &&
-                        !mbar_wait_bounded(&empty[(k - 1) & 1], ((k - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v))
-                        ok = 0;
-                    if (ok) {
-                        mbar_arrive_expect_tx(pfull, 2 * kPRows * 128);
-                        tma_load_2d(sm + Lay::P, &mp, pfull, h * DKk, ptab_row0);
-                        tma_load_2d(sm + Lay::P + kPRows * 128, &mp, pfull, h * DKk + 64, ptab_row0);
-                    }
-                }
-                if (ok && k >= 2 && !mbar_wait_bounded(&empty[s], ((k - 2) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v))
-                    ok = 0;
-            }
+            if (lane == 0 && k >= 2 && !mbar_wait_bounded(&empty[s], ((k - 2) >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v))
+                ok = 0;
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
-            cur_h = h;
             int* kr = reinterpret_cast<int*>(sm + Lay::KROW) + s * kNKP;
             for (int j = lane; j < kNKP; j += 32) kr[j] = key_row(wv, L, j);
             // The window and the table are published to the compute warps by the stage's full barrier: lane 0's
@@ -736,19 +733,20 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
     bf16* Pb = reinterpret_cast<bf16*>(sm + Lay::PB);
     const int* krow_all = reinterpret_cast<const int*>(sm + Lay::KROW);
     float* bias = reinterpret_cast<float*>(sm + Lay::BIAS);   // [0, 128): pos_bias_u, [128, 256): pos_bias_v
-    const uint8_t* Ps = sm + Lay::P;
     const float scale = rsqrtf(static_cast<float>(DKk));
     const int g = lane >> 2, t4 = lane & 3;
     volatile int* go = abort_flag + 1;
-    int cur_h = -1, nph = 0;
+    const int h_first = first / n;
+    int cur_h = -1;
     for (int k = 0; first + k < last; ++k) {
         const int item = first + k, h = item / n, s = k & 1;
-        const int hoff = h * DKk;
+        const int hoff = h * DKk, pb = (h - h_first) & 1;
+        const uint8_t* Ps = sm + Lay::P + pb * Lay::PBUF;
         const bool new_head = h != cur_h;
         // One thread makes the bounded waits and the whole group follows its verdict, so that no warp leaves while
         // the others wait at a group barrier; then every thread observes the completed phases (at once).
         if (tid == 0) {
-            bool ok = !new_head || mbar_wait_bounded(pfull, nph & 1, err, DEV_TIMEOUT_ATTN, abort_v);
+            bool ok = !new_head || mbar_wait_bounded(&pfull[pb], 0, err, DEV_TIMEOUT_ATTN, abort_v);
             ok = ok && mbar_wait_bounded(&full[s], (k >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v);
             *go = ok ? 1 : 0;
         }
@@ -756,8 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tma_kernel(
         compute_sync();
         if (!*go) break;
         if (new_head) {
-            mbar_wait_bounded(pfull, nph & 1, err, DEV_TIMEOUT_ATTN, abort_v);
-            ++nph;
+            mbar_wait_bounded(&pfull[pb], 0, err, DEV_TIMEOUT_ATTN, abort_v);
             cur_h = h;
         }
         mbar_wait_bounded(&full[s], (k >> 1) & 1, err, DEV_TIMEOUT_ATTN, abort_v);
