@@ -149,6 +149,23 @@ def gemm_flops_per_step(n: int, T: int, R: int, cfg) -> float:
     return float(layers + sub + joint)
 
 
+def step_bytes_per_kind(n: int, T: int, cfg) -> dict:
+    """Algorithmic HBM bytes per step of the bandwidth-bound kernels (bf16 activations and caches, fp32 residual):
+    attention per (stream, head) the cached K and V window (L rows each), the chunk's Q, K and V rows, the output
+    and the K/V append; the conv module per stream T pointwise-conv rows in (2 D), T rows out, the 8-row ring read
+    and written; LayerNorm per row the fp32 row read and the bf16 row written (the fused pair also writes the fp32
+    row back), for the layer's norms (norm_ff1 once, then per layer norm_att, norm_conv, norm_ff2 and the fused
+    norm_out + next norm_ff1, the last layer's norm_out alone)."""
+    D, NL, L, H = cfg.d_model, cfg.n_layers, cfg.left_context, cfg.n_heads
+    dk = D // H
+    attn = NL * n * H * 2 * (2 * L * dk + 3 * T * dk + T * dk + 2 * T * dk)
+    conv = NL * n * 2 * (T * 2 * D + T * D + 2 * 8 * D)
+    rows = n * T
+    ln_plain = (1 + 3 * NL) * rows * (4 * D + 2 * D)
+    ln_pair = (NL - 1) * rows * (4 * D + 4 * D + 2 * D) + rows * (4 * D + 4 * D)
+    return {"attention": float(attn), "conv": float(conv), "norm": float(ln_plain + ln_pair)}
+
+
 def weight_bytes(cfg) -> float:
     """bf16 bytes of every GEMM operand a step reads: 24 layers x 24.12 M, the subsampling pointwise and output
     projections, and joint.enc."""
@@ -828,8 +845,13 @@ def main():
         if i >= 2:
             g_runs.append(eng.graph_timers_read())
     eng.graph_timers(False)
+    kernel_roof_graph = None
     if g_runs and g_runs[-1]["gemm_tc2"][1] > 0:
         kernel_graph = {k: round(sum(r[k][0] for r in g_runs) / len(g_runs), 4) for k in g_runs[-1] if g_runs[-1][k][1]}
+        kbytes = step_bytes_per_kind(n, T, cfg)
+        kernel_roof_graph = {k: {"bytes_per_step": kbytes[k], "gbs": kbytes[k] / (kernel_graph[k] / 1e3) / 1e9,
+                                 "frac": kbytes[k] / (kernel_graph[k] / 1e3) / 1e9 / hbm}
+                             for k in kbytes if kernel_graph.get(k)}
         g_ms = kernel_graph["gemm_tc2"]
         g_ach = flops / (g_ms / 1e3) / 1e12
         graph_mode = {"achieved": g_ach, "frac": g_ach / bf16_sus, "gemm_ms_per_step": g_ms,
@@ -956,6 +978,7 @@ def main():
                             "graph_mode": graph_mode},
                "kernel_ms_per_step": {k: round(v[0] / 2, 4) for k, v in prof.items() if v[1]},
                "kernel_ms_per_step_graph": kernel_graph,
+               "kernel_roofline_graph": kernel_roof_graph,
                "kernel_attribution_graph": ("the same kinds in the graph-replayed step, as in the timed region: per "
                                             "launch, last CTA end - first CTA past the grid-dependency wait "
                                             "(global-timer stamps), summed per kind, mean of 3 steps outside the "
