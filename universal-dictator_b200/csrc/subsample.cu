@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(256, 2) conv01_kernel(const float* __restrict_
 // flight at once (masked rows zero-filled); each thread owns one channel group (taps in registers, loaded before
 // the grid-dependency wait) and a run of output columns.
 template <typename T>
-__global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, int Tin, int Fin,
+__global__ void __launch_bounds__(256, 3) dwconv2_kernel(const T* __restrict__ in, int Tin, int Fin,
                                                       const BatchEntry* __restrict__ meta, const float* __restrict__ w,
                                                       const float* __restrict__ bias, T* __restrict__ out, int Tout,
                                                       int Fout, int C) {
@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, 
     constexpr int VW = Vec16<T>::N;
     extern __shared__ __align__(16) unsigned char smraw[];
     T* xs = reinterpret_cast<T*>(smraw);   // [3][Fin][C]
+    float* ws = reinterpret_cast<float*>(smraw + sizeof(T) * 3 * static_cast<size_t>(Fin) * C);   // [9][C] taps, [C] bias
     const int b = blockIdx.x, t = blockIdx.y;
     const int groups = C / VW;
     const int lanes_f = blockDim.x / groups;
@@ -202,20 +203,12 @@ __global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, 
     const int per = (Fout + lanes_f - 1) / lanes_f;
     const int fa = fl * per, fb = fl < lanes_f ? min(Fout, fa + per) : fa;
     const int c = g * VW;
-    // Taps and bias (weights, never written by the previous kernel) before the grid-dependency wait.
-    float wr[9][VW], br[VW];
-#pragma unroll
-    for (int e = 0; e < VW; e += 4) {
-        const float4 bb = *reinterpret_cast<const float4*>(bias + c + e);
-        br[e] = bb.x; br[e + 1] = bb.y; br[e + 2] = bb.z; br[e + 3] = bb.w;
-    }
-#pragma unroll
-    for (int k = 0; k < 9; ++k)
-#pragma unroll
-        for (int e = 0; e < VW; e += 4) {
-            const float4 ww = *reinterpret_cast<const float4*>(w + k * C + c + e);
-            wr[k][e] = ww.x; wr[k][e + 1] = ww.y; wr[k][e + 2] = ww.z; wr[k][e + 3] = ww.w;
-        }
+    // Taps and bias (weights, never written by the previous kernel) to shared memory before the grid-dependency
+    // wait; kept out of registers so that three CTAs fit on an SM.
+    for (int i = threadIdx.x * 4; i < 9 * C; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(ws + i) = *reinterpret_cast<const float4*>(w + i);
+    for (int i = threadIdx.x * 4; i < C; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(ws + 9 * C + i) = *reinterpret_cast<const float4*>(bias + i);
     pdl_wait();
     // The three input rows 2 t - 2 .. 2 t (zero where masked), every 16-byte chunk in flight at once.
     const int vin = nxt(nxt(meta[b].valid_mel));
@@ -233,7 +226,10 @@ __global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, 
     for (int f = fa; f < fb; ++f) {
         float acc[VW];
 #pragma unroll
-        for (int e = 0; e < VW; ++e) acc[e] = br[e];
+        for (int e = 0; e < VW; e += 4) {
+            const float4 bb = *reinterpret_cast<const float4*>(ws + 9 * C + c + e);
+            acc[e] = bb.x; acc[e + 1] = bb.y; acc[e + 2] = bb.z; acc[e + 3] = bb.w;
+        }
 #pragma unroll
         for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
@@ -243,7 +239,13 @@ __global__ void __launch_bounds__(256) dwconv2_kernel(const T* __restrict__ in, 
                 float x[VW];
                 load16<T>(xs + (kh * Fin + q) * C + c, x);
 #pragma unroll
-                for (int e = 0; e < VW; ++e) acc[e] = fmaf(wr[kh * 3 + kw][e], x[e], acc[e]);
+                for (int e = 0; e < VW; e += 4) {
+                    const float4 ww = *reinterpret_cast<const float4*>(ws + (kh * 3 + kw) * C + c + e);
+                    acc[e] = fmaf(ww.x, x[e], acc[e]);
+                    acc[e + 1] = fmaf(ww.y, x[e + 1], acc[e + 1]);
+                    acc[e + 2] = fmaf(ww.z, x[e + 2], acc[e + 2]);
+                    acc[e + 3] = fmaf(ww.w, x[e + 3], acc[e + 3]);
+                }
             }
         store16<T>(out + ((static_cast<size_t>(b) * Tout + t) * Fout + f) * C + c, acc);
     }
@@ -307,9 +309,9 @@ void sub_conv01(const float* mel, int rows_stride, int mel_bins, const BatchEntr
 template <typename T>
 void sub_dwconv2(const T* in, int Tin, int Fin, const BatchEntry* meta, int n, const float* w, const float* b, T* out,
                  int Tout, int Fout, int C, cudaStream_t s) {
-    const size_t smem = sizeof(T) * 3 * static_cast<size_t>(Fin) * C;
+    const size_t smem = sizeof(T) * 3 * static_cast<size_t>(Fin) * C + sizeof(float) * 10 * C;
     static size_t attr_set[kMaxDevices] = {};   // per instantiation (T) and device
-    if (smem > 48 * 1024) ensure_dyn_smem(dwconv2_kernel<T>, smem, attr_set);
+    ensure_dyn_smem(dwconv2_kernel<T>, smem, attr_set);
     launch_pdl(dwconv2_kernel<T>, dim3(n, Tout), dim3(256), smem, s, in, Tin, Fin, meta, w, b, out, Tout, Fout, C);
 }
 
